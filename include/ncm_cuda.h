@@ -1,0 +1,162 @@
+/*
+ * ncm_cuda.h — C ABI of the ncmorph_b200 CUDA library (libncm_cuda.so).
+ *
+ * This is the drop-in boundary between ncmorph's host code (the Zig
+ * `src/decoder.zig`, `src/ncm_body.zig`, `src/ncm_model.zig` callers and the
+ * planned `packages/vq`) and hand-written sm_100a kernels. Each entry point
+ * names the reference function it stands in for.
+ *
+ * Conventions
+ *  - Every function returns NCM_OK (0) or a negative ncm status; none aborts,
+ *    traps or prints. ncm_last_error() gives the message of the calling
+ *    thread's last failure.
+ *  - Pointers are DEVICE pointers unless the name ends in `_host_f32`, whose
+ *    buffers are host memory in the reference's "f32 slice carrying bf16
+ *    values" convention (src/loader.zig:338-341).
+ *  - bf16 tensors are passed as uint16_t bit patterns, row-major.
+ *  - Buffers are caller-owned. The context owns its device workspace.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream) and is asynchronous, except the `_host_f32` functions, which
+ *    return after the result is in host memory. ncm_sync() waits and also
+ *    reports device-side failures (a timed-out pipeline wait, a bad index).
+ *  - Shapes are validated on the host; a bad shape returns NCM_EINVAL where
+ *    the reference would `std.debug.assert`.
+ *  - A context may be used from one host thread at a time.
+ */
+#ifndef NCM_CUDA_H
+#define NCM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NCM_API __attribute__((visibility("default")))
+#else
+#define NCM_API
+#endif
+
+typedef struct ncm_ctx ncm_ctx_t;
+typedef void* ncm_stream_t; /* cudaStream_t */
+
+enum ncm_status {
+  NCM_OK = 0,
+  NCM_EINVAL = -1,   /* bad shape, null pointer or misaligned buffer */
+  NCM_ECUDA = -2,    /* CUDA runtime error */
+  NCM_ENOMEM = -3,   /* device workspace could not be allocated */
+  NCM_ETIMEOUT = -4, /* a device-side bounded wait gave up */
+  NCM_ERANGE = -5,   /* an index (token id, code) is out of range */
+  NCM_ENOTSUP = -6   /* the device is not an sm_100 part */
+};
+
+/* ------------------------------------------------------------ context */
+
+/* Creates a context on CUDA device `device` (must be compute capability 10.0).
+ * Replaces the reference's implicit single-threaded CPU state. */
+NCM_API int ncm_ctx_create(int device, ncm_ctx_t** out);
+NCM_API int ncm_ctx_destroy(ncm_ctx_t* ctx);
+/* Waits for `stream`, then checks the context's device error word. */
+NCM_API int ncm_sync(ncm_ctx_t* ctx, ncm_stream_t stream);
+NCM_API const char* ncm_status_string(int status);
+NCM_API const char* ncm_last_error(void);
+NCM_API int ncm_version(void);
+
+/* --------------------------------------------------------- L7: bf16 */
+
+/* y[i] = bf16(x[i]) with round-to-nearest-even and NaN -> 0x7FC0.
+ * Replaces bf16_t.from_f32 (packages/bf16/root.zig:17-22) applied elementwise. */
+NCM_API int ncm_f32_to_bf16(ncm_ctx_t* ctx, const float* x, uint16_t* y, int64_t n, ncm_stream_t stream);
+/* y[i] = f32(x[i]) exactly. Replaces bf16_t.to_f32 / widen_little_endian
+ * (packages/bf16/root.zig:25-37). */
+NCM_API int ncm_bf16_to_f32(ncm_ctx_t* ctx, const uint16_t* x, float* y, int64_t n, ncm_stream_t stream);
+
+/* ------------------------------------------------------ L1: bf16 linear */
+
+/* y[M,N] = bf16( x[M,K] . W[N,K]^T (+ bias[N]) ), bf16 operands, f32
+ * accumulation in tensor memory, one bf16 rounding at the output.
+ * Replaces matmul_bf16 / matmul_bf16_bias (packages/kernels/root.zig:96-104,
+ * matmul_bf16_impl :106-142). `bias` may be NULL. K must be a multiple of 8. */
+NCM_API int ncm_linear_bf16(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                    int64_t M, int64_t K, int64_t N, ncm_stream_t stream);
+
+/* Host-slice form of ncm_linear_bf16 with the reference's calling convention:
+ * f32 slices whose values are rounded to bf16 on entry (as matmul_bf16_impl
+ * does, root.zig:121-129) and an f32 output slice holding bf16 values.
+ * Drop-in for kernels.matmul_bf16(_bias) (packages/kernels/root.zig:96-104). */
+NCM_API int ncm_linear_bf16_host_f32(ncm_ctx_t* ctx, const float* x, const float* w, const float* bias, float* y,
+                             int64_t M, int64_t K, int64_t N);
+
+/* Host-slice stand-in for the f32 kernels.matmul (packages/kernels/root.zig:25-65)
+ * used by ncm_body/ncm_model. It runs on the same bf16 tensor-core path
+ * (operands rounded to bf16, f32 accumulation) and returns the f32
+ * accumulator without the final bf16 rounding. */
+NCM_API int ncm_matmul_host_f32(ncm_ctx_t* ctx, const float* x, const float* w, float* y, int64_t M, int64_t K,
+                        int64_t N);
+
+/* ------------------------------------------------- R1-R6: RVQ tokenizer */
+
+/* sqnorm[k] = sum_d e[k,d]^2, accumulated in f64 and rounded once to f32.
+ * The ||e_k||^2 term of the distance in research/reference/vq_forward_semantics.md:81. */
+NCM_API int ncm_code_sqnorm(ncm_ctx_t* ctx, const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D,
+                    ncm_stream_t stream);
+
+/* One residual-VQ level (vq_forward_semantics.md:68-72):
+ *   codes[n] = argmin_k ( sqnorm[k] - 2 * bf16(residual[n]) . e[k] )  (lowest k on ties)
+ *   residual[n] -= e[codes[n]]                                         (f32)
+ * The distance GEMM runs on tcgen05 with bf16 operands and f32 accumulation.
+ * residual [N,D] f32 in/out, codebook [K,D] bf16, sqnorm [K] f32 (NULL: computed),
+ * codes [N] int32 out. D must be a multiple of 8. */
+NCM_API int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, const float* sqnorm,
+                  int32_t* codes, int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
+/* L residual levels over x (vq_forward_semantics.md:59-82 at a single scale):
+ * residual = f32(x); for l: ncm_rvq_level(codebooks[l]).
+ * x [N,D] bf16; codebooks [L,K,D] bf16; sqnorms [L,K] f32 or NULL (computed);
+ * codes [L,N] int32 out; recon [N,D] bf16 out or NULL (= decode of the codes);
+ * residual_out [N,D] f32 out or NULL (the residual after the last level). */
+NCM_API int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks, const float* sqnorms, int32_t L,
+                   int32_t* codes, uint16_t* recon, float* residual_out, int64_t N, int64_t D, int64_t K,
+                   ncm_stream_t stream);
+
+/* Area pooling by an integer factor (F.interpolate mode="area" with T % factor == 0,
+ * vq_forward_semantics.md:67,80): y[b,j,:] = (sum_{i<factor} x[b,j*factor+i,:]) / factor,
+ * summed in increasing i in f32. x [B,T,D] f32, y [B,T/factor,D] f32. */
+NCM_API int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, int64_t T, int64_t D, int32_t factor,
+                 ncm_stream_t stream);
+
+/* Decode (vq_forward_semantics.md:69,82): recon[n,:] = bf16( sum_l e_l[codes[l,n],:] ),
+ * summed over l in increasing order in f32. codes [L,N]; codebooks [L,K,D]. A code
+ * outside [0,K) makes the call fail with NCM_ERANGE (reported by ncm_sync). */
+NCM_API int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codebooks, int32_t L, uint16_t* recon,
+                   int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
+/* Multiscale tokenizer forward (research/ncm_facts.md:81; scales coarse -> fine):
+ *   h = linear_bf16(x, w_in, b_in); r = f32(h); recon = 0
+ *   for s: u = pool(r, f_s); L levels of ncm_rvq_level on u; q = sum_l e_{s,l}[code]
+ *          r -= up(q, f_s); recon += up(q, f_s)       (nearest-repeat upsampling)
+ *   y = linear_bf16(bf16(recon), w_out, b_out)
+ * Codes are written scale-major: scale s occupies L * B*T/f_s entries, level-major. */
+typedef struct ncm_tokenizer_config {
+  int64_t batch;            /* B */
+  int64_t seq_len;          /* T */
+  int64_t model_width;      /* width of x and y */
+  int64_t vq_width;         /* D, the quantised width */
+  int64_t codebook_size;    /* K */
+  int32_t num_scales;       /* S (<= 16) */
+  int32_t levels_per_scale; /* L */
+  int32_t pool_factors[16]; /* f_s, coarse to fine; each divides seq_len */
+} ncm_tokenizer_config_t;
+
+NCM_API int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x, const uint16_t* w_in,
+                          const uint16_t* b_in, const uint16_t* codebooks, const float* sqnorms,
+                          const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
+                          uint16_t* y, ncm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NCM_CUDA_H */

@@ -1,0 +1,99 @@
+"""ctypes binding of libncm_cuda.so (the C ABI declared in include/ncm_cuda.h).
+
+The library is loaded from this package directory only. There is no fallback:
+if the shared object is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libncm_cuda.so"
+
+NCM_OK = 0
+NCM_EINVAL = -1
+NCM_ECUDA = -2
+NCM_ENOMEM = -3
+NCM_ETIMEOUT = -4
+NCM_ERANGE = -5
+NCM_ENOTSUP = -6
+
+c_i32 = ctypes.c_int32
+c_i64 = ctypes.c_int64
+c_vp = ctypes.c_void_p
+
+
+class TokenizerConfig(ctypes.Structure):
+    """Mirror of ncm_tokenizer_config_t."""
+
+    _fields_ = [
+        ("batch", c_i64),
+        ("seq_len", c_i64),
+        ("model_width", c_i64),
+        ("vq_width", c_i64),
+        ("codebook_size", c_i64),
+        ("num_scales", c_i32),
+        ("levels_per_scale", c_i32),
+        ("pool_factors", c_i32 * 16),
+    ]
+
+
+# name -> argtypes (all functions return int status unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "ncm_ctx_create": [ctypes.c_int, ctypes.POINTER(c_vp)],
+    "ncm_ctx_destroy": [c_vp],
+    "ncm_sync": [c_vp, c_vp],
+    "ncm_status_string": [ctypes.c_int],
+    "ncm_last_error": [],
+    "ncm_version": [],
+    "ncm_f32_to_bf16": [c_vp, c_vp, c_vp, c_i64, c_vp],
+    "ncm_bf16_to_f32": [c_vp, c_vp, c_vp, c_i64, c_vp],
+    "ncm_linear_bf16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_linear_bf16_host_f32": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64],
+    "ncm_matmul_host_f32": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64],
+    "ncm_code_sqnorm": [c_vp, c_vp, c_vp, c_i64, c_i64, c_vp],
+    "ncm_rvq_level": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_rvq_encode": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_pool_avg": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp],
+    "ncm_rvq_decode": [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_tokenizer_forward": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, c_vp, c_vp],
+}
+_RESTYPES = {"ncm_status_string": ctypes.c_char_p, "ncm_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+class NcmError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"ncm status {status}: {message}")
+        self.status = status
+
+
+def load() -> ctypes.CDLL:
+    """Loads libncm_cuda.so from the package directory (raises if absent)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m ncmorph_b200.build` (there is no CPU fallback)")
+    lib = ctypes.CDLL(os.fspath(LIB_PATH), mode=ctypes.RTLD_LOCAL)
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != NCM_OK:
+        msg = load().ncm_last_error()
+        raise NcmError(status, msg.decode(errors="replace") if msg else "")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

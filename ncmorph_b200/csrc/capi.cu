@@ -1,0 +1,475 @@
+// C-ABI entry points of libncm_cuda.so (declared in include/ncm_cuda.h):
+// argument validation, context/workspace management and the composition of
+// the kernels in rvq.cu and gemm.cu into the reference-shaped operations.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int check_ctx(ncm_ctx* ctx) {
+  if (ctx == nullptr) return ncm_fail(NCM_EINVAL, "null context");
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != ctx->device) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  }
+  return NCM_OK;
+}
+
+}  // namespace
+
+int ncm_set_cuda_error(cudaError_t e) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "CUDA error %d: %s", static_cast<int>(e), cudaGetErrorString(e));
+  return NCM_ECUDA;
+}
+
+int ncm_fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+namespace ncm {
+
+void* ctx_workspace(ncm_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->ws_bytes) return ctx->ws;
+  if (ctx->ws != nullptr) {
+    cudaDeviceSynchronize();
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+  }
+  const size_t want = bytes + bytes / 4;
+  if (cudaMalloc(&ctx->ws, want) != cudaSuccess) {
+    cudaGetLastError();
+    ctx->ws = nullptr;
+    return nullptr;
+  }
+  ctx->ws_bytes = want;
+  return ctx->ws;
+}
+
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  auto fn = tmap_encode_fn();
+  if (fn == nullptr || rows == 0 || cols == 0 || (cols * 2) % 16 != 0 || !aligned16(base)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64u, box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// One RVQ level on a bf16 view `a_bf16` of the residual. `resid` is updated
+// in place (or initialised from src_bf16 when given); `shadow` receives
+// bf16(resid) for the next level when non-null.
+static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* src_bf16, float* resid,
+                          uint16_t* shadow, const uint16_t* codebook, const float* sqnorm, int32_t* codes,
+                          RvqPartial* part, const RvqPlan& plan, int64_t N, int64_t D, int64_t K, bool update,
+                          cudaStream_t stream) {
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, D, 256))
+    return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
+                    (long long)D, (long long)K);
+  NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream));
+  NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, src_bf16, resid, shadow, codebook, ctx->d_err, N, D, K, update,
+                                stream));
+  return NCM_OK;
+}
+
+}  // namespace ncm
+
+using namespace ncm;
+
+extern "C" {
+
+int ncm_version(void) { return 100; }
+
+const char* ncm_status_string(int s) {
+  switch (s) {
+    case NCM_OK: return "ok";
+    case NCM_EINVAL: return "invalid argument";
+    case NCM_ECUDA: return "CUDA error";
+    case NCM_ENOMEM: return "out of device memory";
+    case NCM_ETIMEOUT: return "device wait timed out";
+    case NCM_ERANGE: return "index out of range";
+    case NCM_ENOTSUP: return "unsupported device";
+    default: return "unknown status";
+  }
+}
+
+const char* ncm_last_error(void) { return g_last_error; }
+
+int ncm_ctx_create(int device, ncm_ctx_t** out) {
+  if (out == nullptr) return ncm_fail(NCM_EINVAL, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  if (device < 0 || device >= n) return ncm_fail(NCM_EINVAL, "device %d out of range (%d devices)", device, n);
+  cudaDeviceProp prop;
+  NCM_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10 || prop.minor != 0)
+    return ncm_fail(NCM_ENOTSUP, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major,
+                    prop.minor);
+  NCM_CUDA_TRY(cudaSetDevice(device));
+  ncm_ctx* ctx = new ncm_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  e = cudaMalloc(&ctx->d_err, 256);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return ncm_set_cuda_error(e);
+  }
+  cudaMemset(ctx->d_err, 0, 256);
+  cudaDeviceSynchronize();
+  *out = ctx;
+  return NCM_OK;
+}
+
+int ncm_ctx_destroy(ncm_ctx_t* ctx) {
+  if (ctx == nullptr) return NCM_OK;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
+  delete ctx;
+  return NCM_OK;
+}
+
+int ncm_sync(ncm_ctx_t* ctx, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  NCM_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int err = 0;
+  NCM_CUDA_TRY(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    cudaDeviceSynchronize();
+    if (err & kErrWaitTimeout) return ncm_fail(NCM_ETIMEOUT, "a device-side pipeline wait timed out (flags %d)", err);
+    return ncm_fail(NCM_ERANGE, "a kernel met an out-of-range index (flags %d)", err);
+  }
+  return NCM_OK;
+}
+
+int ncm_f32_to_bf16(ncm_ctx_t* ctx, const float* x, uint16_t* y, int64_t n, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr))) return ncm_fail(NCM_EINVAL, "f32_to_bf16: bad arguments");
+  if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "f32_to_bf16: buffers must be 16-byte aligned");
+  NCM_CUDA_TRY(launch_f32_to_bf16(x, y, n, static_cast<cudaStream_t>(stream)));
+  return NCM_OK;
+}
+
+int ncm_bf16_to_f32(ncm_ctx_t* ctx, const uint16_t* x, float* y, int64_t n, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr))) return ncm_fail(NCM_EINVAL, "bf16_to_f32: bad arguments");
+  if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "bf16_to_f32: buffers must be 16-byte aligned");
+  NCM_CUDA_TRY(launch_bf16_to_f32(x, y, n, static_cast<cudaStream_t>(stream)));
+  return NCM_OK;
+}
+
+int ncm_linear_bf16(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                    int64_t M, int64_t K, int64_t N, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (M <= 0 || K <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return ncm_fail(NCM_EINVAL, "linear: bad shape M=%lld K=%lld N=%lld", (long long)M, (long long)K, (long long)N);
+  if (K % 8 != 0) return ncm_fail(NCM_EINVAL, "linear: K=%lld must be a multiple of 8", (long long)K);
+  if (!x || !w || !y) return ncm_fail(NCM_EINVAL, "linear: null buffer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)))
+    return ncm_fail(NCM_EINVAL, "linear: buffers must be 16-byte aligned");
+  return linear_bf16(ctx, x, w, bias, y, nullptr, M, K, N, static_cast<cudaStream_t>(stream));
+}
+
+// Shared body of the host-slice linears: round f32 operands to bf16 on the
+// device, run the tensor-core GEMM, copy the result back.
+static int linear_host_common(ncm_ctx* ctx, const float* x, const float* w, const float* bias, float* y, int64_t M,
+                              int64_t K, int64_t N, bool round_output) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (M <= 0 || K <= 0 || N <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return ncm_fail(NCM_EINVAL, "linear: bad shape M=%lld K=%lld N=%lld", (long long)M, (long long)K, (long long)N);
+  if (!x || !w || !y) return ncm_fail(NCM_EINVAL, "linear: null buffer");
+  // Pad K to a multiple of 8 with zeros (TMA rows must be 16-byte strided).
+  const int64_t Kp = (K + 7) / 8 * 8;
+  WsCarver cv;
+  const size_t o_xf = cv.take(sizeof(float) * M * Kp);
+  const size_t o_wf = cv.take(sizeof(float) * N * Kp);
+  const size_t o_xb = cv.take(2 * M * Kp);
+  const size_t o_wb = cv.take(2 * N * Kp);
+  const size_t o_bf = cv.take(sizeof(float) * N);
+  const size_t o_bb = cv.take(2 * N);
+  const size_t o_y = cv.take(sizeof(float) * M * N);
+  const size_t o_yb = cv.take(2 * M * N);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "linear: workspace allocation failed");
+  float* xf = reinterpret_cast<float*>(ws + o_xf);
+  float* wf = reinterpret_cast<float*>(ws + o_wf);
+  uint16_t* xb = reinterpret_cast<uint16_t*>(ws + o_xb);
+  uint16_t* wb = reinterpret_cast<uint16_t*>(ws + o_wb);
+  float* bf = reinterpret_cast<float*>(ws + o_bf);
+  uint16_t* bb = reinterpret_cast<uint16_t*>(ws + o_bb);
+  float* yf = reinterpret_cast<float*>(ws + o_y);
+  uint16_t* yb = reinterpret_cast<uint16_t*>(ws + o_yb);
+  cudaStream_t st = 0;
+  if (Kp == K) {
+    NCM_CUDA_TRY(cudaMemcpyAsync(xf, x, sizeof(float) * M * K, cudaMemcpyHostToDevice, st));
+    NCM_CUDA_TRY(cudaMemcpyAsync(wf, w, sizeof(float) * N * K, cudaMemcpyHostToDevice, st));
+  } else {
+    NCM_CUDA_TRY(cudaMemsetAsync(xf, 0, sizeof(float) * M * Kp, st));
+    NCM_CUDA_TRY(cudaMemsetAsync(wf, 0, sizeof(float) * N * Kp, st));
+    NCM_CUDA_TRY(cudaMemcpy2DAsync(xf, sizeof(float) * Kp, x, sizeof(float) * K, sizeof(float) * K, M,
+                                   cudaMemcpyHostToDevice, st));
+    NCM_CUDA_TRY(cudaMemcpy2DAsync(wf, sizeof(float) * Kp, w, sizeof(float) * K, sizeof(float) * K, N,
+                                   cudaMemcpyHostToDevice, st));
+  }
+  NCM_CUDA_TRY(launch_f32_to_bf16(xf, xb, M * Kp, st));
+  NCM_CUDA_TRY(launch_f32_to_bf16(wf, wb, N * Kp, st));
+  const uint16_t* bias_dev = nullptr;
+  if (bias != nullptr) {
+    NCM_CUDA_TRY(cudaMemcpyAsync(bf, bias, sizeof(float) * N, cudaMemcpyHostToDevice, st));
+    NCM_CUDA_TRY(launch_f32_to_bf16(bf, bb, N, st));
+    bias_dev = bb;
+  }
+  if (round_output) {
+    rc = linear_bf16(ctx, xb, wb, bias_dev, yb, nullptr, M, Kp, N, st);
+    if (rc) return rc;
+    NCM_CUDA_TRY(launch_bf16_to_f32(yb, yf, M * N, st));
+  } else {
+    rc = linear_bf16(ctx, xb, wb, bias_dev, nullptr, yf, M, Kp, N, st);
+    if (rc) return rc;
+  }
+  NCM_CUDA_TRY(cudaMemcpyAsync(y, yf, sizeof(float) * M * N, cudaMemcpyDeviceToHost, st));
+  return ncm_sync(ctx, st);
+}
+
+int ncm_linear_bf16_host_f32(ncm_ctx_t* ctx, const float* x, const float* w, const float* bias, float* y, int64_t M,
+                             int64_t K, int64_t N) {
+  return linear_host_common(ctx, x, w, bias, y, M, K, N, true);
+}
+
+int ncm_matmul_host_f32(ncm_ctx_t* ctx, const float* x, const float* w, float* y, int64_t M, int64_t K, int64_t N) {
+  return linear_host_common(ctx, x, w, nullptr, y, M, K, N, false);
+}
+
+int ncm_code_sqnorm(ncm_ctx_t* ctx, const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D,
+                    ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (K <= 0 || D <= 0 || D % 8 != 0 || !codebook || !sqnorm)
+    return ncm_fail(NCM_EINVAL, "code_sqnorm: bad arguments (K=%lld D=%lld)", (long long)K, (long long)D);
+  if (!aligned16(codebook)) return ncm_fail(NCM_EINVAL, "code_sqnorm: codebook must be 16-byte aligned");
+  NCM_CUDA_TRY(launch_code_sqnorm(codebook, sqnorm, K, D, static_cast<cudaStream_t>(stream)));
+  return NCM_OK;
+}
+
+static int check_rvq_shape(int64_t N, int64_t D, int64_t K) {
+  if (N <= 0 || D <= 0 || K <= 0 || N > INT32_MAX || K > INT32_MAX || D > 65536)
+    return ncm_fail(NCM_EINVAL, "rvq: bad shape N=%lld D=%lld K=%lld", (long long)N, (long long)D, (long long)K);
+  if (D % 8 != 0) return ncm_fail(NCM_EINVAL, "rvq: D=%lld must be a multiple of 8", (long long)D);
+  return NCM_OK;
+}
+
+int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, const float* sqnorm, int32_t* codes,
+                  int64_t N, int64_t D, int64_t K, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_rvq_shape(N, D, K))) return rc;
+  if (!residual || !codebook || !codes) return ncm_fail(NCM_EINVAL, "rvq_level: null buffer");
+  if (!aligned16(residual) || !aligned16(codebook) || !aligned16(codes) || (sqnorm && !aligned16(sqnorm)))
+    return ncm_fail(NCM_EINVAL, "rvq_level: buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K);
+  WsCarver cv;
+  const size_t o_sh = cv.take(2 * N * D);
+  const size_t o_part = cv.take(plan.partial_bytes);
+  const size_t o_sq = cv.take(sizeof(float) * K);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_level: workspace allocation failed");
+  uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
+  if (sqnorm == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    NCM_CUDA_TRY(launch_code_sqnorm(codebook, sq, K, D, st));
+    sqnorm = sq;
+  }
+  NCM_CUDA_TRY(launch_f32_to_bf16(residual, shadow, N * D, st));
+  return rvq_level_core(ctx, shadow, nullptr, residual, nullptr, codebook, sqnorm, codes,
+                        reinterpret_cast<RvqPartial*>(ws + o_part), plan, N, D, K, true, st);
+}
+
+int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks, const float* sqnorms, int32_t L,
+                   int32_t* codes, uint16_t* recon, float* residual_out, int64_t N, int64_t D, int64_t K,
+                   ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_rvq_shape(N, D, K))) return rc;
+  if (L <= 0 || L > 64) return ncm_fail(NCM_EINVAL, "rvq_encode: L=%d must be in [1,64]", L);
+  if (!x || !codebooks || !codes) return ncm_fail(NCM_EINVAL, "rvq_encode: null buffer");
+  if (!aligned16(x) || !aligned16(codebooks) || !aligned16(codes) || (sqnorms && !aligned16(sqnorms)) ||
+      (recon && !aligned16(recon)) || (residual_out && !aligned16(residual_out)))
+    return ncm_fail(NCM_EINVAL, "rvq_encode: buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K);
+  WsCarver cv;
+  const size_t o_sh = cv.take(2 * N * D);
+  const size_t o_res = residual_out ? 0 : cv.take(sizeof(float) * N * D);
+  const size_t o_part = cv.take(plan.partial_bytes);
+  const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * K * L);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_encode: workspace allocation failed");
+  uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
+  float* resid = residual_out ? residual_out : reinterpret_cast<float*>(ws + o_res);
+  RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
+  if (sqnorms == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, K * L, D, st));
+    sqnorms = sq;
+  }
+  for (int l = 0; l < L; ++l) {
+    const bool last = (l == L - 1);
+    const bool update = !last || residual_out != nullptr;
+    const uint16_t* a = (l == 0) ? x : shadow;
+    rc = rvq_level_core(ctx, a, l == 0 ? x : nullptr, resid, last ? nullptr : shadow,
+                        codebooks + static_cast<size_t>(l) * K * D, sqnorms + static_cast<size_t>(l) * K,
+                        codes + static_cast<size_t>(l) * N, part, plan, N, D, K, update, st);
+    if (rc) return rc;
+  }
+  if (recon != nullptr) NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+  return NCM_OK;
+}
+
+int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, int64_t T, int64_t D, int32_t factor,
+                 ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (B <= 0 || T <= 0 || D <= 0 || factor <= 0 || T % factor != 0 || D % 4 != 0 || !x || !y)
+    return ncm_fail(NCM_EINVAL, "pool_avg: bad arguments (B=%lld T=%lld D=%lld factor=%d)", (long long)B,
+                    (long long)T, (long long)D, factor);
+  if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "pool_avg: buffers must be 16-byte aligned");
+  NCM_CUDA_TRY(launch_pool_avg(x, y, nullptr, B, T, D, factor, static_cast<cudaStream_t>(stream)));
+  return NCM_OK;
+}
+
+int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codebooks, int32_t L, uint16_t* recon,
+                   int64_t N, int64_t D, int64_t K, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_rvq_shape(N, D, K))) return rc;
+  if (L <= 0 || !codes || !codebooks || !recon) return ncm_fail(NCM_EINVAL, "rvq_decode: bad arguments");
+  if (!aligned16(codes) || !aligned16(codebooks) || !aligned16(recon))
+    return ncm_fail(NCM_EINVAL, "rvq_decode: buffers must be 16-byte aligned");
+  NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err,
+                                 static_cast<cudaStream_t>(stream)));
+  return NCM_OK;
+}
+
+int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x, const uint16_t* w_in,
+                          const uint16_t* b_in, const uint16_t* codebooks, const float* sqnorms,
+                          const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon, uint16_t* y,
+                          ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (cfg == nullptr) return ncm_fail(NCM_EINVAL, "tokenizer: null config");
+  const int64_t B = cfg->batch, T = cfg->seq_len, Din = cfg->model_width, D = cfg->vq_width, K = cfg->codebook_size;
+  const int S = cfg->num_scales, L = cfg->levels_per_scale;
+  if (B <= 0 || T <= 0 || Din <= 0 || Din % 8 != 0 || S <= 0 || S > 16 || L <= 0 || L > 64)
+    return ncm_fail(NCM_EINVAL, "tokenizer: bad config");
+  if ((rc = check_rvq_shape(B * T, D, K))) return rc;
+  for (int s = 0; s < S; ++s)
+    if (cfg->pool_factors[s] <= 0 || T % cfg->pool_factors[s] != 0)
+      return ncm_fail(NCM_EINVAL, "tokenizer: pool factor %d does not divide T=%lld", cfg->pool_factors[s],
+                      (long long)T);
+  if (!x || !w_in || !codebooks || !w_out || !codes || !y)
+    return ncm_fail(NCM_EINVAL, "tokenizer: null buffer");
+  if (!aligned16(x) || !aligned16(w_in) || !aligned16(codebooks) || !aligned16(w_out) || !aligned16(codes) ||
+      !aligned16(y) || (recon && !aligned16(recon)) || (sqnorms && !aligned16(sqnorms)) ||
+      (b_in && !aligned16(b_in)) || (b_out && !aligned16(b_out)))
+    return ncm_fail(NCM_EINVAL, "tokenizer: buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t N = B * T;
+  int64_t max_rows = 0;
+  for (int s = 0; s < S; ++s) max_rows = std::max<int64_t>(max_rows, N / cfg->pool_factors[s]);
+  size_t part_bytes = 0;
+  for (int s = 0; s < S; ++s)
+    part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, N / cfg->pool_factors[s], K).partial_bytes);
+  WsCarver cv;
+  const size_t o_h = cv.take(2 * N * D);
+  const size_t o_r = cv.take(sizeof(float) * N * D);
+  const size_t o_acc = cv.take(sizeof(float) * N * D);
+  const size_t o_u = cv.take(sizeof(float) * max_rows * D);
+  const size_t o_ub = cv.take(2 * max_rows * D);
+  const size_t o_rb = recon ? 0 : cv.take(2 * N * D);
+  const size_t o_part = cv.take(part_bytes);
+  const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * S * L * K);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "tokenizer: workspace allocation failed");
+  uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
+  float* r = reinterpret_cast<float*>(ws + o_r);
+  float* acc = reinterpret_cast<float*>(ws + o_acc);
+  float* u = reinterpret_cast<float*>(ws + o_u);
+  uint16_t* ub = reinterpret_cast<uint16_t*>(ws + o_ub);
+  uint16_t* rb = recon ? recon : reinterpret_cast<uint16_t*>(ws + o_rb);
+  RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
+  if (sqnorms == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, static_cast<int64_t>(S) * L * K, D, st));
+    sqnorms = sq;
+  }
+  // input projection, then the f32 residual
+  rc = linear_bf16(ctx, x, w_in, b_in, h, nullptr, N, Din, D, st);
+  if (rc) return rc;
+  NCM_CUDA_TRY(launch_bf16_to_f32(h, r, N * D, st));
+  NCM_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(float) * N * D, st));
+  int32_t* codes_s = codes;
+  for (int s = 0; s < S; ++s) {
+    const int f = cfg->pool_factors[s];
+    const int64_t rows = N / f;
+    const RvqPlan plan = rvq_plan(ctx->num_sms, rows, K);
+    NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, f, st));
+    for (int l = 0; l < L; ++l) {
+      const size_t cb_off = (static_cast<size_t>(s) * L + l) * K;
+      rc = rvq_level_core(ctx, ub, nullptr, u, l == L - 1 ? nullptr : ub, codebooks + cb_off * D, sqnorms + cb_off,
+                          codes_s + static_cast<size_t>(l) * rows, part, plan, rows, D, K, l != L - 1, st);
+      if (rc) return rc;
+    }
+    NCM_CUDA_TRY(launch_scale_update(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, acc, B, T, D, K,
+                                     f, ctx->d_err, st));
+    codes_s += static_cast<size_t>(L) * rows;
+  }
+  NCM_CUDA_TRY(launch_f32_to_bf16(acc, rb, N * D, st));
+  return linear_bf16(ctx, rb, w_out, b_out, y, nullptr, N, D, Din, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,361 @@
+// bf16 linear layer y = x . W^T (+ bias) on tcgen05 tensor cores (L1).
+//
+// Same pipeline skeleton as the RVQ distance kernel: persistent CTAs (one per
+// SM), warp 0 issues TMA loads of 128-byte-swizzled K-major tiles into a
+// multi-stage mbarrier ring, warp 1 issues tcgen05.mma (bf16 x bf16 -> f32 in
+// tensor memory), warps 2-5 drain the double-buffered TMEM accumulator, add
+// the bias in f32, round once to bf16 and store.
+//
+// Skinny problems (M <= 64 tokens: decode-time GEMV shapes) run "swapped":
+// the 128-row MMA operand is the weight and the token rows form the narrow N
+// side of the instruction (16/32/64), so the kernel streams W once at HBM
+// speed instead of padding the tokens to 128 rows.
+#include <algorithm>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace ncm {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+  static constexpr uint32_t TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+};
+
+template <int BN>
+struct __align__(1024) GemmSmem {
+  uint8_t a[GemmCfg<BN>::STAGES][A_BYTES];
+  uint8_t b[GemmCfg<BN>::STAGES][GemmCfg<BN>::B_BYTES];
+  uint64_t full[GemmCfg<BN>::STAGES];
+  uint64_t empty[GemmCfg<BN>::STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct LinearArgs {
+  const uint16_t* bias;  // [N] or null
+  uint16_t* y;           // [M,N] bf16 (or null)
+  float* y_f32;          // [M,N] f32 (or null)
+  int* err;
+  int M, N, K;
+  int tiles_a, tiles_b;  // tiles along the 128-row operand and the BN operand
+  int a_fast;            // raster: 1 = consecutive tiles walk the A-operand tiles
+  int vec_ok;            // y rows are 16-byte aligned (N % 8 == 0)
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& ta, int& tb) {
+  if (a.a_fast) {
+    tb = tile / a.tiles_a;
+    ta = tile - tb * a.tiles_a;
+  } else {
+    ta = tile / a.tiles_b;
+    tb = tile - ta * a.tiles_b;
+  }
+}
+
+template <int BN, bool SWAP>
+__global__ void __launch_bounds__(THREADS, 1)
+    linear_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const LinearArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  GemmSmem<BN>& S = *reinterpret_cast<GemmSmem<BN>*>(smem_raw + pad);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = (args.K + BK - 1) / BK;
+  const int n_tiles = args.tiles_a * args.tiles_b;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.tfull[b], 1);
+      mbar_init(&S.tempty[b], 4);
+    }
+    mbar_init(&S.drain, 1);
+    S.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&S.tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  volatile int* abort_flag = &S.abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued[STAGES];
+      uint32_t issued_parity[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        int ta, tb;
+        tile_coords(tile, args, ta, tb);
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, ta * BM);
+          tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * BN);
+          issued[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(args.err, kErrWaitTimeout);
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const uint32_t b = acc_it & 1u;
+        const uint32_t ap = (acc_it >> 1) & 1u;
+        if (!mbar_wait(&S.tempty[b], ap ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dt = tmem + b * BN;
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&S.full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(S.a[stage]);
+          const uint32_t b0 = smem_u32(S.b[stage]);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                       (kc | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&S.tfull[b]);
+        ++acc_it;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(args.err, kErrWaitTimeout);
+        tc_commit(&S.drain);
+        mbar_wait(&S.drain, 0, nullptr);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    uint32_t acc_it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      int ta, tb;
+      tile_coords(tile, args, ta, tb);
+      const uint32_t b = acc_it & 1u;
+      const uint32_t ap = (acc_it >> 1) & 1u;
+      if (!mbar_wait(&S.tfull[b], ap, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+      const int arow = ta * BM + q * 32 + lane;  // row of the 128-row operand this thread owns
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld_x16(tbase + c, v);
+        tmem_wait_ld();
+        if (!SWAP) {
+          // arow = token m, columns = outputs n
+          const int m = arow;
+          const int n0 = tb * BN + c;
+          if (m < args.M) {
+            float f[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = n0 + j;
+              float acc = __uint_as_float(v[j]);
+              if (args.bias != nullptr && n < args.N) acc += bf16_to_f32(__ldg(args.bias + n));
+              f[j] = acc;
+            }
+            const size_t o = static_cast<size_t>(m) * args.N + n0;
+            if (args.y_f32 != nullptr) {
+              for (int j = 0; j < 16; ++j)
+                if (n0 + j < args.N) args.y_f32[o + j] = f[j];
+            } else if (args.vec_ok && n0 + 16 <= args.N) {
+              uint4 w0, w1;
+              w0.x = pack_bf16x2(f[0], f[1]);
+              w0.y = pack_bf16x2(f[2], f[3]);
+              w0.z = pack_bf16x2(f[4], f[5]);
+              w0.w = pack_bf16x2(f[6], f[7]);
+              w1.x = pack_bf16x2(f[8], f[9]);
+              w1.y = pack_bf16x2(f[10], f[11]);
+              w1.z = pack_bf16x2(f[12], f[13]);
+              w1.w = pack_bf16x2(f[14], f[15]);
+              *reinterpret_cast<uint4*>(args.y + o) = w0;
+              *reinterpret_cast<uint4*>(args.y + o + 8) = w1;
+            } else {
+              for (int j = 0; j < 16; ++j)
+                if (n0 + j < args.N) args.y[o + j] = f32_to_bf16(f[j]);
+            }
+          }
+        } else {
+          // arow = output n, columns = tokens m
+          const int n = arow;
+          if (n < args.N) {
+            const float bv = args.bias != nullptr ? bf16_to_f32(__ldg(args.bias + n)) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = tb * BN + c + j;
+              if (m < args.M) {
+                const float acc = __uint_as_float(v[j]) + bv;
+                const size_t o = static_cast<size_t>(m) * args.N + n;
+                if (args.y_f32 != nullptr)
+                  args.y_f32[o] = acc;
+                else
+                  args.y[o] = f32_to_bf16(acc);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.tempty[b]);
+      ++acc_it;
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      atomicOr(args.err, kErrWaitTimeout);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN, bool SWAP>
+cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const LinearArgs& a, int grid,
+                          cudaStream_t stream) {
+  constexpr size_t smem = sizeof(GemmSmem<BN>) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  linear_bf16_kernel<BN, SWAP><<<grid, THREADS, smem, stream>>>(tmA, tmB, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, float* y_f32,
+                int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
+  LinearArgs a{};
+  a.bias = bias;
+  a.y = y;
+  a.y_f32 = y_f32;
+  a.err = ctx->d_err;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.vec_ok = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+  const bool swap = M <= 64;
+  CUtensorMap tmA, tmB;
+  int bn;
+  if (swap) {
+    bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    if (!make_tmap_bf16_2d(&tmA, w, N, K, BM) || !make_tmap_bf16_2d(&tmB, x, M, K, bn))
+      return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
+                      (long long)K, (long long)N);
+    a.tiles_a = ceil_div(N, BM);
+    a.tiles_b = ceil_div(M, bn);
+    a.a_fast = 1;
+  } else {
+    const long long mt = ceil_div(M, BM);
+    const int sms = ctx->num_sms;
+    if (mt * ceil_div(N, 256) >= sms)
+      bn = 256;
+    else if (mt * ceil_div(N, 128) >= sms)
+      bn = 128;
+    else
+      bn = 64;
+    if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, bn))
+      return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
+                      (long long)K, (long long)N);
+    a.tiles_a = static_cast<int>(mt);
+    a.tiles_b = ceil_div(N, bn);
+    // Keep the smaller operand L2-resident: walk the tiles of the larger one
+    // slowly, so concurrently running CTAs share its tile.
+    const double a_bytes = double(M) * K * 2, b_bytes = double(N) * K * 2;
+    a.a_fast = a_bytes <= b_bytes ? 1 : 0;
+  }
+  const int tiles = a.tiles_a * a.tiles_b;
+  const int grid = std::min(tiles, ctx->num_sms);
+  cudaError_t e;
+  if (swap) {
+    switch (bn) {
+      case 16: e = launch_linear<16, true>(tmA, tmB, a, grid, stream); break;
+      case 32: e = launch_linear<32, true>(tmA, tmB, a, grid, stream); break;
+      default: e = launch_linear<64, true>(tmA, tmB, a, grid, stream); break;
+    }
+  } else {
+    switch (bn) {
+      case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
+      case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
+      default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
+    }
+  }
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  return NCM_OK;
+}
+
+}  // namespace ncm

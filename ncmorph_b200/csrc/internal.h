@@ -1,0 +1,84 @@
+// Host-side internals shared by the library's translation units: the context
+// object, its device workspace, tensor-map encoding and kernel launchers.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+struct ncm_ctx {
+  int device = 0;
+  int num_sms = 0;
+  int* d_err = nullptr;      // device error word (bit flags, see ptx.cuh)
+  void* ws = nullptr;        // growable device workspace
+  size_t ws_bytes = 0;
+  // host staging for the *_host_f32 entry points
+  void* h_stage = nullptr;
+  size_t h_stage_bytes = 0;
+};
+
+namespace ncm {
+
+// Carves consecutive 256-byte-aligned regions out of the context workspace.
+struct WsCarver {
+  size_t offset = 0;
+  size_t take(size_t bytes) {
+    const size_t at = offset;
+    offset += (bytes + 255) & ~static_cast<size_t>(255);
+    return at;
+  }
+};
+
+// Ensures the workspace holds at least `bytes`; returns its base or nullptr.
+void* ctx_workspace(ncm_ctx* ctx, size_t bytes);
+
+// Builds a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a
+// box of [box_rows, 64] and 128-byte swizzling. Returns false on failure.
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+// ---- RVQ launchers (rvq.cu)
+struct RvqPartial {
+  float d;
+  int idx;
+};
+
+// Plans how many code splits one level uses; returns workspace bytes needed
+// for the partial results (0 when no split).
+struct RvqPlan {
+  int row_blocks, code_tiles, splits, tiles_per_split, n_units, grid;
+  size_t partial_bytes;
+};
+RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K);
+
+// argmin_k (sqnorm[k] - 2 a_n . e_k) over bf16 rows `a` [N,D] (via tmA) and
+// codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials.
+cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
+                              int64_t D, int64_t K, cudaStream_t stream);
+
+// Final code per row (reducing partials when splits > 1), then
+// resid = (src_bf16 ? f32(src_bf16) : resid) - e[code]; shadow = bf16(resid).
+cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_t* codes, const uint16_t* src_bf16,
+                             float* resid, uint16_t* shadow, const uint16_t* codebook, int* err, int64_t N,
+                             int64_t D, int64_t K, bool update, cudaStream_t stream);
+
+cudaError_t launch_code_sqnorm(const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D, cudaStream_t stream);
+cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, int L, uint16_t* recon_bf16,
+                              float* recon_f32, int64_t N, int64_t D, int64_t K, int* err, cudaStream_t stream);
+cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t B, int64_t T, int64_t D, int f,
+                            cudaStream_t stream);
+cudaError_t launch_scale_update(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* recon,
+                                int64_t B, int64_t T, int64_t D, int64_t K, int f, int* err, cudaStream_t stream);
+cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t stream);
+cudaError_t launch_bf16_to_f32(const uint16_t* x, float* y, int64_t n, cudaStream_t stream);
+
+// ---- bf16 linear (gemm.cu)
+// y[M,N] = bf16(x[M,K] . w[N,K]^T + bias). If y_f32 is non-null the f32
+// accumulator (+bias) is written there instead of the bf16 output.
+int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, float* y_f32,
+                int64_t M, int64_t K, int64_t N, cudaStream_t stream);
+
+}  // namespace ncm

@@ -1,0 +1,632 @@
+// Residual-vector-quantisation kernels (R1-R6).
+//
+// The per-level hot kernel, rvq_argmin_kernel, is the distance GEMM
+//     dist[n,k] = ||e_k||^2 - 2 * bf16(r_n) . e_k
+// on the 5th-generation tensor cores (tcgen05.mma, bf16 operands, f32
+// accumulators in tensor memory) with the argmin folded into the epilogue, so
+// the [N,K] distance matrix never leaves the SM. Operand tiles arrive by TMA
+// into 128-byte-swizzled shared memory; a 4-stage mbarrier ring overlaps TMA,
+// MMA and the argmin epilogue, and two 256-column TMEM accumulators let the
+// epilogue of code tile t run while the MMA of tile t+1 proceeds.
+//
+// Warp roles (192 threads, one CTA per SM, persistent over work units):
+//   warp 0     TMA producer (one elected lane)
+//   warp 1     TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5  argmin epilogue, one thread per accumulator row (TMEM lane)
+//
+// A work unit is (row block of 128 residuals, range of code tiles). When the
+// rows alone cannot fill the GPU the code range is split, each split writes a
+// (distance, index) partial per row, and rvq_apply_kernel reduces them.
+#include <cfloat>
+#include <climits>
+#include <cmath>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace ncm {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+
+struct __align__(1024) ArgminSmem {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  float csq[4][BN];  // per epilogue warp: ||e||^2 of the current code tile
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t ARGMIN_SMEM = sizeof(ArgminSmem) + 1024;
+static_assert(ARGMIN_SMEM <= 232448, "shared memory budget");
+
+struct ArgminArgs {
+  const float* csq;
+  int32_t* codes;
+  RvqPartial* part;
+  int* err;
+  int N, D, K;
+  int splits, tiles_per_split, code_tiles, n_units;
+};
+
+__device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err) {
+  *abort_flag = 1;
+  atomicOr(err, kErrWaitTimeout);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    rvq_argmin_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const ArgminArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  ArgminSmem& S = *reinterpret_cast<ArgminSmem*>(smem_raw + pad);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = (args.D + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.tfull[b], 1);
+      mbar_init(&S.tempty[b], 4);
+    }
+    mbar_init(&S.drain, 1);
+    S.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&S.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  volatile int* abort_flag = &S.abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_parity[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
+        const int rb = unit / args.splits;
+        const int sp = unit - rb * args.splits;
+        const int t0 = sp * args.tiles_per_split;
+        const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
+        for (int t = t0; ok && t < t1; ++t) {
+          for (int kc = 0; kc < nk; ++kc) {
+            if (!mbar_wait(&S.empty[stage], phase ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&S.full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, rb * BM);
+            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, t * BN);
+            issued[stage] = true;
+            issued_parity[stage] = phase;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag, args.err);
+        // let every copy this thread issued land before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_it = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
+        const int rb = unit / args.splits;
+        const int sp = unit - rb * args.splits;
+        const int t0 = sp * args.tiles_per_split;
+        const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
+        (void)rb;
+        for (int t = t0; ok && t < t1; ++t) {
+          const uint32_t b = acc_it & 1u;
+          const uint32_t ap = (acc_it >> 1) & 1u;
+          if (!mbar_wait(&S.tempty[b], ap ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dt = tmem + b * BN;
+          for (int kc = 0; kc < nk; ++kc) {
+            if (!mbar_wait(&S.full[stage], phase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(S.a[stage]);
+            const uint32_t b0 = smem_u32(S.b[stage]);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                         (kc | k) != 0 ? 1u : 0u);
+            }
+            tc_commit(&S.empty[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_commit(&S.tfull[b]);
+          ++acc_it;
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag, args.err);
+        tc_commit(&S.drain);  // wait for every MMA issued so far before TMEM is freed
+        mbar_wait(&S.drain, 0, nullptr);
+      }
+    }
+  } else {
+    // -------------------------------------------------- argmin epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    float* csq_s = S.csq[warp - 2];
+    uint32_t acc_it = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
+      const int rb = unit / args.splits;
+      const int sp = unit - rb * args.splits;
+      const int t0 = sp * args.tiles_per_split;
+      const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
+      const int row = rb * BM + q * 32 + lane;
+      float best = INFINITY;
+      int bidx = t0 * BN;
+      for (int t = t0; t < t1; ++t) {
+        const uint32_t b = acc_it & 1u;
+        const uint32_t ap = (acc_it >> 1) & 1u;
+        // ||e||^2 of this tile's codes; codes past K get +inf so they never win
+#pragma unroll
+        for (int j = lane; j < BN; j += 32) {
+          const int code = t * BN + j;
+          csq_s[j] = code < args.K ? __ldg(args.csq + code) : INFINITY;
+        }
+        __syncwarp();
+        if (!mbar_wait(&S.tfull[b], ap, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_x32(tbase + c, v);
+          tmem_wait_ld();
+          const float4* cs4 = reinterpret_cast<const float4*>(csq_s + c);
+          float m = INFINITY;
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 cv = cs4[j4];
+            const float d0 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 0]), cv.x);
+            const float d1 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 1]), cv.y);
+            const float d2 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 2]), cv.z);
+            const float d3 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 3]), cv.w);
+            v[4 * j4 + 0] = __float_as_uint(d0);
+            v[4 * j4 + 1] = __float_as_uint(d1);
+            v[4 * j4 + 2] = __float_as_uint(d2);
+            v[4 * j4 + 3] = __float_as_uint(d3);
+            m = fminf(m, fminf(fminf(d0, d1), fminf(d2, d3)));
+          }
+          if (m < best) {  // strict: an equal distance from a lower code keeps its place
+            int jj = 0;
+#pragma unroll
+            for (int j = 31; j >= 0; --j) jj = (__uint_as_float(v[j]) == m) ? j : jj;
+            best = m;
+            bidx = t * BN + c + jj;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.tempty[b]);
+        ++acc_it;
+      }
+      if (!ok) break;
+      if (row < args.N) {
+        if (args.splits == 1) {
+          args.codes[row] = bidx;
+        } else {
+          args.part[static_cast<size_t>(sp) * args.N + row] = RvqPartial{best, bidx};
+        }
+      }
+    }
+    if (!ok) raise_abort(abort_flag, args.err);
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// -------------------------------------------------------------- apply
+// One warp per row: final code (reducing split partials lexicographically by
+// (distance, index)), then the f32 residual update and its bf16 shadow.
+struct ApplyArgs {
+  const RvqPartial* part;
+  int splits;
+  int32_t* codes;
+  const uint16_t* src_bf16;
+  float* resid;
+  uint16_t* shadow;
+  const uint16_t* codebook;
+  int* err;
+  int N, D, K;
+  int update;
+};
+
+__global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.N) return;
+  int code;
+  if (a.splits > 1) {
+    float bd = INFINITY;
+    int bi = INT_MAX;
+    for (int s = lane; s < a.splits; s += 32) {
+      const RvqPartial p = a.part[static_cast<size_t>(s) * a.N + row];
+      if (p.d < bd || (p.d == bd && p.idx < bi)) {
+        bd = p.d;
+        bi = p.idx;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float od = __shfl_xor_sync(0xffffffffu, bd, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (od < bd || (od == bd && oi < bi)) {
+        bd = od;
+        bi = oi;
+      }
+    }
+    code = bi;
+    if (code == INT_MAX) code = a.part[row].idx;  // every distance was NaN/inf
+    if (lane == 0) a.codes[row] = code;
+  } else {
+    code = a.codes[row];
+  }
+  if (!a.update) return;
+  if (code < 0 || code >= a.K) {
+    if (lane == 0) atomicOr(a.err, kErrBadIndex);
+    return;
+  }
+  const size_t ro = static_cast<size_t>(row) * a.D;
+  const uint16_t* e = a.codebook + static_cast<size_t>(code) * a.D;
+#pragma unroll 4
+  for (int d = lane * 4; d < a.D; d += 128) {
+    float4 r;
+    if (a.src_bf16 != nullptr) {
+      const uint2 s = *reinterpret_cast<const uint2*>(a.src_bf16 + ro + d);
+      r = make_float4(bf16lo(s.x), bf16hi(s.x), bf16lo(s.y), bf16hi(s.y));
+    } else {
+      r = *reinterpret_cast<const float4*>(a.resid + ro + d);
+    }
+    const uint2 ev = __ldg(reinterpret_cast<const uint2*>(e + d));
+    r.x -= bf16lo(ev.x);
+    r.y -= bf16hi(ev.x);
+    r.z -= bf16lo(ev.y);
+    r.w -= bf16hi(ev.y);
+    *reinterpret_cast<float4*>(a.resid + ro + d) = r;
+    if (a.shadow != nullptr) {
+      *reinterpret_cast<uint2*>(a.shadow + ro + d) = make_uint2(pack_bf16x2(r.x, r.y), pack_bf16x2(r.z, r.w));
+    }
+  }
+}
+
+// ---------------------------------------------------------- sqnorm (R1)
+// One warp per code; squares of bf16 values are exact in f64 and their sum is
+// exact for any realistic D, so the f32 result does not depend on order.
+__global__ void __launch_bounds__(256) code_sqnorm_kernel(const uint16_t* __restrict__ cb, float* __restrict__ out,
+                                                          int K, int D) {
+  const int k = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= K) return;
+  const uint16_t* e = cb + static_cast<size_t>(k) * D;
+  double s = 0.0;
+  for (int d = lane * 2; d < D; d += 64) {
+    const uint32_t p = *reinterpret_cast<const uint32_t*>(e + d);
+    const double lo = bf16lo(p), hi = bf16hi(p);
+    s += lo * lo + hi * hi;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[k] = static_cast<float>(s);
+}
+
+// ------------------------------------------------------------ decode (R5)
+// One warp per row: recon[n] = sum_l e_l[codes[l,n]] in f32, level order.
+__global__ void __launch_bounds__(256) rvq_decode_kernel(const int32_t* __restrict__ codes,
+                                                         const uint16_t* __restrict__ cbs, int L,
+                                                         uint16_t* __restrict__ out_bf16,
+                                                         float* __restrict__ out_f32, int N, int D, int K,
+                                                         int* err) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= N) return;
+  for (int l = 0; l < L; ++l) {
+    const int c = codes[static_cast<size_t>(l) * N + row];
+    if (c < 0 || c >= K) {
+      if (lane == 0) atomicOr(err, kErrBadIndex);
+      return;
+    }
+  }
+  const size_t ro = static_cast<size_t>(row) * D;
+  for (int d = lane * 4; d < D; d += 128) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int l = 0; l < L; ++l) {
+      const int c = __ldg(codes + static_cast<size_t>(l) * N + row);
+      const uint2 ev =
+          __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
+      acc.x += bf16lo(ev.x);
+      acc.y += bf16hi(ev.x);
+      acc.z += bf16lo(ev.y);
+      acc.w += bf16hi(ev.y);
+    }
+    if (out_bf16 != nullptr)
+      *reinterpret_cast<uint2*>(out_bf16 + ro + d) =
+          make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+    if (out_f32 != nullptr) *reinterpret_cast<float4*>(out_f32 + ro + d) = acc;
+  }
+}
+
+// -------------------------------------------------------------- pool (R4)
+// y[b,j,:] = (sum_{i<f} x[b,j*f+i,:]) / f, increasing i, f32. One thread per
+// 4 channels of one output row.
+__global__ void __launch_bounds__(256) pool_avg_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                       uint16_t* __restrict__ y_bf16, long long rows_out, int D,
+                                                       int f) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int d4 = D / 4;
+  if (idx >= rows_out * d4) return;
+  const long long orow = idx / d4;
+  const int d = static_cast<int>(idx - orow * d4) * 4;
+  const float* src = x + orow * f * D + d;
+  float4 s = *reinterpret_cast<const float4*>(src);
+  for (int i = 1; i < f; ++i) {
+    const float4 v = *reinterpret_cast<const float4*>(src + static_cast<size_t>(i) * D);
+    s.x += v.x;
+    s.y += v.y;
+    s.z += v.z;
+    s.w += v.w;
+  }
+  const float inv = static_cast<float>(f);
+  s.x /= inv;
+  s.y /= inv;
+  s.z /= inv;
+  s.w /= inv;
+  *reinterpret_cast<float4*>(y + orow * D + d) = s;
+  if (y_bf16 != nullptr)
+    *reinterpret_cast<uint2*>(y_bf16 + orow * D + d) = make_uint2(pack_bf16x2(s.x, s.y), pack_bf16x2(s.z, s.w));
+}
+
+// ------------------------------------------------------ scale update (R6)
+// For each pooled row p of one scale: q = sum_l e_l[codes[l,p]] (f32, level
+// order); then for the f full-resolution rows it covers: r -= q, recon += q.
+__global__ void __launch_bounds__(256) scale_update_kernel(const int32_t* __restrict__ codes,
+                                                           const uint16_t* __restrict__ cbs, int L,
+                                                           float* __restrict__ resid, float* __restrict__ recon,
+                                                           long long rows_pooled, int D, int K, int f, int* err) {
+  const long long p = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (p >= rows_pooled) return;
+  for (int l = 0; l < L; ++l) {
+    const int c = codes[static_cast<size_t>(l) * rows_pooled + p];
+    if (c < 0 || c >= K) {
+      if (lane == 0) atomicOr(err, kErrBadIndex);
+      return;
+    }
+  }
+  for (int d = lane * 4; d < D; d += 128) {
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int l = 0; l < L; ++l) {
+      const int c = __ldg(codes + static_cast<size_t>(l) * rows_pooled + p);
+      const uint2 ev = __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
+      q.x += bf16lo(ev.x);
+      q.y += bf16hi(ev.x);
+      q.z += bf16lo(ev.y);
+      q.w += bf16hi(ev.y);
+    }
+    for (int i = 0; i < f; ++i) {
+      const size_t o = (static_cast<size_t>(p) * f + i) * D + d;
+      float4 r = *reinterpret_cast<float4*>(resid + o);
+      float4 a = *reinterpret_cast<float4*>(recon + o);
+      r.x -= q.x;
+      r.y -= q.y;
+      r.z -= q.z;
+      r.w -= q.w;
+      a.x += q.x;
+      a.y += q.y;
+      a.z += q.z;
+      a.w += q.w;
+      *reinterpret_cast<float4*>(resid + o) = r;
+      *reinterpret_cast<float4*>(recon + o) = a;
+    }
+  }
+}
+
+// ------------------------------------------------------------ casts (L7)
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ y,
+                                                          long long n) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(x + i);
+    *reinterpret_cast<uint2*>(y + i) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  } else {
+    for (long long j = i; j < n; ++j) y[j] = f32_to_bf16(x[j]);
+  }
+}
+
+__global__ void __launch_bounds__(256) bf16_to_f32_kernel(const uint16_t* __restrict__ x, float* __restrict__ y,
+                                                          long long n) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const uint2 v = *reinterpret_cast<const uint2*>(x + i);
+    *reinterpret_cast<float4*>(y + i) = make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y));
+  } else {
+    for (long long j = i; j < n; ++j) y[j] = bf16_to_f32(x[j]);
+  }
+}
+
+}  // namespace
+
+// ================================================================== host
+
+RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
+  RvqPlan p{};
+  p.row_blocks = ceil_div(N, BM);
+  p.code_tiles = ceil_div(K, BN);
+  // Pick the split count that minimises (waves x tiles per unit); prefer fewer
+  // splits on ties since every split adds a partial write and a reduction.
+  long long best_cost = -1;
+  int best_s = 1;
+  for (int s = 1; s <= p.code_tiles; ++s) {
+    const int tps = ceil_div(p.code_tiles, s);
+    const int s_eff = ceil_div(p.code_tiles, tps);
+    if (s_eff != s) continue;
+    const long long units = static_cast<long long>(p.row_blocks) * s;
+    const long long waves = (units + num_sms - 1) / num_sms;
+    const long long cost = waves * tps;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_s = s;
+    }
+  }
+  p.splits = best_s;
+  p.tiles_per_split = ceil_div(p.code_tiles, best_s);
+  p.n_units = p.row_blocks * p.splits;
+  p.grid = p.n_units < num_sms ? p.n_units : num_sms;
+  p.partial_bytes = p.splits > 1 ? static_cast<size_t>(p.splits) * N * sizeof(RvqPartial) : 0;
+  return p;
+}
+
+cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
+                              int64_t D, int64_t K, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(rvq_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ARGMIN_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  ArgminArgs a;
+  a.csq = sqnorm;
+  a.codes = codes;
+  a.part = part;
+  a.err = err;
+  a.N = static_cast<int>(N);
+  a.D = static_cast<int>(D);
+  a.K = static_cast<int>(K);
+  a.splits = plan.splits;
+  a.tiles_per_split = plan.tiles_per_split;
+  a.code_tiles = plan.code_tiles;
+  a.n_units = plan.n_units;
+  rvq_argmin_kernel<<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_t* codes, const uint16_t* src_bf16,
+                             float* resid, uint16_t* shadow, const uint16_t* codebook, int* err, int64_t N,
+                             int64_t D, int64_t K, bool update, cudaStream_t stream) {
+  if (plan.splits == 1 && !update) return cudaSuccess;
+  ApplyArgs a;
+  a.part = part;
+  a.splits = plan.splits;
+  a.codes = codes;
+  a.src_bf16 = src_bf16;
+  a.resid = resid;
+  a.shadow = shadow;
+  a.codebook = codebook;
+  a.err = err;
+  a.N = static_cast<int>(N);
+  a.D = static_cast<int>(D);
+  a.K = static_cast<int>(K);
+  a.update = update ? 1 : 0;
+  rvq_apply_kernel<<<ceil_div(N, 8), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_code_sqnorm(const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D, cudaStream_t stream) {
+  code_sqnorm_kernel<<<ceil_div(K, 8), 256, 0, stream>>>(codebook, sqnorm, static_cast<int>(K),
+                                                         static_cast<int>(D));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, int L, uint16_t* recon_bf16,
+                              float* recon_f32, int64_t N, int64_t D, int64_t K, int* err, cudaStream_t stream) {
+  rvq_decode_kernel<<<ceil_div(N, 8), 256, 0, stream>>>(codes, codebooks, L, recon_bf16, recon_f32,
+                                                        static_cast<int>(N), static_cast<int>(D),
+                                                        static_cast<int>(K), err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t B, int64_t T, int64_t D, int f,
+                            cudaStream_t stream) {
+  const long long rows_out = B * (T / f);
+  const long long threads = rows_out * (D / 4);
+  pool_avg_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, y_bf16, rows_out,
+                                                                                   static_cast<int>(D), f);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scale_update(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* recon,
+                                int64_t B, int64_t T, int64_t D, int64_t K, int f, int* err, cudaStream_t stream) {
+  const long long rows_pooled = B * (T / f);
+  scale_update_kernel<<<static_cast<unsigned>((rows_pooled + 7) / 8), 256, 0, stream>>>(
+      codes, codebooks, L, resid, recon, rows_pooled, static_cast<int>(D), static_cast<int>(K), f, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t stream) {
+  const long long threads = (n + 3) / 4;
+  if (threads == 0) return cudaSuccess;
+  f32_to_bf16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const uint16_t* x, float* y, int64_t n, cudaStream_t stream) {
+  const long long threads = (n + 3) / 4;
+  if (threads == 0) return cudaSuccess;
+  bf16_to_f32_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+}  // namespace ncm

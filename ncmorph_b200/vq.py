@@ -1,0 +1,150 @@
+"""Residual vector quantisation on B200: the device-side mirror of the
+multiscale RVQ tokenizer forward that ncmorph specifies for its planned
+``packages/vq`` (research/reference/vq_forward_semantics.md:59-82,
+research/ncm_facts.md:62-82, PROJECT.md:250-285).
+
+Numerics (fixed by this implementation, restated by the CPU oracle):
+  * residuals are f32; the distance GEMM operand is bf16(residual);
+  * codebooks are bf16; ||e_k||^2 is summed exactly (f64) and rounded to f32;
+  * dist = ||e_k||^2 - 2 * (bf16(r) . e_k) with f32 accumulation on tcgen05;
+    ||r||^2 is dropped (constant per row);
+  * argmin picks the lowest index among equal distances (torch.argmin rule);
+  * the residual update r -= e[code] is exact f32 arithmetic;
+  * reconstructions sum the chosen codewords in f32 (level order) and round
+    once to bf16.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .device import context, need, ptr, stream_of
+
+bf16 = torch.bfloat16
+
+
+def code_sqnorm(codebook: torch.Tensor) -> torch.Tensor:
+    """||e_k||^2 for a bf16 codebook [..., K, D] -> f32 [..., K] (R1)."""
+    need(codebook, bf16, "codebook")
+    D = codebook.shape[-1]
+    K = codebook.numel() // D
+    out = torch.empty(codebook.shape[:-1], dtype=torch.float32, device=codebook.device)
+    _lib.call("ncm_code_sqnorm", context(codebook.device), ptr(codebook), ptr(out), K, D, stream_of(codebook))
+    return out
+
+
+def rvq_level(residual: torch.Tensor, codebook: torch.Tensor, sqnorm: torch.Tensor | None = None,
+              codes: torch.Tensor | None = None) -> torch.Tensor:
+    """One RVQ level (R2+R3): returns int32 codes [N]; updates `residual` in place."""
+    N, D = residual.shape
+    K = codebook.shape[0]
+    need(residual, torch.float32, "residual")
+    need(codebook, bf16, "codebook", (K, D))
+    if sqnorm is not None:
+        need(sqnorm, torch.float32, "sqnorm", (K,))
+    if codes is None:
+        codes = torch.empty(N, dtype=torch.int32, device=residual.device)
+    need(codes, torch.int32, "codes", (N,))
+    _lib.call("ncm_rvq_level", context(residual.device), ptr(residual), ptr(codebook), ptr(sqnorm), ptr(codes),
+              N, D, K, stream_of(residual))
+    return codes
+
+
+def rvq_encode(x: torch.Tensor, codebooks: torch.Tensor, sqnorms: torch.Tensor | None = None, *,
+               want_recon: bool = True, want_residual: bool = False,
+               codes: torch.Tensor | None = None, recon: torch.Tensor | None = None):
+    """L residual levels over bf16 x [N, D] with bf16 codebooks [L, K, D].
+
+    Returns (codes int32 [L, N], recon bf16 [N, D] or None, residual f32 [N, D] or None).
+    """
+    N, D = x.shape
+    L, K, D2 = codebooks.shape
+    if D2 != D:
+        raise ValueError("codebook width differs from x")
+    need(x, bf16, "x")
+    need(codebooks, bf16, "codebooks")
+    if sqnorms is not None:
+        need(sqnorms, torch.float32, "sqnorms", (L, K))
+    dev = x.device
+    if codes is None:
+        codes = torch.empty((L, N), dtype=torch.int32, device=dev)
+    need(codes, torch.int32, "codes", (L, N))
+    if want_recon and recon is None:
+        recon = torch.empty((N, D), dtype=bf16, device=dev)
+    if recon is not None:
+        need(recon, bf16, "recon", (N, D))
+    residual = torch.empty((N, D), dtype=torch.float32, device=dev) if want_residual else None
+    _lib.call("ncm_rvq_encode", context(dev), ptr(x), ptr(codebooks), ptr(sqnorms), L, ptr(codes), ptr(recon),
+              ptr(residual), N, D, K, stream_of(x))
+    return codes, recon, residual
+
+
+def rvq_decode(codes: torch.Tensor, codebooks: torch.Tensor) -> torch.Tensor:
+    """recon[n] = bf16(sum_l e_l[codes[l, n]]) (R5)."""
+    L, N = codes.shape
+    L2, K, D = codebooks.shape
+    if L2 != L:
+        raise ValueError("codes and codebooks disagree on the number of levels")
+    need(codes, torch.int32, "codes")
+    need(codebooks, bf16, "codebooks")
+    recon = torch.empty((N, D), dtype=bf16, device=codes.device)
+    _lib.call("ncm_rvq_decode", context(codes.device), ptr(codes), ptr(codebooks), L, ptr(recon), N, D, K,
+              stream_of(codes))
+    return recon
+
+
+def pool_avg(x: torch.Tensor, factor: int) -> torch.Tensor:
+    """Area pooling [B, T, D] -> [B, T/factor, D] in f32 (R4)."""
+    B, T, D = x.shape
+    need(x, torch.float32, "x")
+    y = torch.empty((B, T // factor, D), dtype=torch.float32, device=x.device)
+    _lib.call("ncm_pool_avg", context(x.device), ptr(x), ptr(y), B, T, D, int(factor), stream_of(x))
+    return y
+
+
+def tokenizer_config(batch: int, seq_len: int, model_width: int, vq_width: int, codebook_size: int,
+                     pool_factors: list[int], levels_per_scale: int) -> _lib.TokenizerConfig:
+    cfg = _lib.TokenizerConfig()
+    cfg.batch, cfg.seq_len, cfg.model_width, cfg.vq_width = batch, seq_len, model_width, vq_width
+    cfg.codebook_size = codebook_size
+    cfg.num_scales = len(pool_factors)
+    cfg.levels_per_scale = levels_per_scale
+    for i, f in enumerate(pool_factors):
+        cfg.pool_factors[i] = int(f)
+    return cfg
+
+
+def tokenizer_forward(x: torch.Tensor, w_in: torch.Tensor, codebooks: torch.Tensor, w_out: torch.Tensor,
+                      pool_factors: list[int], *, b_in: torch.Tensor | None = None,
+                      b_out: torch.Tensor | None = None, sqnorms: torch.Tensor | None = None):
+    """Multiscale RVQ tokenizer forward (R6).
+
+    x [B, T, Din] bf16; w_in [D, Din]; codebooks [S, L, K, D]; w_out [Din, D].
+    Returns (codes: list over scales of int32 [L, B*T/f_s], recon bf16 [B, T, D], y bf16 [B, T, Din]).
+    """
+    B, T, Din = x.shape
+    S, L, K, D = codebooks.shape
+    if len(pool_factors) != S:
+        raise ValueError("one pool factor per scale is required")
+    need(x, bf16, "x")
+    need(w_in, bf16, "w_in", (D, Din))
+    need(codebooks, bf16, "codebooks")
+    need(w_out, bf16, "w_out", (Din, D))
+    if sqnorms is not None:
+        need(sqnorms, torch.float32, "sqnorms", (S, L, K))
+    dev = x.device
+    rows = [B * T // f for f in pool_factors]
+    codes_flat = torch.empty(sum(L * r for r in rows), dtype=torch.int32, device=dev)
+    recon = torch.empty((B, T, D), dtype=bf16, device=dev)
+    y = torch.empty((B, T, Din), dtype=bf16, device=dev)
+    cfg = tokenizer_config(B, T, Din, D, K, pool_factors, L)
+    _lib.call("ncm_tokenizer_forward", context(dev), ctypes.byref(cfg), ptr(x), ptr(w_in), ptr(b_in),
+              ptr(codebooks), ptr(sqnorms), ptr(w_out), ptr(b_out), ptr(codes_flat), ptr(recon), ptr(y),
+              stream_of(x))
+    codes, off = [], 0
+    for r in rows:
+        codes.append(codes_flat[off:off + L * r].view(L, r))
+        off += L * r
+    return codes, recon, y

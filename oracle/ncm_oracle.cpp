@@ -1,0 +1,639 @@
+// CPU oracle for ncmorph_b200 — TEST INFRASTRUCTURE ONLY (see ncm_oracle.h).
+//
+// Compiled with -ffp-contract=off: products and sums are rounded separately
+// exactly where the reference's strict-float Zig does, and fused only where
+// the reference calls @mulAdd (written here as fmaf).
+#include "ncm_oracle.h"
+
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+inline uint32_t f2u(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return u;
+}
+inline float u2f(uint32_t u) {
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// packages/bf16/root.zig:17-22 — RNE, every NaN -> 0x7FC0
+inline uint16_t bf16_from(float v) {
+  const uint32_t x = f2u(v);
+  if ((x & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  const uint32_t bias = 0x7FFFu + ((x >> 16) & 1u);
+  return static_cast<uint16_t>((x + bias) >> 16);
+}
+// packages/bf16/root.zig:25-27
+inline float bf16_to(uint16_t b) { return u2f(static_cast<uint32_t>(b) << 16); }
+// packages/kernels/root.zig:10-12
+inline float rb(float v) { return bf16_to(bf16_from(v)); }
+inline float mrb(float v, bool on) { return on ? rb(v) : v; }
+// packages/kernels/root.zig:144-148
+inline float ftz(float v) {
+  const uint32_t b = f2u(v);
+  if ((b & 0x7F800000u) == 0) return u2f(b & 0x80000000u);
+  return v;
+}
+
+const float kInf = std::numeric_limits<float>::infinity();
+
+// packages/kernels/root.zig:106-142, one output element.
+inline float matmul_bf16_elem(const float* x, const float* w, const float* bias, size_t o, size_t in_w) {
+  const size_t rbs = std::min(in_w, in_w > 1024 ? size_t(1024) : size_t(512));
+  float sum = 0.0f;
+  for (size_t bs = 0; bs < in_w; bs += rbs) {
+    const size_t be = std::min(bs + rbs, in_w);
+    float partial = 0.0f;
+    size_t i = bs;
+    while (i + 1 < be) {
+      const float xh = ftz(rb(x[i + 1]));
+      const float wh = ftz(rb(w[i + 1]));
+      const float xl = ftz(rb(x[i]));
+      const float wl = ftz(rb(w[i]));
+      partial = ftz(std::fmaf(xh, wh, partial));
+      partial = ftz(std::fmaf(xl, wl, partial));
+      i += 2;
+    }
+    if (i < be) partial = ftz(std::fmaf(ftz(rb(x[i])), ftz(rb(w[i])), partial));
+    sum += partial;
+  }
+  if (bias != nullptr) sum += rb(bias[o]);
+  return rb(sum);
+}
+
+// packages/kernels/root.zig:583-609 (project)
+void project(const float* in, const float* w, const float* bias, float* out, size_t T, size_t in_w, size_t out_w,
+             bool bf16_mode) {
+  if (bf16_mode) {
+    orc_matmul_bf16(in, w, bias, out, T, in_w, out_w);
+    return;
+  }
+  orc_matmul(in, w, out, T, in_w, out_w);
+  if (bias != nullptr)
+    for (size_t t = 0; t < T; ++t)
+      for (size_t o = 0; o < out_w; ++o) out[t * out_w + o] += bias[o];
+}
+
+// packages/kernels/root.zig:615-633
+void rotate_head(float* v, const float* c, const float* s, size_t n, bool bm) {
+  const size_t h = n / 2;
+  for (size_t i = 0; i < h; ++i) {
+    const float first = v[i];
+    const float second = v[i + h];
+    const float cos_first = mrb(c[i], bm);
+    const float sin_first = mrb(s[i], bm);
+    const float cos_second = mrb(c[i + h], bm);
+    const float sin_second = mrb(s[i + h], bm);
+    const float left = mrb(first * cos_first, bm);
+    const float right = mrb(-second * sin_first, bm);
+    const float right2 = mrb(first * sin_second, bm);
+    const float left2 = mrb(second * cos_second, bm);
+    v[i] = mrb(left + right, bm);
+    v[i + h] = mrb(left2 + right2, bm);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+uint16_t orc_bf16_from_f32(float v) { return bf16_from(v); }
+float orc_bf16_to_f32(uint16_t b) { return bf16_to(b); }
+void orc_bf16_from_f32_n(const float* x, uint16_t* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = bf16_from(x[i]);
+}
+void orc_round_bf16_n(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = rb(x[i]);
+}
+
+// packages/kernels/root.zig:25-65: 32-wide tiles over tokens, outputs and
+// inputs; each output accumulates in increasing k.
+void orc_matmul(const float* in, const float* w, float* out, size_t T, size_t in_w, size_t out_w) {
+  const size_t B = 32;
+  for (size_t t0 = 0; t0 < T; t0 += B) {
+    const size_t t1 = std::min(t0 + B, T);
+    for (size_t o0 = 0; o0 < out_w; o0 += B) {
+      const size_t o1 = std::min(o0 + B, out_w);
+      for (size_t t = t0; t < t1; ++t)
+        for (size_t o = o0; o < o1; ++o) out[t * out_w + o] = 0.0f;
+      for (size_t i0 = 0; i0 < in_w; i0 += B) {
+        const size_t i1 = std::min(i0 + B, in_w);
+        for (size_t t = t0; t < t1; ++t)
+          for (size_t o = o0; o < o1; ++o) {
+            float acc = out[t * out_w + o];
+            for (size_t i = i0; i < i1; ++i) acc += in[t * in_w + i] * w[o * in_w + i];
+            out[t * out_w + o] = acc;
+          }
+      }
+    }
+  }
+}
+
+// packages/kernels/root.zig:71-93
+void orc_matmul_reference(const float* in, const float* w, float* out, size_t T, size_t in_w, size_t out_w) {
+  for (size_t t = 0; t < T; ++t)
+    for (size_t o = 0; o < out_w; ++o) {
+      float s = 0.0f;
+      for (size_t i = 0; i < in_w; ++i) s += in[t * in_w + i] * w[o * in_w + i];
+      out[t * out_w + o] = s;
+    }
+}
+
+void orc_matmul_bf16(const float* in, const float* w, const float* bias, float* out, size_t T, size_t in_w,
+                     size_t out_w) {
+  for (size_t t = 0; t < T; ++t)
+    for (size_t o = 0; o < out_w; ++o) out[t * out_w + o] = matmul_bf16_elem(in + t * in_w, w + o * in_w, bias, o, in_w);
+}
+
+void orc_matmul_bf16_mt(const float* in, const float* w, const float* bias, float* out, size_t T, size_t in_w,
+                        size_t out_w, int threads) {
+  const long long total = static_cast<long long>(T) * static_cast<long long>(out_w);
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (long long e = 0; e < total; ++e) {
+    const size_t t = static_cast<size_t>(e) / out_w;
+    const size_t o = static_cast<size_t>(e) % out_w;
+    out[e] = matmul_bf16_elem(in + t * in_w, w + o * in_w, bias, o, in_w);
+  }
+}
+
+// packages/kernels/root.zig:152-224 — PyTorch's 8-lane AVX2 cascade order.
+float orc_sum_squares_pinned(const float* x, size_t n) {
+  const size_t vw = 8;
+  const size_t vc = n / vw;
+  const size_t row_count = vc / 4;
+  size_t log2_rows = 0, log2_limit = 1;
+  while (log2_limit < row_count) {
+    ++log2_rows;
+    log2_limit *= 2;
+  }
+  const size_t level_power = std::max<size_t>(4, log2_rows / 4);
+  const size_t level_step = size_t(1) << level_power;
+  const size_t level_mask = level_step - 1;
+  float acc[4][4][8];
+  std::memset(acc, 0, sizeof(acc));
+  size_t ri = 0;
+  while (ri + level_step <= row_count) {
+    for (size_t s = 0; s < level_step; ++s)
+      for (size_t r = 0; r < 4; ++r) {
+        const size_t vi = (ri + s) * 4 + r;
+        for (size_t l = 0; l < vw; ++l) {
+          const float v = x[vi * vw + l];
+          acc[0][r][l] += v * v;
+        }
+      }
+    ri += level_step;
+    for (size_t lv = 1; lv < 4; ++lv) {
+      for (size_t r = 0; r < 4; ++r)
+        for (size_t l = 0; l < vw; ++l) {
+          acc[lv][r][l] += acc[lv - 1][r][l];
+          acc[lv - 1][r][l] = 0.0f;
+        }
+      if ((ri & (level_mask << (lv * level_power))) != 0) break;
+    }
+  }
+  for (size_t g = ri; g < row_count; ++g)
+    for (size_t r = 0; r < 4; ++r) {
+      const size_t vi = g * 4 + r;
+      for (size_t l = 0; l < vw; ++l) {
+        const float v = x[vi * vw + l];
+        acc[0][r][l] += v * v;
+      }
+    }
+  for (size_t lv = 1; lv < 4; ++lv)
+    for (size_t r = 0; r < 4; ++r)
+      for (size_t l = 0; l < vw; ++l) acc[0][r][l] += acc[lv][r][l];
+  for (size_t vi = row_count * 4; vi < vc; ++vi)
+    for (size_t l = 0; l < vw; ++l) {
+      const float v = x[vi * vw + l];
+      acc[0][0][l] += v * v;
+    }
+  float vs[8];
+  for (size_t l = 0; l < vw; ++l) vs[l] = acc[0][0][l];
+  for (size_t r = 1; r < 4; ++r)
+    for (size_t l = 0; l < vw; ++l) vs[l] += acc[0][r][l];
+  float sum = 0.0f;
+  for (size_t i = vc * vw; i < n; ++i) sum += x[i] * x[i];
+  for (size_t l = 0; l < vw; ++l) sum += vs[l];
+  return sum;
+}
+
+// packages/kernels/root.zig:226-239
+void orc_rms_norm(const float* in, const float* w, float* out, size_t n, float eps) {
+  const float ss = orc_sum_squares_pinned(in, n);
+  const float ms = ss / static_cast<float>(n);
+  const float inv = 1.0f / std::sqrt(ms + eps);
+  for (size_t i = 0; i < n; ++i) {
+    const float nv = in[i] * inv;
+    out[i] = nv * w[i];
+  }
+}
+
+// packages/kernels/root.zig:243-252
+void orc_rms_norm_bf16(const float* in, const float* w, float* out, size_t n, float eps) {
+  const float ss = orc_sum_squares_pinned(in, n);
+  const float ms = ss / static_cast<float>(n);
+  const float inv = 1.0f / std::sqrt(ms + eps);
+  for (size_t i = 0; i < n; ++i) {
+    const float nv = rb(in[i] * inv);
+    out[i] = rb(nv * rb(w[i]));
+  }
+}
+
+// packages/kernels/root.zig:255-261 (std.math.exp restated as C expf)
+void orc_silu(const float* in, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    const float v = in[i];
+    const float sg = 1.0f / (1.0f + std::exp(-v));
+    out[i] = v * sg;
+  }
+}
+
+// packages/kernels/root.zig:264-269
+void orc_silu_bf16(const float* in, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    const float v = in[i];
+    out[i] = rb(v / (1.0f + std::exp(-v)));
+  }
+}
+
+// packages/kernels/root.zig:272-285
+void orc_softmax(const float* in, float* out, size_t n) {
+  float m = in[0];
+  for (size_t i = 1; i < n; ++i) m = std::max(m, in[i]);
+  float s = 0.0f;
+  for (size_t i = 0; i < n; ++i) {
+    out[i] = std::exp(in[i] - m);
+    s += out[i];
+  }
+  for (size_t i = 0; i < n; ++i) out[i] /= s;
+}
+
+// src/ncm_norm.zig:21-49
+void orc_rms_norm_rows(const float* in, const float* w, const float* bias, float* out, size_t rows, size_t width,
+                       float eps) {
+  for (size_t r = 0; r < rows; ++r) {
+    orc_rms_norm(in + r * width, w, out + r * width, width, eps);
+    if (bias != nullptr)
+      for (size_t i = 0; i < width; ++i) out[r * width + i] += bias[i];
+  }
+}
+
+// packages/kernels/root.zig:305-348, :668-674 (libm powf/cosf/sinf as the reference links them)
+void orc_rope_default(size_t hd, float theta, size_t positions, float* inv_freq, float* cos_t, float* sin_t) {
+  const float hdf = static_cast<float>(hd);
+  for (size_t i = 0; i < hd / 2; ++i) {
+    const float ex = static_cast<float>(2 * i) / hdf;
+    inv_freq[i] = 1.0f / powf(theta, ex);
+  }
+  orc_rope_tables(inv_freq, hd / 2, positions, cos_t, sin_t);
+}
+
+void orc_rope_tables(const float* inv_freq, size_t half, size_t positions, float* cos_t, float* sin_t) {
+  const size_t hd = half * 2;
+  for (size_t p = 0; p < positions; ++p) {
+    const float pf = static_cast<float>(p);
+    for (size_t i = 0; i < half; ++i) {
+      const float ang = pf * inv_freq[i];
+      const float cv = cosf(ang), sv = sinf(ang);
+      cos_t[p * hd + i] = cv;
+      cos_t[p * hd + half + i] = cv;
+      sin_t[p * hd + i] = sv;
+      sin_t[p * hd + half + i] = sv;
+    }
+  }
+}
+
+// packages/kernels/root.zig:636-666
+void orc_rope_llama3(size_t hd, float theta, float factor, float low_ff, float high_ff, size_t orig_max,
+                     float* inv_freq) {
+  const float hdf = static_cast<float>(hd);
+  for (size_t i = 0; i < hd / 2; ++i) {
+    const float ex = static_cast<float>(2 * i) / hdf;
+    inv_freq[i] = 1.0f / powf(theta, ex);
+  }
+  const float old_ctx = static_cast<float>(orig_max);
+  const float low_wl = static_cast<float>(static_cast<double>(orig_max) / static_cast<double>(low_ff));
+  const float high_wl = static_cast<float>(static_cast<double>(orig_max) / static_cast<double>(high_ff));
+  const float two_pi = static_cast<float>(2.0 * 3.14159265358979323846);
+  for (size_t i = 0; i < hd / 2; ++i) {
+    const float f = inv_freq[i];
+    const float wl = two_pi / f;
+    const float lf = wl > low_wl ? f / factor : f;
+    const float sm = (old_ctx / wl - low_ff) / (high_ff - low_ff);
+    const float smoothed = (1.0f - sm) * lf / factor + sm * lf;
+    const bool medium = !(wl < high_wl) && !(wl > low_wl);
+    inv_freq[i] = medium ? smoothed : lf;
+  }
+}
+
+// packages/kernels/root.zig:380-399
+void orc_causal_mask(const size_t* qpos, size_t nq, const size_t* kpos, size_t nk, long window, uint8_t* out) {
+  for (size_t q = 0; q < nq; ++q)
+    for (size_t k = 0; k < nk; ++k) {
+      const bool causal = kpos[k] <= qpos[q];
+      bool in_window = true;
+      if (window > 0) {
+        const size_t w = static_cast<size_t>(window);
+        in_window = qpos[q] < w || kpos[k] > qpos[q] - w;
+      }
+      out[q * nk + k] = (causal && in_window) ? 1 : 0;
+    }
+}
+
+static bool padded(const uint8_t* pm, size_t pl, size_t i) { return pl != 0 && pm[i] != 0; }
+
+// src/ncm_mask.zig:10-42
+int orc_block_diagonal_mask(size_t prefix, const size_t* levels, size_t nl, const uint8_t* pm, size_t pl,
+                            uint8_t* out, size_t out_len) {
+  if (pl != 0 && pl != prefix) return -1;
+  size_t tgt = 0;
+  for (size_t i = 0; i < nl; ++i) tgt += levels[i];
+  const size_t S = prefix + tgt;
+  if (out_len != S * S) return -2;
+  std::memset(out, 0, out_len);
+  for (size_t q = 0; q < prefix; ++q)
+    for (size_t k = 0; k < prefix; ++k) out[q * S + k] = !padded(pm, pl, k);
+  size_t off = prefix;
+  for (size_t i = 0; i < nl; ++i) {
+    for (size_t q = off; q < off + levels[i]; ++q) {
+      for (size_t k = 0; k < prefix; ++k) out[q * S + k] = !padded(pm, pl, k);
+      for (size_t k = off; k < off + levels[i]; ++k) out[q * S + k] = 1;
+    }
+    off += levels[i];
+  }
+  return 0;
+}
+
+// Block-causal over scales: the block-diagonal mask plus, for each level,
+// every position of the earlier (coarser) levels. Not in ncmorph (its
+// PROJECT.md D8 keeps block_causal out of scope); restated for the config
+// whose mask is block-causal.
+int orc_block_causal_mask(size_t prefix, const size_t* levels, size_t nl, const uint8_t* pm, size_t pl, uint8_t* out,
+                          size_t out_len) {
+  const int rc = orc_block_diagonal_mask(prefix, levels, nl, pm, pl, out, out_len);
+  if (rc != 0) return rc;
+  size_t tgt = 0;
+  for (size_t i = 0; i < nl; ++i) tgt += levels[i];
+  const size_t S = prefix + tgt;
+  size_t off = prefix;
+  for (size_t i = 0; i < nl; ++i) {
+    for (size_t q = off; q < off + levels[i]; ++q)
+      for (size_t k = prefix; k < off; ++k) out[q * S + k] = 1;
+    off += levels[i];
+  }
+  return 0;
+}
+
+// src/ncm_position.zig:11-22
+int orc_fill_level_positions(size_t prefix, const size_t* levels, size_t nl, size_t* out, size_t out_len) {
+  size_t S = prefix;
+  for (size_t i = 0; i < nl; ++i) S += levels[i];
+  if (out_len != S) return -1;
+  for (size_t p = 0; p < prefix; ++p) out[p] = p;
+  size_t off = prefix;
+  for (size_t i = 0; i < nl; ++i) {
+    for (size_t p = 0; p < levels[i]; ++p) out[off + p] = p;
+    off += levels[i];
+  }
+  return 0;
+}
+
+// src/ncm_model.zig:296-326: x <- x + conv1d_k3(x) (zero padding), weight [out][in][3]
+int orc_apply_post_upsample_conv(float* x, const float* w, const float* b, size_t rows, size_t width) {
+  std::vector<float> out(rows * width);
+  for (size_t p = 0; p < rows; ++p)
+    for (size_t oc = 0; oc < width; ++oc) {
+      float v = b[oc];
+      for (size_t ic = 0; ic < width; ++ic)
+        for (size_t kk = 0; kk < 3; ++kk) {
+          const long ip = static_cast<long>(p) + static_cast<long>(kk) - 1;
+          if (ip < 0 || ip >= static_cast<long>(rows)) continue;
+          v += w[oc * width * 3 + ic * 3 + kk] * x[static_cast<size_t>(ip) * width + ic];
+        }
+      out[p * width + oc] = x[p * width + oc] + v;
+    }
+  std::memcpy(x, out.data(), sizeof(float) * rows * width);
+  return 0;
+}
+
+// packages/kernels/root.zig:450-581
+int orc_attention(const float* in, const orc_attention_weights_t* W, size_t T, size_t hidden, size_t H, size_t Hkv,
+                  size_t hd, float eps, const float* cos_t, const float* sin_t, const uint8_t* mask, float* out,
+                  int bf16_mode, float* ctx_trace) {
+  if (T == 0 || hidden == 0 || hd == 0 || H == 0 || Hkv == 0 || H % Hkv != 0) return -1;
+  if ((W->q_norm == nullptr) != (W->k_norm == nullptr)) return -1;
+  const bool bm = bf16_mode != 0;
+  const size_t qw = H * hd, kvw = Hkv * hd;
+  std::vector<float> Q(T * qw), Kt(T * kvw), V(T * kvw), C(T * qw);
+  project(in, W->q_w, W->q_b, Q.data(), T, hidden, qw, bm);
+  project(in, W->k_w, W->k_b, Kt.data(), T, hidden, kvw, bm);
+  project(in, W->v_w, W->v_b, V.data(), T, hidden, kvw, bm);
+  const size_t group = H / Hkv;
+  for (size_t t = 0; t < T; ++t)
+    for (size_t h = 0; h < H; ++h) {
+      float* q = &Q[t * qw + h * hd];
+      if (W->q_norm) {
+        if (bm)
+          orc_rms_norm_bf16(q, W->q_norm, q, hd, eps);
+        else
+          orc_rms_norm(q, W->q_norm, q, hd, eps);
+      }
+      rotate_head(q, cos_t + t * hd, sin_t + t * hd, hd, bm);
+    }
+  for (size_t t = 0; t < T; ++t)
+    for (size_t h = 0; h < Hkv; ++h) {
+      float* k = &Kt[t * kvw + h * hd];
+      if (W->k_norm) {
+        if (bm)
+          orc_rms_norm_bf16(k, W->k_norm, k, hd, eps);
+        else
+          orc_rms_norm(k, W->k_norm, k, hd, eps);
+      }
+      rotate_head(k, cos_t + t * hd, sin_t + t * hd, hd, bm);
+    }
+  std::vector<float> sc(T), pr(T);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  for (size_t qi = 0; qi < T; ++qi)
+    for (size_t h = 0; h < H; ++h) {
+      const float* q = &Q[qi * qw + h * hd];
+      const size_t kvh = h / group;
+      bool any = false;
+      for (size_t ki = 0; ki < T; ++ki) {
+        if (!mask[qi * T + ki]) {
+          sc[ki] = -kInf;
+          continue;
+        }
+        any = true;
+        const float* k = &Kt[ki * kvw + kvh * hd];
+        float s = 0.0f;
+        for (size_t d = 0; d < hd; ++d) s += q[d] * k[d];
+        const float sv = mrb(s, bm);
+        sc[ki] = mrb(sv * scale, bm);
+      }
+      if (any) {
+        orc_softmax(sc.data(), pr.data(), T);
+        if (bm)
+          for (size_t ki = 0; ki < T; ++ki) pr[ki] = rb(pr[ki]);
+      } else {
+        std::fill(pr.begin(), pr.end(), 0.0f);
+      }
+      float* c = &C[qi * qw + h * hd];
+      for (size_t d = 0; d < hd; ++d) {
+        float s = 0.0f;
+        for (size_t ki = 0; ki < T; ++ki) s += pr[ki] * V[ki * kvw + kvh * hd + d];
+        c[d] = mrb(s, bm);
+      }
+    }
+  if (ctx_trace) std::memcpy(ctx_trace, C.data(), sizeof(float) * T * qw);
+  project(C.data(), W->o_w, W->o_b, out, T, qw, hidden, bm);
+  return 0;
+}
+
+// ------------------------------------------------------------------- RVQ
+// ||e_k||^2: squares of bf16 values are exact in f64 and their f64 sum is
+// exact for any realistic D; one rounding to f32.
+void orc_code_sqnorm(const uint16_t* cb, float* out, size_t K, size_t D) {
+  for (size_t k = 0; k < K; ++k) {
+    double s = 0.0;
+    for (size_t d = 0; d < D; ++d) {
+      const double v = bf16_to(cb[k * D + d]);
+      s += v * v;
+    }
+    out[k] = static_cast<float>(s);
+  }
+}
+
+// One RVQ level (vq_forward_semantics.md:68-72, distance :81):
+//   dist_k = fmaf(-2, dot_k, ||e_k||^2), dot_k = sequential fmaf over d of bf16(r)_d * e_kd
+//   best = lowest k with the minimal dist (torch.argmin tie rule)
+//   r -= e[code] (f32), code = codes_in[n] when teacher-forcing, else best.
+void orc_rvq_level(float* resid, const uint16_t* cb, const float* sqnorm, const int32_t* codes_in,
+                   int32_t* best_out, float* rel_gap, size_t N, size_t D, size_t K, int threads) {
+  constexpr size_t KB = 16;  // codes per block (independent accumulators)
+  constexpr size_t RB = 4;   // rows per block
+  const size_t Kp = (K + KB - 1) / KB * KB;
+  std::vector<float> eT(D * Kp, 0.0f);  // codebook transposed to [D][Kp]
+  for (size_t k = 0; k < K; ++k)
+    for (size_t d = 0; d < D; ++d) eT[d * Kp + k] = bf16_to(cb[k * D + d]);
+  const long long nblk = static_cast<long long>((N + RB - 1) / RB);
+  if (threads < 1) threads = 1;
+#pragma omp parallel num_threads(threads)
+  {
+    std::vector<float> a(RB * D);
+    std::vector<double> a2(RB);
+#pragma omp for schedule(dynamic, 1)
+    for (long long blk = 0; blk < nblk; ++blk) {
+      const size_t n0 = static_cast<size_t>(blk) * RB;
+      const size_t nr = std::min(RB, N - n0);
+      for (size_t r = 0; r < RB; ++r) {
+        double s = 0.0;
+        for (size_t d = 0; d < D; ++d) {
+          const float v = r < nr ? rb(resid[(n0 + r) * D + d]) : 0.0f;
+          a[r * D + d] = v;
+          s += static_cast<double>(v) * v;
+        }
+        a2[r] = s;
+      }
+      float best[RB], second[RB];
+      int32_t bi[RB];
+      for (size_t r = 0; r < RB; ++r) best[r] = kInf, second[r] = kInf, bi[r] = 0;
+      for (size_t k0 = 0; k0 < Kp; k0 += KB) {
+        float acc[RB][KB];
+        for (size_t r = 0; r < RB; ++r)
+          for (size_t j = 0; j < KB; ++j) acc[r][j] = 0.0f;
+        for (size_t d = 0; d < D; ++d) {
+          const float* e = &eT[d * Kp + k0];
+          for (size_t r = 0; r < RB; ++r) {
+            const float av = a[r * D + d];
+            for (size_t j = 0; j < KB; ++j) acc[r][j] = std::fmaf(av, e[j], acc[r][j]);
+          }
+        }
+        for (size_t r = 0; r < nr; ++r)
+          for (size_t j = 0; j < KB && k0 + j < K; ++j) {
+            const float dist = std::fmaf(-2.0f, acc[r][j], sqnorm[k0 + j]);
+            if (dist < best[r]) {
+              second[r] = best[r];
+              best[r] = dist;
+              bi[r] = static_cast<int32_t>(k0 + j);
+            } else if (dist < second[r]) {
+              second[r] = dist;
+            }
+          }
+      }
+      for (size_t r = 0; r < nr; ++r) {
+        const size_t n = n0 + r;
+        if (best_out) best_out[n] = bi[r];
+        if (rel_gap) {
+          const double full = a2[r] + static_cast<double>(best[r]);
+          const double gap = static_cast<double>(second[r]) - static_cast<double>(best[r]);
+          rel_gap[n] = static_cast<float>(gap / std::max(full, 1e-30));
+        }
+        const int32_t code = codes_in ? codes_in[n] : bi[r];
+        if (code < 0 || static_cast<size_t>(code) >= K) continue;
+        for (size_t d = 0; d < D; ++d) resid[n * D + d] -= bf16_to(cb[static_cast<size_t>(code) * D + d]);
+      }
+    }
+  }
+}
+
+// vq_forward_semantics.md:69,82 — recon = sum over levels of the chosen codewords (f32, level order)
+void orc_rvq_decode(const int32_t* codes, const uint16_t* cbs, size_t L, float* recon, size_t N, size_t D, size_t K) {
+  for (size_t n = 0; n < N; ++n)
+    for (size_t d = 0; d < D; ++d) {
+      float acc = 0.0f;
+      for (size_t l = 0; l < L; ++l) {
+        const int32_t c = codes[l * N + n];
+        acc += bf16_to(cbs[(l * K + static_cast<size_t>(c)) * D + d]);
+      }
+      recon[n * D + d] = acc;
+    }
+}
+
+// vq_forward_semantics.md:67,80: F.interpolate(mode="area") with an integer
+// factor = mean of f consecutive rows, summed in increasing order.
+void orc_pool_avg(const float* x, float* y, size_t B, size_t T, size_t D, size_t f) {
+  const size_t To = T / f;
+  for (size_t b = 0; b < B; ++b)
+    for (size_t j = 0; j < To; ++j)
+      for (size_t d = 0; d < D; ++d) {
+        const float* src = x + (b * T + j * f) * D + d;
+        float s = src[0];
+        for (size_t i = 1; i < f; ++i) s += src[i * D];
+        y[(b * To + j) * D + d] = s / static_cast<float>(f);
+      }
+}
+
+// Multiscale step: q = sum_l e_l[code] (f32, level order) per pooled row,
+// nearest-repeat upsampled; r -= q, recon += q.
+void orc_scale_update(const int32_t* codes, const uint16_t* cbs, size_t L, float* resid, float* recon, size_t B,
+                      size_t T, size_t D, size_t K, size_t f) {
+  const size_t P = B * (T / f);
+  std::vector<float> q(D);
+  for (size_t p = 0; p < P; ++p) {
+    for (size_t d = 0; d < D; ++d) {
+      float acc = 0.0f;
+      for (size_t l = 0; l < L; ++l) acc += bf16_to(cbs[(l * K + static_cast<size_t>(codes[l * P + p])) * D + d]);
+      q[d] = acc;
+    }
+    for (size_t i = 0; i < f; ++i) {
+      const size_t row = p * f + i;
+      for (size_t d = 0; d < D; ++d) {
+        resid[row * D + d] -= q[d];
+        recon[row * D + d] += q[d];
+      }
+    }
+  }
+}
+
+}  // extern "C"
