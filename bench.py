@@ -1,0 +1,330 @@
+#!/usr/bin/env python
+"""Benchmark of the RVQ encode hot path.
+
+Workload: N = 2^20 vectors of D = 1024 (bf16, N(0,1), seeded synthetic data),
+8 residual levels with K = 16384 codewords each (level l ~ N(0, 0.6^l)),
+codebooks replicated, token rows sharded across the ranks (the fixed-size
+config-5 problem: strong scaling), codes and reconstructions all-gathered
+over NCCL after the encode. One step = one encode of the whole problem.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU runs are launched by torchrun, one rank per GPU. Rank 0 prints ONE
+JSON line. `--impl reference` times the CPU restatement of the path (the
+reference has no runnable implementation here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "rvq_encode_vectors_per_s"
+UNIT = "vectors/s"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--rows", type=int, default=1 << 20)
+    p.add_argument("--dim", type=int, default=1024)
+    p.add_argument("--levels", type=int, default=8)
+    p.add_argument("--codes", type=int, default=16384)
+    p.add_argument("--cpu-rows", type=int, default=2048, help="rows per CPU-baseline sample")
+    p.add_argument("--seed", type=int, default=20260)
+    return p.parse_args()
+
+
+def config_dict(a, world):
+    return {
+        "workload": "rvq_encode (BASELINE config 5)",
+        "rows": a.rows,
+        "dim": a.dim,
+        "levels": a.levels,
+        "codebook_size": a.codes,
+        "rows_per_gpu": a.rows // world,
+        "parallelism": f"row-sharded x{world}, codebooks replicated",
+        "collective": "NCCL all_gather of codes and bf16 reconstructions" if world > 1 else "none (1 GPU)",
+        "l2": "inputs exceed L2 (bf16 rows 2 GiB/N, f32 residual 4 GiB/N); codebooks (32 MiB/level) stay L2-resident by design",
+        "data": "synthetic seeded N(0,1) rows, N(0,0.6^l) codebooks",
+    }
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = str(gpu_index)
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        mhz, maxmhz, reasons = [], [], set()
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9 or parts[0] != self.gpu:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxmhz.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxmhz), "samples": len(mhz),
+                "reasons": sorted(reasons)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(rows_per_launch: int):
+    """DRAM bytes per rvq_argmin launch from the committed ncu summary, scaled
+    from the captured case to this launch by rows (traffic ~ rows * D * 2
+    plus one codebook read)."""
+    p = ROOT / "profiles" / "rvq_argmin_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    per_row = (d["dram_bytes_per_launch"] - d["codebook_bytes"]) / d["rows"]
+    return per_row * rows_per_launch + d["codebook_bytes"]
+
+
+# ------------------------------------------------------------ CPU leg
+def cpu_encode_sample(a, rows: int, threads: int):
+    """Times the oracle (the CPU restatement of the path) on `rows` rows of the
+    same workload. Returns (seconds, rows)."""
+    from oracle import pyoracle as orc
+    rng = np.random.default_rng(a.seed + 99)
+    x = orc.bf16_bits(rng.standard_normal((rows, a.dim)).astype(np.float32))
+    cbs = np.stack([orc.bf16_bits((rng.standard_normal((a.codes, a.dim)) * 0.6 ** l).astype(np.float32))
+                    for l in range(a.levels)])
+    t0 = time.perf_counter()
+    orc.rvq_encode(x, cbs, threads=threads)
+    return time.perf_counter() - t0, rows
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    for _ in range(a.warmup):
+        cpu_encode_sample(a, a.cpu_rows, threads)
+    times = []
+    for _ in range(a.steps):
+        s, n = cpu_encode_sample(a, a.cpu_rows, threads)
+        times.append(s)
+    sec = sum(times) / len(times)
+    value = a.cpu_rows / sec
+    sample = (f"{a.cpu_rows} rows x {a.levels} levels x K={a.codes} x D={a.dim} per step "
+              f"(oracle port, includes its per-level codebook transpose)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 operands, f32 accumulation", "data": "synthetic",
+        "config": config_dict(a, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------ GPU leg
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    from ncmorph_b200 import _lib, device as ndev, vq
+    import ctypes
+
+    if a.rows % world:
+        raise SystemExit("rows must divide evenly across ranks")
+    n = a.rows // world
+    L, K, D = a.levels, a.codes, a.dim
+    g = torch.Generator(device=dev).manual_seed(a.seed + 1000 * rank)
+    x = torch.randn((n, D), generator=g, device=dev).to(torch.bfloat16)
+    gc = torch.Generator(device=dev).manual_seed(a.seed)  # same codebooks on every rank
+    decay = torch.tensor([0.6 ** l for l in range(L)], device=dev).view(L, 1, 1)
+    cbs = (torch.randn((L, K, D), generator=gc, device=dev) * decay).to(torch.bfloat16)
+    sq = vq.code_sqnorm(cbs)
+    codes = torch.empty((L, n), dtype=torch.int32, device=dev)
+    recon = torch.empty((n, D), dtype=torch.bfloat16, device=dev)
+    codes_all = torch.empty((world, L, n), dtype=torch.int32, device=dev) if world > 1 else None
+    recon_all = torch.empty((a.rows, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    ctx = ndev.context(dev)
+    lib = _lib.load()
+
+    def step():
+        vq.rvq_encode(x, cbs, sq, codes=codes, recon=recon)
+        if world > 1:
+            dist.all_gather_into_tensor(codes_all, codes)
+            dist.all_gather_into_tensor(recon_all, recon)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    for _ in range(a.warmup):
+        step()
+    ndev.sync(dev)
+
+    # ---- value: device-resident inputs; per-kernel events for the roofline
+    lib.ncm_profile_read(ctx, b"*", None, None)
+    lib.ncm_profile_enable(ctx, 1)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = timed(step, a.steps)
+    clocks = sampler.stop() if sampler else None
+    lib.ncm_profile_enable(ctx, 0)
+    tot = ctypes.c_double()
+    cnt = ctypes.c_int64()
+    _lib.check(lib.ncm_profile_read(ctx, b"rvq_argmin", ctypes.byref(tot), ctypes.byref(cnt)))
+    argmin_ms, argmin_launches = tot.value, cnt.value
+    other_ms = ctypes.c_double()
+    other_cnt = ctypes.c_int64()
+    _lib.check(lib.ncm_profile_read(ctx, b"*", ctypes.byref(other_ms), ctypes.byref(other_cnt)))
+    launches = argmin_launches + other_cnt.value
+    ndev.sync(dev)
+    argmin_avg_ms = max_over_ranks(argmin_ms / max(argmin_launches, 1))
+    kernel_share = argmin_ms / max(argmin_ms + other_ms.value, 1e-9)
+
+    # ---- e2e: host rows in, gathered codes out, through the same C-ABI calls
+    x_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(x.cpu())
+    gathered = codes_all if world > 1 else codes
+    codes_host = torch.empty(gathered.shape, dtype=torch.int32).pin_memory()
+
+    def step_e2e():
+        x.copy_(x_host, non_blocking=True)
+        step()
+        codes_host.copy_(gathered, non_blocking=True)
+
+    step_e2e()
+    torch.cuda.synchronize()
+    ms_e2e = timed(step_e2e, a.steps)
+    ndev.sync(dev)
+
+    value = a.rows / (ms * 1e-3)
+    e2e_value = a.rows / (ms_e2e * 1e-3)
+    peaks, peak_kind = measured_peaks()
+    flops_per_launch = 2.0 * n * K * D
+    achieved = flops_per_launch / (argmin_avg_ms * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    traffic = ncu_traffic(n)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        threads = os.cpu_count() or 1
+        sec, rows = cpu_encode_sample(a, a.cpu_rows, threads)
+        cpu = {"value": rows / sec, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{rows} rows x {L} levels x K={K} x D={D} through the oracle port"}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 operands, f32 accumulation", "data": "synthetic", "config": config_dict(a, world),
+        "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": ms_e2e, "h2d_bytes_per_step": n * D * 2,
+                "d2h_bytes_per_step": int(gathered.numel() * 4)},
+        "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
+                     "frac_of_burst": achieved / float(peaks["bf16_tflops"]),
+                     "flops_per_launch": flops_per_launch, "avg_launch_ms": argmin_avg_ms,
+                     "launches": argmin_launches, "share_of_kernel_time": kernel_share,
+                     "traffic": traffic},
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

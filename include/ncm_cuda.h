@@ -155,6 +155,18 @@ NCM_API int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                           const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
                           uint16_t* y, ncm_stream_t stream);
 
+/* ------------------------------------------------------- measurement */
+
+/* Benchmark instrumentation (no reference counterpart: ncmorph has no timing
+ * code). Launch counts per kernel family are always kept; while profiling is
+ * enabled, CUDA events are also recorded on the launch stream around every
+ * launch. ncm_profile_read synchronises, returns the summed device time (ms)
+ * and launch count of one family since the last read, and resets them.
+ * Families: "rvq_argmin", "rvq_apply", "linear_bf16", "rvq_decode",
+ * "code_sqnorm", "pool_avg", "scale_update", "cast"; "*" = all of them. */
+NCM_API int ncm_profile_enable(ncm_ctx_t* ctx, int on);
+NCM_API int ncm_profile_read(ncm_ctx_t* ctx, const char* kernel, double* total_ms, int64_t* launches);
+
 #ifdef __cplusplus
 }
 #endif

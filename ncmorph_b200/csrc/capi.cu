@@ -58,6 +58,31 @@ int ncm_fail(int status, const char* fmt, ...) {
 
 namespace ncm {
 
+const char* const kKernelNames[KID_COUNT] = {"rvq_argmin", "rvq_apply", "linear_bf16", "rvq_decode",
+                                             "code_sqnorm", "pool_avg",   "scale_update", "cast"};
+
+Launch::Launch(ncm_ctx* ctx, KernelId id, cudaStream_t stream) : ctx_(ctx), id_(id), stream_(stream) {
+  ProfState& p = ctx->prof;
+  ++p.launches[id];
+  if (!p.on) return;
+  auto& v = p.events[id];
+  if (p.used[id] == v.size()) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    v.emplace_back(a, b);
+  }
+  cudaEventRecord(v[p.used[id]].first, stream);
+  stop_ = v[p.used[id]].second;
+  ++p.used[id];
+}
+
+Launch::~Launch() {
+  if (stop_ != nullptr) cudaEventRecord(stop_, stream_);
+}
+
 void* ctx_workspace(ncm_ctx* ctx, size_t bytes) {
   if (bytes <= ctx->ws_bytes) return ctx->ws;
   if (ctx->ws != nullptr) {
@@ -100,9 +125,15 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
   if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, D, 256))
     return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
                     (long long)D, (long long)K);
-  NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream));
-  NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, src_bf16, resid, shadow, codebook, ctx->d_err, N, D, K, update,
-                                stream));
+  {
+    Launch _launch(ctx, KID_RVQ_ARGMIN, stream);
+    NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream));
+  }
+  if (plan.splits > 1 || update) {
+    Launch _launch(ctx, KID_RVQ_APPLY, stream);
+    NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, src_bf16, resid, shadow, codebook, ctx->d_err, N, D, K, update,
+                                  stream));
+  }
   return NCM_OK;
 }
 
@@ -187,7 +218,10 @@ int ncm_f32_to_bf16(ncm_ctx_t* ctx, const float* x, uint16_t* y, int64_t n, ncm_
   if (rc) return rc;
   if (n < 0 || (n > 0 && (x == nullptr || y == nullptr))) return ncm_fail(NCM_EINVAL, "f32_to_bf16: bad arguments");
   if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "f32_to_bf16: buffers must be 16-byte aligned");
-  NCM_CUDA_TRY(launch_f32_to_bf16(x, y, n, static_cast<cudaStream_t>(stream)));
+  {
+    Launch _launch(ctx, KID_CAST, static_cast<cudaStream_t>(stream));
+    NCM_CUDA_TRY(launch_f32_to_bf16(x, y, n, static_cast<cudaStream_t>(stream)));
+  }
   return NCM_OK;
 }
 
@@ -196,7 +230,10 @@ int ncm_bf16_to_f32(ncm_ctx_t* ctx, const uint16_t* x, float* y, int64_t n, ncm_
   if (rc) return rc;
   if (n < 0 || (n > 0 && (x == nullptr || y == nullptr))) return ncm_fail(NCM_EINVAL, "bf16_to_f32: bad arguments");
   if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "bf16_to_f32: buffers must be 16-byte aligned");
-  NCM_CUDA_TRY(launch_bf16_to_f32(x, y, n, static_cast<cudaStream_t>(stream)));
+  {
+    Launch _launch(ctx, KID_CAST, static_cast<cudaStream_t>(stream));
+    NCM_CUDA_TRY(launch_bf16_to_f32(x, y, n, static_cast<cudaStream_t>(stream)));
+  }
   return NCM_OK;
 }
 
@@ -255,18 +292,30 @@ static int linear_host_common(ncm_ctx* ctx, const float* x, const float* w, cons
     NCM_CUDA_TRY(cudaMemcpy2DAsync(wf, sizeof(float) * Kp, w, sizeof(float) * K, sizeof(float) * K, N,
                                    cudaMemcpyHostToDevice, st));
   }
-  NCM_CUDA_TRY(launch_f32_to_bf16(xf, xb, M * Kp, st));
-  NCM_CUDA_TRY(launch_f32_to_bf16(wf, wb, N * Kp, st));
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(xf, xb, M * Kp, st));
+  }
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(wf, wb, N * Kp, st));
+  }
   const uint16_t* bias_dev = nullptr;
   if (bias != nullptr) {
     NCM_CUDA_TRY(cudaMemcpyAsync(bf, bias, sizeof(float) * N, cudaMemcpyHostToDevice, st));
-    NCM_CUDA_TRY(launch_f32_to_bf16(bf, bb, N, st));
+    {
+      Launch _launch(ctx, KID_CAST, st);
+      NCM_CUDA_TRY(launch_f32_to_bf16(bf, bb, N, st));
+    }
     bias_dev = bb;
   }
   if (round_output) {
     rc = linear_bf16(ctx, xb, wb, bias_dev, yb, nullptr, M, Kp, N, st);
     if (rc) return rc;
-    NCM_CUDA_TRY(launch_bf16_to_f32(yb, yf, M * N, st));
+    {
+      Launch _launch(ctx, KID_CAST, st);
+      NCM_CUDA_TRY(launch_bf16_to_f32(yb, yf, M * N, st));
+    }
   } else {
     rc = linear_bf16(ctx, xb, wb, bias_dev, nullptr, yf, M, Kp, N, st);
     if (rc) return rc;
@@ -291,7 +340,10 @@ int ncm_code_sqnorm(ncm_ctx_t* ctx, const uint16_t* codebook, float* sqnorm, int
   if (K <= 0 || D <= 0 || D % 8 != 0 || !codebook || !sqnorm)
     return ncm_fail(NCM_EINVAL, "code_sqnorm: bad arguments (K=%lld D=%lld)", (long long)K, (long long)D);
   if (!aligned16(codebook)) return ncm_fail(NCM_EINVAL, "code_sqnorm: codebook must be 16-byte aligned");
-  NCM_CUDA_TRY(launch_code_sqnorm(codebook, sqnorm, K, D, static_cast<cudaStream_t>(stream)));
+  {
+    Launch _launch(ctx, KID_SQNORM, static_cast<cudaStream_t>(stream));
+    NCM_CUDA_TRY(launch_code_sqnorm(codebook, sqnorm, K, D, static_cast<cudaStream_t>(stream)));
+  }
   return NCM_OK;
 }
 
@@ -321,10 +373,16 @@ int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, con
   uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
   if (sqnorm == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
-    NCM_CUDA_TRY(launch_code_sqnorm(codebook, sq, K, D, st));
+    {
+      Launch _launch(ctx, KID_SQNORM, st);
+      NCM_CUDA_TRY(launch_code_sqnorm(codebook, sq, K, D, st));
+    }
     sqnorm = sq;
   }
-  NCM_CUDA_TRY(launch_f32_to_bf16(residual, shadow, N * D, st));
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(residual, shadow, N * D, st));
+  }
   return rvq_level_core(ctx, shadow, nullptr, residual, nullptr, codebook, sqnorm, codes,
                         reinterpret_cast<RvqPartial*>(ws + o_part), plan, N, D, K, true, st);
 }
@@ -354,7 +412,10 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
   RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
   if (sqnorms == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
-    NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, K * L, D, st));
+    {
+      Launch _launch(ctx, KID_SQNORM, st);
+      NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, K * L, D, st));
+    }
     sqnorms = sq;
   }
   for (int l = 0; l < L; ++l) {
@@ -366,7 +427,10 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
                         codes + static_cast<size_t>(l) * N, part, plan, N, D, K, update, st);
     if (rc) return rc;
   }
-  if (recon != nullptr) NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+  if (recon != nullptr) {
+    Launch _launch(ctx, KID_DECODE, st);
+    NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+  }
   return NCM_OK;
 }
 
@@ -378,7 +442,10 @@ int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, int64_t T,
     return ncm_fail(NCM_EINVAL, "pool_avg: bad arguments (B=%lld T=%lld D=%lld factor=%d)", (long long)B,
                     (long long)T, (long long)D, factor);
   if (!aligned16(x) || !aligned16(y)) return ncm_fail(NCM_EINVAL, "pool_avg: buffers must be 16-byte aligned");
-  NCM_CUDA_TRY(launch_pool_avg(x, y, nullptr, B, T, D, factor, static_cast<cudaStream_t>(stream)));
+  {
+    Launch _launch(ctx, KID_POOL, static_cast<cudaStream_t>(stream));
+    NCM_CUDA_TRY(launch_pool_avg(x, y, nullptr, B, T, D, factor, static_cast<cudaStream_t>(stream)));
+  }
   return NCM_OK;
 }
 
@@ -390,8 +457,11 @@ int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codeboo
   if (L <= 0 || !codes || !codebooks || !recon) return ncm_fail(NCM_EINVAL, "rvq_decode: bad arguments");
   if (!aligned16(codes) || !aligned16(codebooks) || !aligned16(recon))
     return ncm_fail(NCM_EINVAL, "rvq_decode: buffers must be 16-byte aligned");
-  NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err,
+  {
+    Launch _launch(ctx, KID_DECODE, static_cast<cudaStream_t>(stream));
+    NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err,
                                  static_cast<cudaStream_t>(stream)));
+  }
   return NCM_OK;
 }
 
@@ -444,32 +514,82 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
   RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
   if (sqnorms == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
-    NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, static_cast<int64_t>(S) * L * K, D, st));
+    {
+      Launch _launch(ctx, KID_SQNORM, st);
+      NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, static_cast<int64_t>(S) * L * K, D, st));
+    }
     sqnorms = sq;
   }
   // input projection, then the f32 residual
   rc = linear_bf16(ctx, x, w_in, b_in, h, nullptr, N, Din, D, st);
   if (rc) return rc;
-  NCM_CUDA_TRY(launch_bf16_to_f32(h, r, N * D, st));
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_bf16_to_f32(h, r, N * D, st));
+  }
   NCM_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(float) * N * D, st));
   int32_t* codes_s = codes;
   for (int s = 0; s < S; ++s) {
     const int f = cfg->pool_factors[s];
     const int64_t rows = N / f;
     const RvqPlan plan = rvq_plan(ctx->num_sms, rows, K);
-    NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, f, st));
+    {
+      Launch _launch(ctx, KID_POOL, st);
+      NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, f, st));
+    }
     for (int l = 0; l < L; ++l) {
       const size_t cb_off = (static_cast<size_t>(s) * L + l) * K;
       rc = rvq_level_core(ctx, ub, nullptr, u, l == L - 1 ? nullptr : ub, codebooks + cb_off * D, sqnorms + cb_off,
                           codes_s + static_cast<size_t>(l) * rows, part, plan, rows, D, K, l != L - 1, st);
       if (rc) return rc;
     }
-    NCM_CUDA_TRY(launch_scale_update(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, acc, B, T, D, K,
+    {
+      Launch _launch(ctx, KID_SCALE_UPDATE, st);
+      NCM_CUDA_TRY(launch_scale_update(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, acc, B, T, D, K,
                                      f, ctx->d_err, st));
+    }
     codes_s += static_cast<size_t>(L) * rows;
   }
-  NCM_CUDA_TRY(launch_f32_to_bf16(acc, rb, N * D, st));
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(acc, rb, N * D, st));
+  }
   return linear_bf16(ctx, rb, w_out, b_out, y, nullptr, N, D, Din, st);
+}
+
+int ncm_profile_enable(ncm_ctx_t* ctx, int on) {
+  if (ctx == nullptr) return ncm_fail(NCM_EINVAL, "null context");
+  ctx->prof.on = on != 0;
+  return NCM_OK;
+}
+
+int ncm_profile_read(ncm_ctx_t* ctx, const char* kernel, double* total_ms, int64_t* launches) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (kernel == nullptr) return ncm_fail(NCM_EINVAL, "profile_read: null kernel name");
+  const bool all = std::strcmp(kernel, "*") == 0;
+  int which = -1;
+  for (int i = 0; i < KID_COUNT; ++i)
+    if (std::strcmp(kernel, kKernelNames[i]) == 0) which = i;
+  if (!all && which < 0) return ncm_fail(NCM_EINVAL, "profile_read: unknown kernel family '%s'", kernel);
+  double ms = 0.0;
+  long long n = 0;
+  for (int i = 0; i < KID_COUNT; ++i) {
+    if (!all && i != which) continue;
+    ProfState& p = ctx->prof;
+    for (size_t j = 0; j < p.used[i]; ++j) {
+      NCM_CUDA_TRY(cudaEventSynchronize(p.events[i][j].second));
+      float e = 0.f;
+      NCM_CUDA_TRY(cudaEventElapsedTime(&e, p.events[i][j].first, p.events[i][j].second));
+      ms += e;
+    }
+    n += p.launches[i];
+    p.used[i] = 0;
+    p.launches[i] = 0;
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = n;
+  return NCM_OK;
 }
 
 }  // extern "C"

@@ -341,6 +341,7 @@ int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16
   const int tiles = a.tiles_a * a.tiles_b;
   const int grid = std::min(tiles, ctx->num_sms);
   cudaError_t e;
+  Launch _launch(ctx, KID_LINEAR, stream);
   if (swap) {
     switch (bn) {
       case 16: e = launch_linear<16, true>(tmA, tmB, a, grid, stream); break;

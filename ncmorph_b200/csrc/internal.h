@@ -7,7 +7,33 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+#include <vector>
+
 #include "common.cuh"
+
+namespace ncm {
+// Kernel families counted (always) and timed (when profiling is enabled).
+enum KernelId {
+  KID_RVQ_ARGMIN = 0,
+  KID_RVQ_APPLY,
+  KID_LINEAR,
+  KID_DECODE,
+  KID_SQNORM,
+  KID_POOL,
+  KID_SCALE_UPDATE,
+  KID_CAST,
+  KID_COUNT
+};
+extern const char* const kKernelNames[KID_COUNT];
+
+struct ProfState {
+  bool on = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events[KID_COUNT];
+  size_t used[KID_COUNT] = {};
+  long long launches[KID_COUNT] = {};
+};
+}  // namespace ncm
 
 struct ncm_ctx {
   int device = 0;
@@ -18,9 +44,26 @@ struct ncm_ctx {
   // host staging for the *_host_f32 entry points
   void* h_stage = nullptr;
   size_t h_stage_bytes = 0;
+  ncm::ProfState prof;
 };
 
 namespace ncm {
+
+// Counts one launch of kernel family `id` on `stream` and, while profiling is
+// enabled, brackets it with CUDA events recorded on that stream.
+class Launch {
+ public:
+  Launch(ncm_ctx* ctx, KernelId id, cudaStream_t stream);
+  ~Launch();
+  Launch(const Launch&) = delete;
+  Launch& operator=(const Launch&) = delete;
+
+ private:
+  ncm_ctx* ctx_;
+  KernelId id_;
+  cudaStream_t stream_;
+  cudaEvent_t stop_ = nullptr;
+};
 
 // Carves consecutive 256-byte-aligned regions out of the context workspace.
 struct WsCarver {

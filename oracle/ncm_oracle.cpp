@@ -10,6 +10,9 @@
 #include <limits>
 #include <vector>
 
+#if defined(__AVX2__) || defined(__AVX512F__)
+#include <immintrin.h>
+#endif
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -47,6 +50,46 @@ inline float ftz(float v) {
 }
 
 const float kInf = std::numeric_limits<float>::infinity();
+
+// Lane-wise fused multiply-add for the RVQ distance loop: each lane is one
+// independent fmaf chain, so the vector width changes speed, not results.
+#if defined(__AVX512F__)
+constexpr size_t kVecW = 16;
+struct VecF {
+  __m512 v;
+};
+inline VecF vzero() { return {_mm512_setzero_ps()}; }
+inline VecF vload(const float* p) { return {_mm512_loadu_ps(p)}; }
+inline VecF vfma_bcast(float a, VecF b, VecF c) { return {_mm512_fmadd_ps(_mm512_set1_ps(a), b.v, c.v)}; }
+inline void vstore(float* p, VecF v) { _mm512_storeu_ps(p, v.v); }
+#elif defined(__AVX2__) && defined(__FMA__)
+constexpr size_t kVecW = 8;
+struct VecF {
+  __m256 v;
+};
+inline VecF vzero() { return {_mm256_setzero_ps()}; }
+inline VecF vload(const float* p) { return {_mm256_loadu_ps(p)}; }
+inline VecF vfma_bcast(float a, VecF b, VecF c) { return {_mm256_fmadd_ps(_mm256_set1_ps(a), b.v, c.v)}; }
+inline void vstore(float* p, VecF v) { _mm256_storeu_ps(p, v.v); }
+#else
+constexpr size_t kVecW = 8;
+struct VecF {
+  float v[8];
+};
+inline VecF vzero() { return VecF{}; }
+inline VecF vload(const float* p) {
+  VecF r;
+  for (size_t i = 0; i < 8; ++i) r.v[i] = p[i];
+  return r;
+}
+inline VecF vfma_bcast(float a, VecF b, VecF c) {
+  for (size_t i = 0; i < 8; ++i) c.v[i] = std::fmaf(a, b.v[i], c.v[i]);
+  return c;
+}
+inline void vstore(float* p, VecF v) {
+  for (size_t i = 0; i < 8; ++i) p[i] = v.v[i];
+}
+#endif
 
 // packages/kernels/root.zig:106-142, one output element.
 inline float matmul_bf16_elem(const float* x, const float* w, const float* bias, size_t o, size_t in_w) {
@@ -518,72 +561,107 @@ void orc_code_sqnorm(const uint16_t* cb, float* out, size_t K, size_t D) {
 //   dist_k = fmaf(-2, dot_k, ||e_k||^2), dot_k = sequential fmaf over d of bf16(r)_d * e_kd
 //   best = lowest k with the minimal dist (torch.argmin tie rule)
 //   r -= e[code] (f32), code = codes_in[n] when teacher-forcing, else best.
+// Work is split into (4-row block x code chunk) tasks; each output's dot
+// product is the same sequential chain whatever the split, and chunk results
+// merge in increasing code order, so threads change speed, not bits.
+namespace {
+struct Top2 {
+  float best, second;
+  int32_t idx;
+};
+}  // namespace
+
 void orc_rvq_level(float* resid, const uint16_t* cb, const float* sqnorm, const int32_t* codes_in,
                    int32_t* best_out, float* rel_gap, size_t N, size_t D, size_t K, int threads) {
-  constexpr size_t KB = 16;  // codes per block (independent accumulators)
-  constexpr size_t RB = 4;   // rows per block
-  const size_t Kp = (K + KB - 1) / KB * KB;
-  std::vector<float> eT(D * Kp, 0.0f);  // codebook transposed to [D][Kp]
-  for (size_t k = 0; k < K; ++k)
-    for (size_t d = 0; d < D; ++d) eT[d * Kp + k] = bf16_to(cb[k * D + d]);
-  const long long nblk = static_cast<long long>((N + RB - 1) / RB);
+  constexpr size_t KB = kVecW;  // codes per block (one vector of independent accumulators)
+  constexpr size_t RB = 8;      // rows per block
   if (threads < 1) threads = 1;
-#pragma omp parallel num_threads(threads)
-  {
-    std::vector<float> a(RB * D);
-    std::vector<double> a2(RB);
-#pragma omp for schedule(dynamic, 1)
-    for (long long blk = 0; blk < nblk; ++blk) {
-      const size_t n0 = static_cast<size_t>(blk) * RB;
-      const size_t nr = std::min(RB, N - n0);
-      for (size_t r = 0; r < RB; ++r) {
-        double s = 0.0;
-        for (size_t d = 0; d < D; ++d) {
-          const float v = r < nr ? rb(resid[(n0 + r) * D + d]) : 0.0f;
-          a[r * D + d] = v;
-          s += static_cast<double>(v) * v;
-        }
-        a2[r] = s;
+  const size_t Kp = (K + KB - 1) / KB * KB;
+  std::vector<float> eT(D * Kp);  // codebook transposed to [D][Kp], zero-padded
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (long long d0 = 0; d0 < static_cast<long long>(D); d0 += 16) {
+    const size_t d1 = std::min(static_cast<size_t>(d0) + 16, D);
+    for (size_t k = 0; k < Kp; ++k)
+      for (size_t d = static_cast<size_t>(d0); d < d1; ++d)
+        eT[d * Kp + k] = k < K ? bf16_to(cb[k * D + d]) : 0.0f;
+  }
+  const size_t nblk = (N + RB - 1) / RB;
+  const size_t kblocks = Kp / KB;
+  size_t nchunk = 1;
+  while (nblk * nchunk < static_cast<size_t>(threads) * 4 && nchunk * 2 <= kblocks) nchunk *= 2;
+  const size_t kb_per_chunk = (kblocks + nchunk - 1) / nchunk;
+  std::vector<float> a(nblk * RB * D);  // bf16(r), per block transposed to [d][RB]
+  std::vector<double> a2(nblk * RB, 0.0);
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (long long n = 0; n < static_cast<long long>(nblk * RB); ++n) {
+    const size_t blk = static_cast<size_t>(n) / RB, r = static_cast<size_t>(n) % RB;
+    double s = 0.0;
+    for (size_t d = 0; d < D; ++d) {
+      const float v = static_cast<size_t>(n) < N ? rb(resid[n * D + d]) : 0.0f;
+      a[(blk * D + d) * RB + r] = v;
+      s += static_cast<double>(v) * v;
+    }
+    a2[n] = s;
+  }
+  std::vector<Top2> part(nblk * RB * nchunk);
+  const long long tasks = static_cast<long long>(nblk * nchunk);
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 1)
+  for (long long t = 0; t < tasks; ++t) {
+    const size_t blk = static_cast<size_t>(t) / nchunk;
+    const size_t ch = static_cast<size_t>(t) % nchunk;
+    const size_t n0 = blk * RB;
+    const size_t nr = std::min(RB, N - n0);
+    Top2 tp[RB];
+    for (size_t r = 0; r < RB; ++r) tp[r] = Top2{kInf, kInf, static_cast<int32_t>(ch * kb_per_chunk * KB)};
+    const size_t kb0 = ch * kb_per_chunk, kb1 = std::min(kblocks, kb0 + kb_per_chunk);
+    for (size_t kb = kb0; kb < kb1; ++kb) {
+      const size_t k0 = kb * KB;
+      VecF vacc[RB];
+      for (size_t r = 0; r < RB; ++r) vacc[r] = vzero();
+      const float* ab = &a[blk * D * RB];
+      for (size_t d = 0; d < D; ++d) {
+        const VecF e = vload(&eT[d * Kp + k0]);
+        for (size_t r = 0; r < RB; ++r) vacc[r] = vfma_bcast(ab[d * RB + r], e, vacc[r]);
       }
-      float best[RB], second[RB];
-      int32_t bi[RB];
-      for (size_t r = 0; r < RB; ++r) best[r] = kInf, second[r] = kInf, bi[r] = 0;
-      for (size_t k0 = 0; k0 < Kp; k0 += KB) {
-        float acc[RB][KB];
-        for (size_t r = 0; r < RB; ++r)
-          for (size_t j = 0; j < KB; ++j) acc[r][j] = 0.0f;
-        for (size_t d = 0; d < D; ++d) {
-          const float* e = &eT[d * Kp + k0];
-          for (size_t r = 0; r < RB; ++r) {
-            const float av = a[r * D + d];
-            for (size_t j = 0; j < KB; ++j) acc[r][j] = std::fmaf(av, e[j], acc[r][j]);
+      float acc[RB][KB];
+      for (size_t r = 0; r < RB; ++r) vstore(acc[r], vacc[r]);
+      for (size_t r = 0; r < nr; ++r)
+        for (size_t j = 0; j < KB && k0 + j < K; ++j) {
+          const float dist = std::fmaf(-2.0f, acc[r][j], sqnorm[k0 + j]);
+          if (dist < tp[r].best) {
+            tp[r].second = tp[r].best;
+            tp[r].best = dist;
+            tp[r].idx = static_cast<int32_t>(k0 + j);
+          } else if (dist < tp[r].second) {
+            tp[r].second = dist;
           }
         }
-        for (size_t r = 0; r < nr; ++r)
-          for (size_t j = 0; j < KB && k0 + j < K; ++j) {
-            const float dist = std::fmaf(-2.0f, acc[r][j], sqnorm[k0 + j]);
-            if (dist < best[r]) {
-              second[r] = best[r];
-              best[r] = dist;
-              bi[r] = static_cast<int32_t>(k0 + j);
-            } else if (dist < second[r]) {
-              second[r] = dist;
-            }
-          }
-      }
-      for (size_t r = 0; r < nr; ++r) {
-        const size_t n = n0 + r;
-        if (best_out) best_out[n] = bi[r];
-        if (rel_gap) {
-          const double full = a2[r] + static_cast<double>(best[r]);
-          const double gap = static_cast<double>(second[r]) - static_cast<double>(best[r]);
-          rel_gap[n] = static_cast<float>(gap / std::max(full, 1e-30));
-        }
-        const int32_t code = codes_in ? codes_in[n] : bi[r];
-        if (code < 0 || static_cast<size_t>(code) >= K) continue;
-        for (size_t d = 0; d < D; ++d) resid[n * D + d] -= bf16_to(cb[static_cast<size_t>(code) * D + d]);
+    }
+    for (size_t r = 0; r < RB; ++r) part[(n0 + r) * nchunk + ch] = tp[r];
+  }
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (long long nn = 0; nn < static_cast<long long>(N); ++nn) {
+    const size_t n = static_cast<size_t>(nn);
+    Top2 m = part[n * nchunk];
+    for (size_t ch = 1; ch < nchunk; ++ch) {
+      const Top2& c = part[n * nchunk + ch];
+      if (c.best < m.best) {  // strict: on equal distances the lower code (earlier chunk) stays
+        m.second = std::min(m.best, c.second);
+        m.best = c.best;
+        m.idx = c.idx;
+      } else {
+        m.second = std::min(m.second, c.best);
       }
     }
+    if (best_out) best_out[n] = m.idx;
+    if (rel_gap) {
+      const double full = a2[n] + static_cast<double>(m.best);
+      const double gap = static_cast<double>(m.second) - static_cast<double>(m.best);
+      rel_gap[n] = static_cast<float>(gap / std::max(full, 1e-30));
+    }
+    const int32_t code = codes_in ? codes_in[n] : m.idx;
+    if (code < 0 || static_cast<size_t>(code) >= K) continue;
+    for (size_t d = 0; d < D; ++d) resid[n * D + d] -= bf16_to(cb[static_cast<size_t>(code) * D + d]);
   }
 }
 

@@ -30,11 +30,29 @@ class AttnWeights(ctypes.Structure):
                                                "o_w", "o_b")]
 
 
+def _cpu_signature() -> str:
+    """Model name + ISA flags of this host: the library is built with
+    -march=native, so a copy built on another CPU is rebuilt before use."""
+    try:
+        text = pathlib.Path("/proc/cpuinfo").read_text()
+    except OSError:
+        return "unknown"
+    model = next((l for l in text.splitlines() if l.startswith("model name")), "")
+    flags = next((l for l in text.splitlines() if l.startswith("flags")), "")
+    return f"{model}|{flags}"
+
+
 def build() -> pathlib.Path:
-    """Builds the oracle library with make if it is missing or stale."""
-    src = [HERE / "ncm_oracle.cpp", HERE / "ncm_oracle.h"]
-    if not LIB.exists() or LIB.stat().st_mtime < max(s.stat().st_mtime for s in src):
-        subprocess.run(["make", "-s", "-C", os.fspath(HERE)], check=True)
+    """Builds the oracle library with make if it is missing, stale, or was
+    built on a different CPU."""
+    src = [HERE / "ncm_oracle.cpp", HERE / "ncm_oracle.h", HERE / "Makefile"]
+    stamp = HERE / "build" / "cpu.stamp"
+    sig = _cpu_signature()
+    stale = not LIB.exists() or LIB.stat().st_mtime < max(s.stat().st_mtime for s in src)
+    foreign = not stamp.exists() or stamp.read_text() != sig
+    if stale or foreign:
+        subprocess.run(["make", "-s", "-B", "-C", os.fspath(HERE)], check=True)
+        stamp.write_text(sig)
     return LIB
 
 

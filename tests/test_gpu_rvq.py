@@ -1,0 +1,114 @@
+"""GPU parity of the RVQ path (R1-R6) against the CPU oracle, through the C ABI.
+
+Codes are checked level by level with teacher forcing: the oracle advances
+its residual with the GPU's codes, so both sides see bit-identical inputs at
+every level and any code difference is a genuine argmin difference (allowed
+only at near-ties, which are counted).
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import check_codes, from_dev_bf16, gen_bf16, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _cbs(rng, L, K, D, decay):
+    return np.stack([gen_bf16(rng, (K, D), decay ** l) for l in range(L)])
+
+
+def test_code_sqnorm_bit_exact(orc, cuda_dev):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(0)
+    cb = gen_bf16(rng, (3, 1000, 136))
+    got = vq.code_sqnorm(to_dev_bf16(cb, cuda_dev)).cpu().numpy()
+    assert np.array_equal(got, orc.code_sqnorm(cb))
+
+
+@pytest.mark.parametrize("N,D,K", [
+    (4096, 256, 1024),   # config 1 shape, one level
+    (1000, 136, 700),    # ragged rows, D not a multiple of 64, K not a multiple of 256
+    (300, 64, 5000),     # few rows, many codes: code-split path
+    (1, 8, 1),           # smallest legal problem
+    (129, 1024, 257),    # one row past a 128-row block, one code past a 256-code tile
+])
+def test_rvq_level_matches_oracle(orc, cuda_dev, N, D, K):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(N + D + K)
+    r = rng.standard_normal((N, D)).astype(np.float32)
+    cb = gen_bf16(rng, (K, D))
+    sq = orc.code_sqnorm(cb)
+    rd = torch.from_numpy(r).to(cuda_dev)
+    codes = vq.rvq_level(rd, to_dev_bf16(cb, cuda_dev), torch.from_numpy(sq).to(cuda_dev)).cpu().numpy()
+    r_orc = r.copy()
+    best, gap = orc.rvq_level(r_orc, cb, sq, codes_in=codes)
+    check_codes(codes, best, gap, f"level N={N} D={D} K={K}")
+    assert np.array_equal(rd.cpu().numpy(), r_orc)  # f32 residual update, bit for bit
+
+
+def test_rvq_level_ties_pick_lowest_index(cuda_dev, orc):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(5)
+    D = 64
+    base = gen_bf16(rng, (300, D))
+    cb = np.concatenate([base, base[[7]], base[[299]]])   # 300 == 7 and 301 == 299, across code tiles
+    r = orc.bf16_widen(cb[[7, 299, 7]]).astype(np.float32).copy()
+    codes = vq.rvq_level(torch.from_numpy(r).to(cuda_dev), to_dev_bf16(cb, cuda_dev)).cpu().numpy()
+    assert codes.tolist() == [7, 299, 7]
+
+
+def test_config1_encode_decode(orc, cuda_dev):
+    """N=4096, D=256, 4 levels of K=1024, level l ~ N(0, 0.5^l)."""
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(20260)
+    N, D, K, L = 4096, 256, 1024, 4
+    x = gen_bf16(rng, (N, D))
+    cbs = _cbs(rng, L, K, D, 0.5)
+    codes_d, recon_d, resid_d = vq.rvq_encode(to_dev_bf16(x, cuda_dev), to_dev_bf16(cbs, cuda_dev),
+                                              want_residual=True)
+    codes = codes_d.cpu().numpy()
+    best, gaps, resid, recon = orc.rvq_encode(x, cbs, codes_in=codes)
+    stats = [check_codes(codes[l], best[l], gaps[l], f"level {l}") for l in range(L)]
+    flips = sum(s["flips"] for s in stats)
+    print(f"config1 flips={flips} near_ties={sum(s['near_ties'] for s in stats)} of {N * L}")
+    assert np.array_equal(resid_d.cpu().numpy(), resid)
+    assert np.array_equal(from_dev_bf16(recon_d), orc.bf16_bits(recon))
+    # decode entry point reproduces the encode's reconstruction
+    assert torch.equal(vq.rvq_decode(codes_d, to_dev_bf16(cbs, cuda_dev)).view(torch.int16),
+                       recon_d.view(torch.int16))
+    # free-running oracle agrees on every row without a near-tie at any level
+    fb, fg, _, frecon = orc.rvq_encode(x, cbs)
+    clean = (fg >= 1e-3).all(axis=0)
+    assert np.array_equal(codes[:, clean], fb[:, clean])
+    assert clean.mean() > 0.5
+
+
+def test_decode_rejects_out_of_range_codes(cuda_dev):
+    from ncmorph_b200 import _lib, device, vq
+    cbs = torch.zeros((2, 16, 8), dtype=torch.bfloat16, device=cuda_dev)
+    codes = torch.zeros((2, 4), dtype=torch.int32, device=cuda_dev)
+    codes[1, 2] = 16
+    vq.rvq_decode(codes, cbs)
+    with pytest.raises(_lib.NcmError) as ei:
+        device.sync(cuda_dev)
+    assert ei.value.status == _lib.NCM_ERANGE
+    device.sync(cuda_dev)  # the error word was cleared; the context stays usable
+
+
+@pytest.mark.parametrize("B,T,D,f", [(2, 64, 24, 16), (3, 32, 1024, 2), (1, 8, 8, 1), (8, 2048, 64, 4)])
+def test_pool_bit_exact(orc, cuda_dev, B, T, D, f):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(B * T + D)
+    x = rng.standard_normal((B, T, D)).astype(np.float32)
+    y = vq.pool_avg(torch.from_numpy(x).to(cuda_dev), f).cpu().numpy()
+    assert np.array_equal(y.view(np.uint32), orc.pool_avg(x, f).view(np.uint32))
+
+
+def test_argument_validation(cuda_dev):
+    from ncmorph_b200 import _lib, vq
+    r = torch.zeros((4, 12), device=cuda_dev)            # D=12 is not a multiple of 8
+    cb = torch.zeros((3, 12), dtype=torch.bfloat16, device=cuda_dev)
+    with pytest.raises(_lib.NcmError) as ei:
+        vq.rvq_level(r, cb)
+    assert ei.value.status == _lib.NCM_EINVAL

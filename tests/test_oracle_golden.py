@@ -1,0 +1,211 @@
+"""Pins the CPU oracle to ncmorph's own golden vectors and known-answer tests.
+
+Every constant below is taken from the reference's tests (cited per test);
+the oracle must reproduce each one bit-exactly before it is trusted as the
+parity checker for the GPU kernels.
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+
+def _pairs():
+    rows = [l.split() for l in (GOLDEN / "bf16_pairs.txt").read_text().splitlines() if not l.startswith("#")]
+    a = np.array([int(r[0], 16) for r in rows], dtype=np.uint32)
+    b = np.array([int(r[1], 16) for r in rows], dtype=np.uint16)
+    return a, b
+
+
+def test_bf16_matches_every_pytorch_vector(orc):
+    # packages/bf16/root.zig:43-48 over packages/bf16/vectors.zig
+    a, b = _pairs()
+    assert a.size == 4119
+    got = orc.bf16_bits(a.view(np.float32))
+    bad = np.nonzero(got != b)[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first f32 bits {a[bad[0]]:08X}"
+
+
+def test_bf16_round_trips_every_pattern(orc):
+    # packages/bf16/root.zig:50-59
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    back = orc.bf16_bits(orc.bf16_widen(bits))
+    is_nan = (bits & 0x7FFF) > 0x7F80
+    expected = np.where(is_nan, np.uint16(0x7FC0), bits)
+    assert np.array_equal(back, expected)
+
+
+def _digest_inputs():
+    T, K, N = 4, 1536, 576
+    t = np.arange(T)[:, None]
+    k = np.arange(K)[None, :]
+    x = (((t * 29 + k * 37) % 251) - 125).astype(np.float32) / np.float32(128.0)
+    n = np.arange(N)[:, None]
+    w = (((n * 17 + k * 11) % 257) - 128).astype(np.float32) / np.float32(128.0)
+    return x, w
+
+
+def fnv1a_bf16(values: np.ndarray) -> int:
+    digest = 14695981039346656037
+    for v in values.astype(np.float32).ravel().view(np.uint32):
+        digest = ((digest ^ int(v >> 16)) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return digest
+
+
+def test_bf16_linear_digest(orc):
+    # packages/kernels/root.zig:707-744 (M=4, K=1536 -> 1024+512 blocks, N=576)
+    x, w = _digest_inputs()
+    out = orc.matmul_bf16(x, w)
+    assert fnv1a_bf16(out) == 0x547F69F667C8103F
+    flat = out.ravel()
+    assert flat[0] == np.float32(-0.466796875)
+    assert flat[1] == np.float32(1.109375)
+    assert flat[1793] == np.float32(-0.796875)
+
+
+def test_bf16_linear_digest_threaded_same_bits(orc):
+    x, w = _digest_inputs()
+    assert np.array_equal(orc.matmul_bf16(x, w, threads=4).view(np.uint32), orc.matmul_bf16(x, w).view(np.uint32))
+
+
+def test_bf16_linear_flushes_subnormal_products(orc):
+    # packages/kernels/root.zig:746-755
+    v = np.float32(5.421010862427522e-20)
+    out = orc.matmul_bf16(np.array([[v, v]], np.float32), np.array([[v, v]], np.float32))
+    assert out[0, 0] == 0.0
+
+
+def test_bf16_linear_combines_512_wide_k_blocks(orc):
+    # packages/kernels/root.zig:757-770
+    x = np.full((1, 576), 5.960464477539063e-8, np.float32)
+    x[0, 0] = 1.0
+    x[0, -1] = 0.00390625
+    w = np.ones((1, 576), np.float32)
+    assert orc.matmul_bf16(x, w)[0, 0] == np.float32(1.0078125)
+
+
+def test_matmul_hand_computed(orc):
+    # packages/kernels/root.zig:676-688
+    x = np.array([[5, 6], [7, 8]], np.float32)
+    w = np.array([[1, 2], [3, 4]], np.float32)
+    assert np.array_equal(orc.matmul(x, w).ravel(), np.array([17, 39, 23, 53], np.float32))
+
+
+@pytest.mark.parametrize("T,K,N", [(1, 35, 4), (3, 7, 5), (2, 1, 3), (33, 35, 34)])
+def test_matmul_blocked_equals_reference_and_d53(orc, T, K, N):
+    # packages/kernels/root.zig:690-705, check_random_case :836-872
+    rng = np.random.default_rng(0xB12026 + T * 1000 + K)
+    x = (rng.random((T, K), dtype=np.float32) * 2 - 1).astype(np.float32)
+    w = (rng.random((N, K), dtype=np.float32) * 2 - 1).astype(np.float32)
+    blocked = orc.matmul(x, w)
+    ref = orc.matmul(x, w, reference=True)
+    assert np.array_equal(blocked.view(np.uint32), ref.view(np.uint32))
+    exact = x.astype(np.float64) @ w.astype(np.float64).T
+    absprod = np.abs(x.astype(np.float64)) @ np.abs(w.astype(np.float64)).T
+    assert np.all(np.abs(blocked - exact) <= (K + 1) * 2.0 ** -24 * absprod)
+
+
+def test_rms_norm_cascade_sum_bits(orc):
+    # packages/kernels/root.zig:799-817
+    x = ((np.arange(896) * 17) % 101 + 1).astype(np.float32) * np.float32(0.125)
+    assert np.float32(orc.sum_squares_pinned(x)).view(np.uint32) == 0x473BE6E0
+    t = (np.arange(11) + 1).astype(np.float32) * np.float32(0.125)
+    assert np.float32(orc.sum_squares_pinned(t)).view(np.uint32) == 0x40FD0000
+
+
+def test_small_exact_cases(orc):
+    # packages/kernels/root.zig:772-797
+    assert np.array_equal(orc.softmax(np.array([2, 2], np.float32)), np.array([0.5, 0.5], np.float32))
+    assert orc.silu(np.array([0.0], np.float32))[0] == 0.0
+    out = orc.rms_norm(np.full(4, 3, np.float32), np.ones(4, np.float32), 0.0)
+    assert np.array_equal(out, np.ones(4, np.float32))
+
+
+def test_elementwise_d53_bounds(orc):
+    # packages/kernels/root.zig:828-923 (D53 bounds, seeded inputs)
+    rng = np.random.default_rng(0xB22026)
+    x = ((rng.random(17) * 2 - 1) * 2).astype(np.float32)
+    w = (rng.random(17) * 2 - 1).astype(np.float32)
+    got = orc.rms_norm(x, w, 1e-5).astype(np.float64)
+    inv = 1.0 / np.sqrt((x.astype(np.float64) ** 2).mean() + np.float64(np.float32(1e-5)))
+    ref = x.astype(np.float64) * inv * w.astype(np.float64)
+    assert np.all(np.abs(got - ref) <= (17 + 8) / 2 ** 24 * np.abs(ref))
+    s = ((rng.random(64) * 2 - 1) * 8).astype(np.float32)
+    ref = s.astype(np.float64) / (1 + np.exp(-s.astype(np.float64)))
+    got = orc.silu(s).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= 4 / 2 ** 24 * np.abs(ref))
+    z = ((rng.random(19) * 2 - 1) * 8).astype(np.float32)
+    e = np.exp(z.astype(np.float64) - z.max())
+    ref = e / e.sum()
+    assert np.all(np.abs(orc.softmax(z) - ref) <= (19 + 8) / 2 ** 24 * np.abs(ref))
+
+
+def test_block_diagonal_mask_matches_reference_test(orc):
+    # src/ncm_mask.zig:48-64
+    m = orc.block_diagonal_mask(2, [1, 2], [False, True])
+    assert m.shape == (5, 5)
+    assert m[0, 0] and not m[0, 1] and not m[0, 2]
+    assert m[2, 0] and not m[2, 1] and m[2, 2] and not m[2, 3]
+    assert m[3, 3] and m[3, 4] and m[4, 3]
+
+
+def test_block_causal_mask_adds_coarser_levels(orc):
+    diag = orc.block_diagonal_mask(1, [1, 2, 3])
+    causal = orc.block_causal_mask(1, [1, 2, 3])
+    assert np.all(causal >= diag)
+    # the level-2 queries (rows 4..6) see levels 0 and 1 (cols 1..3) but not later ones
+    assert causal[4:7, 1:4].all() and not diag[4:7, 1:4].any()
+    assert not causal[1, 2:].any()
+
+
+def test_level_positions_restart(orc):
+    # src/ncm_position.zig:154-159
+    assert orc.fill_level_positions(2, [1, 2, 3]).tolist() == [0, 1, 0, 0, 1, 0, 1, 2]
+
+
+def test_rope_positions_reuse_tables(orc):
+    # src/ncm_position.zig:120-152: llama3 tables gathered at restarting positions
+    inv = orc.rope_llama3(64, 500000.0, 32.0, 1.0, 4.0, 8192)
+    c, s = orc.rope_tables(inv, 3)
+    pos = [0, 1, 2, 0, 1, 0]
+    cg, sg = c[pos], s[pos]
+    assert np.array_equal(cg[3], c[0]) and np.array_equal(sg[4], s[1])
+
+
+def test_rope_default_against_float64(orc):
+    # B3-style check (packages/kernels/root.zig:925-945): |err| <= 1e-6 against
+    # tables whose angle is the f32 product position * inv_freq (as the
+    # transformers golden computes it) and whose cos/sin are exact.
+    for hd, theta in [(64, 10000.0), (64, 500000.0), (128, 10000.0)]:
+        inv, c, s = orc.rope_default(hd, theta, 4096)
+        inv64 = 1.0 / (np.float64(theta) ** (np.arange(0, hd, 2, dtype=np.float64) / hd))
+        ang = (np.arange(4096, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float64)
+        ref_c = np.concatenate([np.cos(ang)] * 2, axis=1)
+        ref_s = np.concatenate([np.sin(ang)] * 2, axis=1)
+        assert np.max(np.abs(c - ref_c)) <= 1e-6
+        assert np.max(np.abs(s - ref_s)) <= 1e-6
+        assert np.max(np.abs(inv - inv64) / inv64) <= 1e-6
+
+
+def test_attention_fully_masked_query_returns_output_bias(orc):
+    # packages/kernels/root.zig:1031-1066
+    x = np.array([[2, -3]], np.float32)
+    eye = np.array([[1, 0], [0, 1]], np.float32)
+    w = {"q_w": eye, "k_w": eye, "v_w": eye, "o_w": eye, "o_b": np.array([0.25, -0.5], np.float32)}
+    out = orc.attention(x, w, 1, 1, 2, 1e-5, np.ones((1, 2), np.float32), np.zeros((1, 2), np.float32),
+                        np.zeros((1, 1), np.uint8))
+    assert np.array_equal(out.ravel(), np.array([0.25, -0.5], np.float32))
+
+
+def test_tiny_decoder_attention_context(orc):
+    # src/decoder.zig:292-364: zero Q/K weights give uniform causal attention,
+    # so the context of token 1 is the mean of the two values.
+    x = np.array([[0.3, 0.4], [0.7, 0.8]], np.float32)
+    zero = np.zeros((2, 2), np.float32)
+    eye = np.eye(2, dtype=np.float32)
+    w = {"q_w": zero, "k_w": zero, "v_w": eye, "o_w": eye}
+    _, c, s = orc.rope_default(2, 10000.0, 2)
+    mask = orc.causal_mask(np.arange(2), np.arange(2))
+    out = orc.attention(x, w, 1, 1, 2, 1e-5, c, s, mask)
+    assert np.allclose(out[0], x[0], atol=1e-6)
+    assert np.allclose(out[1], (x[0] + x[1]) / 2, atol=1e-6)
