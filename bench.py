@@ -125,10 +125,16 @@ def ncu_traffic(rows_per_launch: int):
     """DRAM bytes per rvq_argmin launch from the committed ncu summary, scaled
     from the captured case to this launch by rows (traffic ~ rows * D * 2
     plus one codebook read)."""
-    p = ROOT / "profiles" / "rvq_argmin_traffic.json"
+    p = ROOT / "profiles" / "rvq_argmin_kernel_n131072.md"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
+    d = {}
+    for line in p.read_text().splitlines():
+        parts = line.strip().split(":")
+        if len(parts) == 2 and parts[0] in ("rows", "dram_bytes_per_launch", "codebook_bytes"):
+            d[parts[0]] = float(parts[1])
+    if len(d) != 3:
+        return None
     per_row = (d["dram_bytes_per_launch"] - d["codebook_bytes"]) / d["rows"]
     return per_row * rows_per_launch + d["codebook_bytes"]
 
