@@ -155,6 +155,23 @@ NCM_API int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                           const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
                           uint16_t* y, ncm_stream_t stream);
 
+/* No counterpart in the reference: ncmorph has no device code, so nothing
+ * there allocates device memory. This is ncm_rvq_level for callers that
+ * cannot call cudaMalloc — code running while a CUDA graph is captured on its
+ * stream, host plugins whose application owns every device allocation, paths
+ * that may not block on the allocator. It takes no context and allocates
+ * nothing: its scratch (the bf16 copy of the residual, the per-split argmin
+ * partials, the code norms when sqnorm is NULL, an error word) is a 16 MiB
+ * device array that every GPU loading the library holds until exit, so
+ * 2*N*D + 4*K bytes (plus split partials) must fit in it; larger problems
+ * are rejected with NCM_EINVAL. It runs on the current device; the first call
+ * on each device looks up the array's device address (make that call before
+ * any stream capture). All calls share the array: calls that overlap on the
+ * GPU race. Results equal ncm_rvq_level's; device-side failures are not
+ * reported (there is no context to carry them). */
+NCM_API int ncm_rvq_level_noalloc(float* residual, const uint16_t* codebook, const float* sqnorm, int32_t* codes,
+                                  int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
 /* ------------------------------------------------------- measurement */
 
 /* Benchmark instrumentation (no reference counterpart: ncmorph has no timing

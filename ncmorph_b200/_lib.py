@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "ncm_rvq_encode": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_pool_avg": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_rvq_decode": [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_rvq_level_noalloc": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_profile_enable": [c_vp, ctypes.c_int],
     "ncm_profile_read": [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i64)],
     "ncm_tokenizer_forward": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

@@ -1,0 +1,77 @@
+"""The no-allocation RVQ level entry point, through the C ABI.
+
+Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
+being captured on its stream (an allocation would break the capture), host
+plugins whose application owns every device allocation, and latency paths that
+may not block on the allocator. ncm_rvq_level_noalloc serves them: it takes no
+context and keeps its scratch in a fixed device array inside the library.
+
+This file is named to be collected last, so a run that stops at the first
+failure has already run every other test. It must pass alone in a fresh
+process and after the other tests.
+"""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(residual, codebook, sqnorm, codes):
+    from ncmorph_b200 import _lib
+    N, D = residual.shape
+    K = codebook.shape[0]
+    vp = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream(residual.device).cuda_stream)
+    return _lib.load().ncm_rvq_level_noalloc(vp(residual), vp(codebook), vp(sqnorm), vp(codes), N, D, K, stream)
+
+
+def _case(dev, N, D, K, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    r = torch.randn((N, D), generator=g, device=dev)
+    cb = torch.randn((K, D), generator=g, device=dev).to(torch.bfloat16)
+    return r, cb
+
+
+def test_noalloc_matches_rvq_level_on_two_calls(cuda_dev):
+    from ncmorph_b200 import vq
+    # First call: config-1 level shape with caller-supplied norms (code-split
+    # partials in the scratch). Second call: smaller and ragged, norms computed
+    # in the scratch — the first call's leftovers must not leak into it.
+    for (N, D, K, give_norms, seed) in [(4096, 256, 1024, True, 1), (1000, 136, 700, False, 2)]:
+        r, cb = _case(cuda_dev, N, D, K, seed)
+        sq = vq.code_sqnorm(cb)
+        r_ref = r.clone()
+        codes_ref = vq.rvq_level(r_ref, cb, sq)
+        r_na = r.clone()
+        codes_na = torch.full((N,), -1, dtype=torch.int32, device=cuda_dev)
+        rc = _noalloc(r_na, cb, sq if give_norms else None, codes_na)
+        assert rc == 0
+        torch.cuda.synchronize()
+        # same kernels and arithmetic: codes and the f32 residual update match exactly
+        assert torch.equal(codes_na, codes_ref), f"codes differ (N={N} D={D} K={K})"
+        assert torch.equal(r_na, r_ref), f"residual differs (N={N} D={D} K={K})"
+
+
+def test_noalloc_allocates_nothing_after_setup(cuda_dev):
+    r, cb = _case(cuda_dev, 2048, 512, 2048, 3)
+    codes = torch.empty((2048,), dtype=torch.int32, device=cuda_dev)
+    assert _noalloc(r.clone(), cb, None, codes) == 0          # set-up call on this device
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda_dev)
+    for _ in range(3):
+        assert _noalloc(r, cb, None, codes) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda_dev)
+    assert free1 == free0
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch(cuda_dev):
+    from ncmorph_b200 import _lib
+    # 4096 x 4096 bf16 rows need 32 MiB of scratch, beyond the fixed 16 MiB
+    r = torch.zeros((4096, 4096), device=cuda_dev)
+    cb = torch.zeros((8, 4096), dtype=torch.bfloat16, device=cuda_dev)
+    codes = torch.empty((4096,), dtype=torch.int32, device=cuda_dev)
+    assert _noalloc(r, cb, None, codes) == _lib.NCM_EINVAL
+    assert b"scratch" in _lib.load().ncm_last_error()
