@@ -284,12 +284,16 @@ template <int BN, bool SWAP>
 cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const LinearArgs& a, int grid,
                           cudaStream_t stream) {
   constexpr size_t smem = sizeof(GemmSmem<BN>) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  // the shared-memory opt-in is per device: remember which devices have it
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !(attr_set & (1ull << dev))) {
+    e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    if (dev < 64) attr_set |= 1ull << dev;
   }
   linear_bf16_kernel<BN, SWAP><<<grid, THREADS, smem, stream>>>(tmA, tmB, a);
   return cudaGetLastError();

@@ -540,12 +540,15 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(rvq_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ARGMIN_SMEM);
+  // the shared-memory opt-in is per device: remember which devices have it
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !(attr_set & (1ull << dev))) {
+    e = cudaFuncSetAttribute(rvq_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ARGMIN_SMEM);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    if (dev < 64) attr_set |= 1ull << dev;
   }
   ArgminArgs a;
   a.csq = sqnorm;

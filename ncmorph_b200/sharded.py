@@ -1,0 +1,90 @@
+"""Row-sharded RVQ encode: one process per GPU, codebooks replicated, codes
+and reconstructions all-gathered over the process group (NCCL over NVLink on
+a B200 node).
+
+Token rows are independent at every RVQ step (research/reference/
+vq_forward_semantics.md:59-82), so rank r encodes the contiguous block of
+rows it owns and the only exchange is the all-gather of the int32 codes and
+the bf16 reconstructions that the north star names. Shards have equal
+padded length so that one all_gather_into_tensor per tensor suffices; padding
+rows are never encoded and are trimmed after the gather.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(total_rows: int, world: int, rank: int) -> tuple[int, int, int]:
+    """(start, stop, padded_len) of rank's contiguous row block."""
+    if total_rows <= 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad sharding arguments")
+    n = -(-total_rows // world)
+    start = min(rank * n, total_rows)
+    stop = min(start + n, total_rows)
+    return start, stop, n
+
+
+def _device_encode(x, codebooks, sqnorms, codes_out, recon_out):
+    from . import vq
+    vq.rvq_encode(x, codebooks, sqnorms, codes=codes_out, recon=recon_out)
+
+
+class ShardedEncoder:
+    """Encodes this rank's rows and all-gathers codes and reconstructions.
+
+    `encode(x, codebooks, sqnorms, codes_out, recon_out)` fills the outputs
+    ([L, n] int32 and [n, D]); it defaults to the tcgen05 path
+    (ncmorph_b200.vq.rvq_encode). Buffers are allocated once; the tensors a
+    call returns are views of them, valid until the next call.
+    """
+
+    def __init__(self, codebooks: torch.Tensor, total_rows: int, x_dtype: torch.dtype = torch.bfloat16,
+                 sqnorms: torch.Tensor | None = None, group=None, encode: Callable | None = None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.codebooks = codebooks
+        self.sqnorms = sqnorms
+        self.total = total_rows
+        self.encode = encode or _device_encode
+        self.start, self.stop, self.n = shard_bounds(total_rows, self.world, self.rank)
+        L, D = codebooks.shape[0], codebooks.shape[-1]
+        dev = codebooks.device
+        self.L = L
+        self.codes_pad = torch.zeros((L, self.n), dtype=torch.int32, device=dev)
+        self.recon_pad = torch.zeros((self.n, D), dtype=x_dtype, device=dev)
+        # outputs concatenated along dim 0 (the layout every backend accepts)
+        self.codes_all = torch.empty((self.world * L, self.n), dtype=torch.int32, device=dev)
+        self.recon_all = torch.empty((self.world * self.n, D), dtype=x_dtype, device=dev)
+
+    @property
+    def rows(self) -> int:
+        return self.stop - self.start
+
+    def __call__(self, x_local: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        valid = self.rows
+        if x_local.shape[0] != valid:
+            raise ValueError(f"rank {self.rank} owns rows [{self.start}, {self.stop}) but got {x_local.shape[0]}")
+        if valid == self.n:
+            self.encode(x_local, self.codebooks, self.sqnorms, self.codes_pad, self.recon_pad)
+        elif valid > 0:  # short last shard: encode into dense buffers, then pad
+            codes = torch.empty((self.L, valid), dtype=torch.int32, device=x_local.device)
+            self.encode(x_local, self.codebooks, self.sqnorms, codes, self.recon_pad[:valid])
+            self.codes_pad[:, :valid] = codes
+        dist.all_gather_into_tensor(self.codes_all, self.codes_pad, group=self.group)
+        dist.all_gather_into_tensor(self.recon_all, self.recon_pad, group=self.group)
+        codes = self.codes_all.view(self.world, self.L, self.n).permute(1, 0, 2).reshape(self.L, -1)
+        return codes[:, : self.total], self.recon_all[: self.total]
+
+
+def sharded_encode(x_local: torch.Tensor, codebooks: torch.Tensor, total_rows: int,
+                   sqnorms: torch.Tensor | None = None, group=None,
+                   encode: Callable | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """One-shot form of ShardedEncoder: returns (codes [L, total_rows] int32,
+    recon [total_rows, D]) on every rank."""
+    enc = ShardedEncoder(codebooks, total_rows, x_local.dtype, sqnorms, group, encode)
+    codes, recon = enc(x_local)
+    return codes.contiguous(), recon
