@@ -155,6 +155,96 @@ NCM_API int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                           const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
                           uint16_t* y, ncm_stream_t stream);
 
+/* -------------------------------------- L3-L6: NCM decoder forward pieces */
+
+/* Row-wise bf16 RMSNorm: y = bf16(bf16(x * inv) * bf16(w)), inv = 1/sqrt(mean(x^2) + eps)
+ * in f32, then + bias (rounded) when bias is non-NULL. x, y [rows, width] bf16 (width % 8 == 0).
+ * Replaces kernels.rms_norm_bf16 (packages/kernels/root.zig:243-252) applied per row
+ * (src/decoder.zig:234-251) and ncm_norm.rms_norm_rows_with_bias (src/ncm_norm.zig:21-49).
+ * The sum of squares is a tree sum, not PyTorch's cascade (root.zig:152-224). */
+NCM_API int ncm_rms_norm_bf16(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                              int64_t rows, int64_t width, float eps, ncm_stream_t stream);
+
+/* out[t, :] = table[ids[t], :] (bf16). Replaces kernels.embedding_row
+ * (packages/kernels/root.zig:288-301) over a sequence; an id outside [0, vocab)
+ * makes ncm_sync report NCM_ERANGE (decoder.zig:107 returns TokenIdOutOfRange). */
+NCM_API int ncm_embedding_gather(ncm_ctx_t* ctx, const uint16_t* table, int64_t vocab, int64_t width,
+                                 const int32_t* ids, int64_t T, uint16_t* out, ncm_stream_t stream);
+
+/* Host function: RoPE cos/sin tables [T, head_dim] at explicit positions, with
+ * libm powf/cosf/sinf exactly as rope_default + rope_tables (root.zig:305-348)
+ * and ncm_position.tables_at_positions (src/ncm_position.zig:71-118) build them. */
+NCM_API int ncm_rope_tables_host(int32_t head_dim, float theta, const int32_t* positions, int64_t T, float* cos_out,
+                                 float* sin_out);
+
+/* Attention mask description. mode: 0 causal (causal_mask, root.zig:380-399,
+ * no sliding window), 1 block-diagonal (src/ncm_mask.zig:10-42), 2 block-causal
+ * (each level also sees every earlier level). In block modes positions are
+ * [prefix | level 0 | level 1 | ...]; prefix_pad_mask bit i marks prefix key i
+ * as padding (prefix_length <= 64). */
+typedef struct ncm_mask {
+  int32_t mode;
+  int32_t prefix_length;
+  uint64_t prefix_pad_mask;
+  int32_t num_levels;
+  int32_t level_lengths[32];
+} ncm_mask_t;
+
+/* Multi-head GQA attention core of attention_impl in bf16 mode
+ * (packages/kernels/root.zig:450-581) from projected rows: qkv [T, qkv_stride]
+ * bf16 holds Q (heads*64 columns), then K (kv_heads*64), then V (kv_heads*64).
+ * If cos/sin [T, 64] (device f32) are given, RoPE is applied IN PLACE to the
+ * Q and K columns first (rotate_head bf16 mode, root.zig:615-633). out [T, heads*64]
+ * bf16 is the context before the output projection. head_dim must be 64; T % 8 == 0. */
+NCM_API int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t,
+                               const float* sin_t, uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads,
+                               const ncm_mask_t* mask, ncm_stream_t stream);
+
+/* NCM body forward (src/ncm_model.zig:89-250) with the bf16 layer of
+ * src/decoder.zig:168-216: input projection (+bias), level embeddings,
+ * per-level restarting RoPE positions, the configured mask, num_layers x
+ * [RMSNorm, fused QKV, RoPE, attention, O projection, residual, RMSNorm,
+ * fused gate|up, SiLU*up, down, residual], final RMSNorm (+bias). All
+ * activations bf16, f32 accumulation. T = prefix_length + sum(level_lengths). */
+typedef struct ncm_decoder_config {
+  int64_t hidden_size;
+  int64_t vq_width;
+  int64_t num_attention_heads;
+  int64_t num_key_value_heads;
+  int64_t head_dim; /* must be 64 */
+  int64_t intermediate_size;
+  float rms_norm_epsilon;
+  float rope_theta; /* default RoPE (rope_default) */
+  int32_t use_level_encoding;
+  ncm_mask_t mask;
+} ncm_decoder_config_t;
+
+typedef struct ncm_decoder_layer_weights {
+  const uint16_t* ln_1;      /* [hidden] */
+  const uint16_t* qkv;       /* [(H + 2*Hkv)*64, hidden]: the fused_qkv_weight of ncm_model.zig:37 */
+  const uint16_t* qkv_bias;  /* nullable */
+  const uint16_t* o;         /* [hidden, H*64] */
+  const uint16_t* o_bias;    /* nullable */
+  const uint16_t* ln_2;      /* [hidden] */
+  const uint16_t* gate_up;   /* [2*F, hidden]: gate_weight rows, then up_weight rows */
+  const uint16_t* down;      /* [hidden, F] */
+} ncm_decoder_layer_weights_t;
+
+typedef struct ncm_decoder_weights {
+  const uint16_t* input_projection;      /* [hidden, vq_width] */
+  const uint16_t* input_projection_bias; /* [hidden] */
+  const uint16_t* level_embedding;       /* [num_levels, hidden] */
+  const uint16_t* final_norm;            /* [hidden] */
+  const uint16_t* final_norm_bias;       /* nullable */
+  int32_t num_layers;
+  const ncm_decoder_layer_weights_t* layers; /* host array of num_layers entries (device pointers) */
+} ncm_decoder_weights_t;
+
+/* inputs [T, vq_width] bf16: the assembled prefix + target rows (ncm_model.zig:128-140);
+ * out [T, hidden] bf16: final-normalised hidden states in [prefix | levels] order. */
+NCM_API int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_decoder_weights_t* weights,
+                            const uint16_t* inputs, uint16_t* out, ncm_stream_t stream);
+
 /* No counterpart in the reference: ncmorph has no device code, so nothing
  * there allocates device memory. This is ncm_rvq_level for callers that
  * cannot call cudaMalloc — code running while a CUDA graph is captured on its
@@ -180,7 +270,8 @@ NCM_API int ncm_rvq_level_noalloc(float* residual, const uint16_t* codebook, con
  * launch. ncm_profile_read synchronises, returns the summed device time (ms)
  * and launch count of one family since the last read, and resets them.
  * Families: "rvq_argmin", "rvq_apply", "linear_bf16", "rvq_decode",
- * "code_sqnorm", "pool_avg", "scale_update", "cast"; "*" = all of them. */
+ * "code_sqnorm", "pool_avg", "scale_update", "cast", "attention",
+ * "decoder_elementwise"; "*" = all of them. */
 NCM_API int ncm_profile_enable(ncm_ctx_t* ctx, int on);
 NCM_API int ncm_profile_read(ncm_ctx_t* ctx, const char* kernel, double* total_ms, int64_t* launches);
 

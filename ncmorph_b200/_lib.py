@@ -40,6 +40,55 @@ class TokenizerConfig(ctypes.Structure):
     ]
 
 
+class Mask(ctypes.Structure):
+    """Mirror of ncm_mask_t."""
+
+    _fields_ = [
+        ("mode", c_i32),
+        ("prefix_length", c_i32),
+        ("prefix_pad_mask", ctypes.c_uint64),
+        ("num_levels", c_i32),
+        ("level_lengths", c_i32 * 32),
+    ]
+
+
+class DecoderConfig(ctypes.Structure):
+    """Mirror of ncm_decoder_config_t."""
+
+    _fields_ = [
+        ("hidden_size", c_i64),
+        ("vq_width", c_i64),
+        ("num_attention_heads", c_i64),
+        ("num_key_value_heads", c_i64),
+        ("head_dim", c_i64),
+        ("intermediate_size", c_i64),
+        ("rms_norm_epsilon", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+        ("use_level_encoding", c_i32),
+        ("mask", Mask),
+    ]
+
+
+class DecoderLayerWeights(ctypes.Structure):
+    """Mirror of ncm_decoder_layer_weights_t (device pointers)."""
+
+    _fields_ = [(n, c_vp) for n in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down")]
+
+
+class DecoderWeights(ctypes.Structure):
+    """Mirror of ncm_decoder_weights_t."""
+
+    _fields_ = [
+        ("input_projection", c_vp),
+        ("input_projection_bias", c_vp),
+        ("level_embedding", c_vp),
+        ("final_norm", c_vp),
+        ("final_norm_bias", c_vp),
+        ("num_layers", c_i32),
+        ("layers", ctypes.POINTER(DecoderLayerWeights)),
+    ]
+
+
 # name -> argtypes (all functions return int status unless listed in _RESTYPES)
 SIGNATURES: dict[str, list] = {
     "ncm_ctx_create": [ctypes.c_int, ctypes.POINTER(c_vp)],
@@ -58,6 +107,11 @@ SIGNATURES: dict[str, list] = {
     "ncm_rvq_encode": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_pool_avg": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_rvq_decode": [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_rms_norm_bf16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp],
+    "ncm_embedding_gather": [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
+    "ncm_rope_tables_host": [c_i32, ctypes.c_float, c_vp, c_i64, c_vp, c_vp],
+    "ncm_attention_bf16": [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, ctypes.POINTER(Mask), c_vp],
+    "ncm_ncm_forward": [c_vp, ctypes.POINTER(DecoderConfig), ctypes.POINTER(DecoderWeights), c_vp, c_vp, c_vp],
     "ncm_rvq_level_noalloc": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_profile_enable": [c_vp, ctypes.c_int],
     "ncm_profile_read": [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i64)],

@@ -58,8 +58,9 @@ int ncm_fail(int status, const char* fmt, ...) {
 
 namespace ncm {
 
-const char* const kKernelNames[KID_COUNT] = {"rvq_argmin", "rvq_apply", "linear_bf16", "rvq_decode",
-                                             "code_sqnorm", "pool_avg",   "scale_update", "cast"};
+const char* const kKernelNames[KID_COUNT] = {"rvq_argmin", "rvq_apply",    "linear_bf16", "rvq_decode",
+                                             "code_sqnorm", "pool_avg",     "scale_update", "cast",
+                                             "attention",   "decoder_elementwise"};
 
 Launch::Launch(ncm_ctx* ctx, KernelId id, cudaStream_t stream) : ctx_(ctx), id_(id), stream_(stream) {
   ProfState& p = ctx->prof;
@@ -102,10 +103,16 @@ void* ctx_workspace(ncm_ctx* ctx, size_t bytes) {
 }
 
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  return make_tmap_bf16_2d_strided(map, base, rows, cols, cols, box_rows);
+}
+
+bool make_tmap_bf16_2d_strided(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                               uint64_t row_stride, uint32_t box_rows) {
   auto fn = tmap_encode_fn();
-  if (fn == nullptr || rows == 0 || cols == 0 || (cols * 2) % 16 != 0 || !aligned16(base)) return false;
+  if (fn == nullptr || rows == 0 || cols == 0 || row_stride < cols || (row_stride * 2) % 16 != 0 || !aligned16(base))
+    return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
   cuuint32_t box[2] = {64u, box_rows};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,

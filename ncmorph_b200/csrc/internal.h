@@ -23,6 +23,8 @@ enum KernelId {
   KID_POOL,
   KID_SCALE_UPDATE,
   KID_CAST,
+  KID_ATTENTION,
+  KID_DECODER_ELEMENTWISE,
   KID_COUNT
 };
 extern const char* const kKernelNames[KID_COUNT];
@@ -81,6 +83,31 @@ void* ctx_workspace(ncm_ctx* ctx, size_t bytes);
 // Builds a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a
 // box of [box_rows, 64] and 128-byte swizzling. Returns false on failure.
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+// Same, over rows `row_stride` elements apart (a column slice of a wider matrix).
+bool make_tmap_bf16_2d_strided(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                               uint64_t row_stride, uint32_t box_rows);
+
+// ---- decoder pieces (decoder.cu, attention.cu)
+cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* y, int rows,
+                                 int width, float eps, cudaStream_t st);
+cudaError_t launch_rope_bf16(uint16_t* qkv, long long stride, int T, int heads_qk, const float* c, const float* s,
+                             cudaStream_t st);
+cudaError_t launch_v_transpose(const uint16_t* qkv, long long stride, long long voff, int T, int vwidth, uint16_t* vt,
+                               cudaStream_t st);
+cudaError_t launch_silu_mul_bf16(const uint16_t* gu, uint16_t* out, int T, int F, cudaStream_t st);
+cudaError_t launch_add_bf16(uint16_t* h, const uint16_t* a, long long n, cudaStream_t st);
+cudaError_t launch_add_level_embedding(uint16_t* h, const uint16_t* emb, const int* row_level, int T, int width,
+                                       cudaStream_t st);
+cudaError_t launch_embedding_gather(const uint16_t* table, int vocab, int width, const int32_t* ids, int T,
+                                    uint16_t* out, int* err, cudaStream_t st);
+void rope_tables_host(int head_dim, float theta, const int* positions, int T, float* cos_out, float* sin_out);
+// Fused masked attention over the Q and K columns of fused QKV rows (row
+// stride qkv_stride elements) and V transposed to [Hkv*64, T]; head_dim 64.
+// mode 0 causal, 1 block-diagonal, 2 block-causal.
+int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const uint16_t* vt, uint16_t* out, int T,
+                   int H, int Hkv, int mode, int prefix, unsigned long long pad_mask, const int* level_lens,
+                   int nlev, cudaStream_t stream);
 
 // ---- RVQ launchers (rvq.cu)
 struct RvqPartial {

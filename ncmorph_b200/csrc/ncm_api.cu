@@ -1,0 +1,224 @@
+// C-ABI entry points of the NCM decoder forward (config 4): RMSNorm,
+// embedding gather, RoPE tables, attention, and the full layer stack.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "internal.h"
+
+namespace {
+
+bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int ctx_ok(ncm_ctx* ctx) {
+  if (ctx == nullptr) return ncm_fail(NCM_EINVAL, "null context");
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != ctx->device) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  }
+  return NCM_OK;
+}
+
+int check_mask(const ncm_mask_t* m, int64_t T) {
+  if (m == nullptr) return ncm_fail(NCM_EINVAL, "attention: null mask");
+  if (m->mode < 0 || m->mode > 2) return ncm_fail(NCM_EINVAL, "attention: mask mode %d unknown", m->mode);
+  if (m->mode == 0) return NCM_OK;
+  if (m->prefix_length < 0 || m->prefix_length > 64)
+    return ncm_fail(NCM_EINVAL, "attention: prefix_length %d outside [0, 64]", m->prefix_length);
+  if (m->num_levels <= 0 || m->num_levels > 32) return ncm_fail(NCM_EINVAL, "attention: num_levels out of range");
+  int64_t s = m->prefix_length;
+  for (int i = 0; i < m->num_levels; ++i) {
+    if (m->level_lengths[i] <= 0) return ncm_fail(NCM_EINVAL, "attention: level %d is empty", i);
+    s += m->level_lengths[i];
+  }
+  if (s != T) return ncm_fail(NCM_EINVAL, "attention: prefix + levels = %lld but T = %lld", (long long)s, (long long)T);
+  return NCM_OK;
+}
+
+}  // namespace
+
+using namespace ncm;
+
+extern "C" {
+
+int ncm_rms_norm_bf16(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                      int64_t rows, int64_t width, float eps, ncm_stream_t stream) {
+  int rc = ctx_ok(ctx);
+  if (rc) return rc;
+  if (rows <= 0 || width <= 0 || width % 8 != 0 || rows > INT32_MAX || width > INT32_MAX || !x || !w || !y)
+    return ncm_fail(NCM_EINVAL, "rms_norm: bad arguments (rows=%lld width=%lld; width %% 8 == 0)", (long long)rows,
+                    (long long)width);
+  if (!a16(x) || !a16(w) || !a16(y) || (bias && !a16(bias)))
+    return ncm_fail(NCM_EINVAL, "rms_norm: buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+  NCM_CUDA_TRY(launch_rms_norm_bf16(x, w, bias, y, static_cast<int>(rows), static_cast<int>(width), eps, st));
+  return NCM_OK;
+}
+
+int ncm_embedding_gather(ncm_ctx_t* ctx, const uint16_t* table, int64_t vocab, int64_t width, const int32_t* ids,
+                         int64_t T, uint16_t* out, ncm_stream_t stream) {
+  int rc = ctx_ok(ctx);
+  if (rc) return rc;
+  if (vocab <= 0 || width <= 0 || width % 8 != 0 || T <= 0 || T > INT32_MAX || vocab > INT32_MAX || !table || !ids ||
+      !out)
+    return ncm_fail(NCM_EINVAL, "embedding_gather: bad arguments");
+  if (!a16(table) || !a16(out)) return ncm_fail(NCM_EINVAL, "embedding_gather: buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+  NCM_CUDA_TRY(launch_embedding_gather(table, static_cast<int>(vocab), static_cast<int>(width), ids,
+                                       static_cast<int>(T), out, ctx->d_err, st));
+  return NCM_OK;
+}
+
+int ncm_rope_tables_host(int32_t head_dim, float theta, const int32_t* positions, int64_t T, float* cos_out,
+                         float* sin_out) {
+  if (head_dim <= 0 || head_dim % 2 != 0 || !(theta > 0.f) || T < 0 || (T > 0 && (!positions || !cos_out || !sin_out)))
+    return ncm_fail(NCM_EINVAL, "rope_tables: bad arguments");
+  rope_tables_host(head_dim, theta, positions, static_cast<int>(T), cos_out, sin_out);
+  return NCM_OK;
+}
+
+int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t, const float* sin_t,
+                       uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
+                       ncm_stream_t stream) {
+  int rc = ctx_ok(ctx);
+  if (rc) return rc;
+  if (T <= 0 || T > INT32_MAX || T % 8 != 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || !qkv || !out)
+    return ncm_fail(NCM_EINVAL, "attention: bad shape (T=%lld must be a multiple of 8, heads %d, kv_heads %d)",
+                    (long long)T, heads, kv_heads);
+  if (qkv_stride < static_cast<int64_t>(heads + 2 * kv_heads) * 64 || qkv_stride % 8 != 0)
+    return ncm_fail(NCM_EINVAL, "attention: qkv_stride %lld too small or not a multiple of 8", (long long)qkv_stride);
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return ncm_fail(NCM_EINVAL, "attention: give both cos and sin");
+  if (!a16(qkv) || !a16(out)) return ncm_fail(NCM_EINVAL, "attention: buffers must be 16-byte aligned");
+  if ((rc = check_mask(mask, T))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t vw = static_cast<int64_t>(kv_heads) * 64;
+  WsCarver cv;
+  const size_t o_vt = cv.take(2 * vw * T);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "attention: workspace allocation failed");
+  uint16_t* vt = reinterpret_cast<uint16_t*>(ws + o_vt);
+  {
+    Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+    if (cos_t != nullptr)
+      NCM_CUDA_TRY(launch_rope_bf16(qkv, qkv_stride, static_cast<int>(T), heads + kv_heads, cos_t, sin_t, st));
+    NCM_CUDA_TRY(launch_v_transpose(qkv, qkv_stride, static_cast<int64_t>(heads + kv_heads) * 64,
+                                    static_cast<int>(T), static_cast<int>(vw), vt, st));
+  }
+  Launch _l(ctx, KID_ATTENTION, st);
+  return attention_bf16(ctx, qkv, qkv_stride, vt, out, static_cast<int>(T), heads, kv_heads, mask->mode,
+                        mask->prefix_length, mask->prefix_pad_mask, mask->level_lengths, mask->num_levels, st);
+}
+
+int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_decoder_weights_t* W,
+                    const uint16_t* inputs, uint16_t* out, ncm_stream_t stream) {
+  int rc = ctx_ok(ctx);
+  if (rc) return rc;
+  if (!cfg || !W || !inputs || !out) return ncm_fail(NCM_EINVAL, "ncm_forward: null argument");
+  const ncm_mask_t& m = cfg->mask;
+  if (m.mode != 1 && m.mode != 2) return ncm_fail(NCM_EINVAL, "ncm_forward: mask mode must be block-diagonal or block-causal");
+  int64_t T = m.prefix_length;
+  for (int i = 0; i < m.num_levels && i < 32; ++i) T += m.level_lengths[i];
+  const int64_t Hd = cfg->hidden_size, V = cfg->vq_width, F = cfg->intermediate_size;
+  const int H = static_cast<int>(cfg->num_attention_heads), Hkv = static_cast<int>(cfg->num_key_value_heads);
+  if (cfg->head_dim != 64) return ncm_fail(NCM_EINVAL, "ncm_forward: head_dim must be 64");
+  if (Hd <= 0 || V <= 0 || F <= 0 || Hd % 8 || V % 8 || F % 8 || H <= 0 || Hkv <= 0 || H % Hkv)
+    return ncm_fail(NCM_EINVAL, "ncm_forward: bad dimensions");
+  if ((rc = check_mask(&m, T))) return rc;
+  if (T % 8 != 0) return ncm_fail(NCM_EINVAL, "ncm_forward: sequence length %lld must be a multiple of 8", (long long)T);
+  if (W->num_layers <= 0 || W->layers == nullptr || !W->input_projection || !W->input_projection_bias ||
+      !W->final_norm || (cfg->use_level_encoding && !W->level_embedding))
+    return ncm_fail(NCM_EINVAL, "ncm_forward: missing weights");
+  for (int l = 0; l < W->num_layers; ++l) {
+    const auto& L = W->layers[l];
+    if (!L.ln_1 || !L.qkv || !L.o || !L.ln_2 || !L.gate_up || !L.down)
+      return ncm_fail(NCM_EINVAL, "ncm_forward: layer %d is missing a weight", l);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t QKV = static_cast<int64_t>(H + 2 * Hkv) * 64;
+  WsCarver cv;
+  const size_t o_h = cv.take(2 * T * Hd), o_n = cv.take(2 * T * Hd), o_qkv = cv.take(2 * T * QKV);
+  const size_t o_vt = cv.take(2 * T * Hkv * 64), o_ctx = cv.take(2 * T * H * 64), o_a = cv.take(2 * T * Hd);
+  const size_t o_gu = cv.take(2 * T * 2 * F), o_act = cv.take(2 * T * F);
+  const size_t o_cos = cv.take(4 * T * 64), o_sin = cv.take(4 * T * 64), o_lv = cv.take(4 * T);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "ncm_forward: workspace allocation failed");
+  uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
+  uint16_t* nrm = reinterpret_cast<uint16_t*>(ws + o_n);
+  uint16_t* qkv = reinterpret_cast<uint16_t*>(ws + o_qkv);
+  uint16_t* vt = reinterpret_cast<uint16_t*>(ws + o_vt);
+  uint16_t* ctxb = reinterpret_cast<uint16_t*>(ws + o_ctx);
+  uint16_t* a = reinterpret_cast<uint16_t*>(ws + o_a);
+  uint16_t* gu = reinterpret_cast<uint16_t*>(ws + o_gu);
+  uint16_t* act = reinterpret_cast<uint16_t*>(ws + o_act);
+  float* cosd = reinterpret_cast<float*>(ws + o_cos);
+  float* sind = reinterpret_cast<float*>(ws + o_sin);
+  int* row_level = reinterpret_cast<int*>(ws + o_lv);
+
+  // positions restart at 0 per level (ncm_position.fill_level_positions), RoPE tables on the host
+  std::vector<int> pos(T), lev(T);
+  {
+    int64_t t = 0;
+    for (; t < m.prefix_length; ++t) pos[t] = static_cast<int>(t), lev[t] = -1;
+    for (int i = 0; i < m.num_levels; ++i)
+      for (int p = 0; p < m.level_lengths[i]; ++p, ++t) pos[t] = p, lev[t] = cfg->use_level_encoding ? i : -1;
+  }
+  std::vector<float> ch(T * 64), sh(T * 64);
+  rope_tables_host(64, cfg->rope_theta, pos.data(), static_cast<int>(T), ch.data(), sh.data());
+  NCM_CUDA_TRY(cudaMemcpyAsync(cosd, ch.data(), 4 * T * 64, cudaMemcpyHostToDevice, st));
+  NCM_CUDA_TRY(cudaMemcpyAsync(sind, sh.data(), 4 * T * 64, cudaMemcpyHostToDevice, st));
+  NCM_CUDA_TRY(cudaMemcpyAsync(row_level, lev.data(), 4 * T, cudaMemcpyHostToDevice, st));
+  // the host vectors must outlive the asynchronous copies
+  NCM_CUDA_TRY(cudaStreamSynchronize(st));
+
+  const int Ti = static_cast<int>(T);
+  const float eps = cfg->rms_norm_epsilon;
+  rc = linear_bf16(ctx, inputs, W->input_projection, W->input_projection_bias, h, nullptr, T, V, Hd, st);
+  if (rc) return rc;
+  if (cfg->use_level_encoding) {
+    Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+    NCM_CUDA_TRY(launch_add_level_embedding(h, W->level_embedding, row_level, Ti, static_cast<int>(Hd), st));
+  }
+  for (int l = 0; l < W->num_layers; ++l) {
+    const auto& L = W->layers[l];
+    {
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_rms_norm_bf16(h, L.ln_1, nullptr, nrm, Ti, static_cast<int>(Hd), eps, st));
+    }
+    if ((rc = linear_bf16(ctx, nrm, L.qkv, L.qkv_bias, qkv, nullptr, T, Hd, QKV, st))) return rc;
+    {
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_rope_bf16(qkv, QKV, Ti, H + Hkv, cosd, sind, st));
+      NCM_CUDA_TRY(launch_v_transpose(qkv, QKV, static_cast<int64_t>(H + Hkv) * 64, Ti, Hkv * 64, vt, st));
+    }
+    {
+      Launch _l(ctx, KID_ATTENTION, st);
+      if ((rc = attention_bf16(ctx, qkv, QKV, vt, ctxb, Ti, H, Hkv, m.mode, m.prefix_length, m.prefix_pad_mask,
+                               m.level_lengths, m.num_levels, st)))
+        return rc;
+    }
+    if ((rc = linear_bf16(ctx, ctxb, L.o, L.o_bias, a, nullptr, T, static_cast<int64_t>(H) * 64, Hd, st))) return rc;
+    {
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_add_bf16(h, a, T * Hd, st));
+      NCM_CUDA_TRY(launch_rms_norm_bf16(h, L.ln_2, nullptr, nrm, Ti, static_cast<int>(Hd), eps, st));
+    }
+    if ((rc = linear_bf16(ctx, nrm, L.gate_up, nullptr, gu, nullptr, T, Hd, 2 * F, st))) return rc;
+    {
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_silu_mul_bf16(gu, act, Ti, static_cast<int>(F), st));
+    }
+    if ((rc = linear_bf16(ctx, act, L.down, nullptr, a, nullptr, T, F, Hd, st))) return rc;
+    {
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_add_bf16(h, a, T * Hd, st));
+    }
+  }
+  Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+  NCM_CUDA_TRY(launch_rms_norm_bf16(h, W->final_norm, W->final_norm_bias, out, Ti, static_cast<int>(Hd), eps, st));
+  return NCM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,163 @@
+"""Device mirror of ncmorph's NCM body forward (src/ncm_model.zig:77-250) in
+bf16 (the layer of src/decoder.zig:168-216), plus the per-op entry points it
+is built from: RMSNorm, embedding gather, RoPE tables and masked attention.
+
+Masks: "causal" (kernels.causal_mask), "block_diagonal" (ncm_mask.zig:10-42,
+ncmorph's only NCM mask) and "block_causal" (each level also attends to
+every earlier level; the BASELINE config-4 pattern).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from .device import context, need, ptr, stream_of
+
+MASK_MODES = {"causal": 0, "block_diagonal": 1, "block_causal": 2}
+bf16 = torch.bfloat16
+
+
+def make_mask(mode: str, prefix_length: int = 0, level_lengths=(), prefix_pad=()) -> _lib.Mask:
+    m = _lib.Mask()
+    m.mode = MASK_MODES[mode]
+    m.prefix_length = int(prefix_length)
+    bits = 0
+    for i, padded in enumerate(prefix_pad):
+        if padded:
+            bits |= 1 << i
+    m.prefix_pad_mask = bits
+    m.num_levels = len(level_lengths)
+    for i, n in enumerate(level_lengths):
+        m.level_lengths[i] = int(n)
+    return m
+
+
+def level_positions(prefix_length: int, level_lengths) -> np.ndarray:
+    """ncm_position.fill_level_positions (src/ncm_position.zig:11-22)."""
+    pos = list(range(prefix_length))
+    for n in level_lengths:
+        pos.extend(range(n))
+    return np.asarray(pos, dtype=np.int32)
+
+
+def rope_tables(head_dim: int, theta: float, positions) -> tuple[np.ndarray, np.ndarray]:
+    """Host RoPE tables [T, head_dim] with libm, as the reference builds them."""
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    T = pos.size
+    c = np.empty((T, head_dim), np.float32)
+    s = np.empty((T, head_dim), np.float32)
+    _lib.call("ncm_rope_tables_host", head_dim, float(theta), ctypes.c_void_p(pos.ctypes.data), T,
+              ctypes.c_void_p(c.ctypes.data), ctypes.c_void_p(s.ctypes.data))
+    return c, s
+
+
+def rms_norm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float, bias: torch.Tensor | None = None):
+    rows, width = x.shape
+    need(x, bf16, "x")
+    need(weight, bf16, "weight", (width,))
+    y = torch.empty_like(x)
+    _lib.call("ncm_rms_norm_bf16", context(x.device), ptr(x), ptr(weight), ptr(bias), ptr(y), rows, width,
+              float(eps), stream_of(x))
+    return y
+
+
+def embedding_gather(table: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    vocab, width = table.shape
+    need(table, bf16, "table")
+    need(ids, torch.int32, "ids")
+    out = torch.empty((ids.numel(), width), dtype=bf16, device=table.device)
+    _lib.call("ncm_embedding_gather", context(table.device), ptr(table), vocab, width, ptr(ids), ids.numel(),
+              ptr(out), stream_of(table))
+    return out
+
+
+def attention_bf16(qkv: torch.Tensor, heads: int, kv_heads: int, mask: _lib.Mask,
+                   cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
+    """Context [T, heads*64] from fused QKV rows [T, (heads + 2*kv_heads)*64];
+    RoPE (if cos/sin given) is applied to qkv in place."""
+    T, stride = qkv.shape
+    need(qkv, bf16, "qkv")
+    out = torch.empty((T, heads * 64), dtype=bf16, device=qkv.device)
+    _lib.call("ncm_attention_bf16", context(qkv.device), ptr(qkv), stride, ptr(cos), ptr(sin), ptr(out), T, heads,
+              kv_heads, ctypes.byref(mask), stream_of(qkv))
+    return out
+
+
+@dataclass
+class LayerWeights:
+    ln_1: torch.Tensor
+    qkv: torch.Tensor
+    o: torch.Tensor
+    ln_2: torch.Tensor
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    qkv_bias: torch.Tensor | None = None
+    o_bias: torch.Tensor | None = None
+
+
+@dataclass
+class Weights:
+    input_projection: torch.Tensor
+    input_projection_bias: torch.Tensor
+    level_embedding: torch.Tensor
+    final_norm: torch.Tensor
+    layers: list = field(default_factory=list)
+    final_norm_bias: torch.Tensor | None = None
+
+
+@dataclass
+class Config:
+    hidden_size: int
+    vq_width: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    intermediate_size: int
+    level_lengths: tuple
+    prefix_length: int = 0
+    mask: str = "block_causal"
+    rms_norm_epsilon: float = 1e-5
+    rope_theta: float = 500000.0
+    use_level_encoding: bool = True
+    head_dim: int = 64
+
+    @property
+    def seq_len(self) -> int:
+        return self.prefix_length + sum(self.level_lengths)
+
+
+def _vp(t):
+    return None if t is None else t.data_ptr()
+
+
+def forward(cfg: Config, w: Weights, inputs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ncm_model.forward on the GPU: inputs [T, vq_width] bf16 -> hidden [T, hidden] bf16."""
+    T = cfg.seq_len
+    need(inputs, bf16, "inputs", (T, cfg.vq_width))
+    c = _lib.DecoderConfig()
+    c.hidden_size, c.vq_width = cfg.hidden_size, cfg.vq_width
+    c.num_attention_heads, c.num_key_value_heads = cfg.num_attention_heads, cfg.num_key_value_heads
+    c.head_dim, c.intermediate_size = cfg.head_dim, cfg.intermediate_size
+    c.rms_norm_epsilon, c.rope_theta = cfg.rms_norm_epsilon, cfg.rope_theta
+    c.use_level_encoding = int(cfg.use_level_encoding)
+    c.mask = make_mask(cfg.mask, cfg.prefix_length, cfg.level_lengths)
+    layers = (_lib.DecoderLayerWeights * len(w.layers))()
+    for i, L in enumerate(w.layers):
+        for name in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down"):
+            setattr(layers[i], name, _vp(getattr(L, name)))
+    W = _lib.DecoderWeights()
+    W.input_projection = _vp(w.input_projection)
+    W.input_projection_bias = _vp(w.input_projection_bias)
+    W.level_embedding = _vp(w.level_embedding)
+    W.final_norm = _vp(w.final_norm)
+    W.final_norm_bias = _vp(w.final_norm_bias)
+    W.num_layers = len(w.layers)
+    W.layers = layers
+    if out is None:
+        out = torch.empty((T, cfg.hidden_size), dtype=bf16, device=inputs.device)
+    _lib.call("ncm_ncm_forward", context(inputs.device), ctypes.byref(c), ctypes.byref(W), ptr(inputs), ptr(out),
+              stream_of(inputs))
+    return out

@@ -1,0 +1,241 @@
+"""GPU parity of the NCM decoder pieces (L3-L6, config 4) against the oracle.
+
+The attention check runs the oracle's restatement of attention_impl in bf16
+mode (packages/kernels/root.zig:450-581) with 0/1 selection matrices as the
+Q/K/V/O projections, so the oracle sees exactly the GPU's Q, K and V and the
+comparison isolates RoPE, masking, softmax and the P.V product. The GPU uses
+an online softmax whose bf16 probabilities are unnormalised, so contexts are
+held to a bf16 bar, not bit equality:
+    |gpu - oracle| <= 2e-2 |oracle| + 1e-2 max|V|
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import check_gemm, from_dev_bf16, gen_bf16, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _selection(rows_from: int, width: int, count: int) -> np.ndarray:
+    w = np.zeros((count, width), np.float32)
+    w[np.arange(count), rows_from + np.arange(count)] = 1.0
+    return w
+
+
+def oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mask_bool):
+    """Context [T, H*64] from qkv rows via orc_attention with selection projections."""
+    T, width = qkv_bits.shape
+    x = orc.bf16_widen(qkv_bits)
+    w = {
+        "q_w": _selection(0, width, H * 64),
+        "k_w": _selection(H * 64, width, Hkv * 64),
+        "v_w": _selection((H + Hkv) * 64, width, Hkv * 64),
+        # output projection: identity onto the first H*64 columns of a width-wide output
+        "o_w": _selection(0, H * 64, H * 64) if width == H * 64 else np.vstack(
+            [np.eye(H * 64, dtype=np.float32), np.zeros((width - H * 64, H * 64), np.float32)]),
+    }
+    out = orc.attention(x, w, H, Hkv, 64, 1e-5, cos, sin, mask_bool.astype(np.uint8), bf16_mode=True)
+    return out[:, : H * 64]
+
+
+def _mask_case(orc, mode, T, prefix=0, levels=(), pad=()):
+    from ncmorph_b200.ncm_model import level_positions, make_mask
+    if mode == "causal":
+        mb = orc.causal_mask(np.arange(T), np.arange(T))
+        pos = np.arange(T, dtype=np.int32)
+    elif mode == "block_diagonal":
+        mb = orc.block_diagonal_mask(prefix, list(levels), list(pad))
+        pos = level_positions(prefix, levels)
+    else:
+        mb = orc.block_causal_mask(prefix, list(levels), list(pad))
+        pos = level_positions(prefix, levels)
+    return make_mask(mode, prefix, levels, pad), mb, pos
+
+
+@pytest.mark.parametrize("mode,T,prefix,levels,pad,H,Hkv", [
+    ("causal", 256, 0, (), (), 4, 2),
+    ("block_diagonal", 256, 2, (14, 16, 32, 64, 128), (False, True), 4, 2),
+    ("block_causal", 256, 0, (16, 16, 32, 64, 128), (), 8, 2),
+    ("block_causal", 200, 1, (7, 32, 160), (False,), 4, 1),
+    ("causal", 384, 0, (), (), 2, 2),
+])
+def test_attention_matches_oracle(orc, cuda_dev, mode, T, prefix, levels, pad, H, Hkv):
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(T + H)
+    width = (H + 2 * Hkv) * 64
+    qkv_bits = gen_bf16(rng, (T, width))
+    mask, mb, pos = _mask_case(orc, mode, T, prefix, levels, pad)
+    cos, sin = ncm_model.rope_tables(64, 500000.0, pos)
+    qkv = to_dev_bf16(qkv_bits, cuda_dev)
+    ctx = ncm_model.attention_bf16(qkv, H, Hkv, mask, torch.from_numpy(cos).to(cuda_dev),
+                                   torch.from_numpy(sin).to(cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(ctx))
+    ref = oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mb)
+    # RoPE was applied in place: Q/K columns must equal the oracle's rotate_head (bf16 mode) bit for bit
+    vmax = np.abs(orc.bf16_widen(qkv_bits[:, (H + Hkv) * 64:])).max()
+    err = np.abs(got - ref)
+    tol = 2e-2 * np.abs(ref) + 1e-2 * vmax
+    bad = np.argwhere(err > tol)
+    assert bad.size == 0, f"{len(bad)} context elements outside the bar; first {bad[0]} got {got[tuple(bad[0])]} ref {ref[tuple(bad[0])]}"
+    print(f"{mode} T={T}: max |err| {err.max():.3g}, mean {err.mean():.3g}")
+
+
+def test_rope_in_place_matches_rotate_head(orc, cuda_dev):
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(3)
+    T, H, Hkv = 64, 2, 1
+    width = (H + 2 * Hkv) * 64
+    qkv_bits = gen_bf16(rng, (T, width))
+    pos = ncm_model.level_positions(0, (32, 32))
+    cos, sin = ncm_model.rope_tables(64, 10000.0, pos)
+    qkv = to_dev_bf16(qkv_bits, cuda_dev)
+    mask = ncm_model.make_mask("block_diagonal", 0, (32, 32))
+    ncm_model.attention_bf16(qkv, H, Hkv, mask, torch.from_numpy(cos).to(cuda_dev), torch.from_numpy(sin).to(cuda_dev))
+    got = from_dev_bf16(qkv)
+    # oracle rotate_head via attention's Q path: project Q with identity, read it back through a 1-key mask? simpler:
+    # restate rotate_head (root.zig:615-633) here in f32 with bf16 rounding at each step
+    def rb(a):
+        return orc.round_bf16(np.asarray(a, np.float32))
+    x = orc.bf16_widen(qkv_bits).copy()
+    for hh in range(H + Hkv):
+        v = x[:, hh * 64:(hh + 1) * 64]
+        first, second = v[:, :32].copy(), v[:, 32:].copy()
+        cf, sf, cs, ss = rb(cos[:, :32]), rb(sin[:, :32]), rb(cos[:, 32:]), rb(sin[:, 32:])
+        left, right = rb(first * cf), rb(-second * sf)
+        right2, left2 = rb(first * ss), rb(second * cs)
+        v[:, :32] = rb(left + right)
+        v[:, 32:] = rb(left2 + right2)
+    assert np.array_equal(got[:, : (H + Hkv) * 64], orc.bf16_bits(x[:, : (H + Hkv) * 64]))
+    assert np.array_equal(got[:, (H + Hkv) * 64:], qkv_bits[:, (H + Hkv) * 64:])  # V untouched
+
+
+def test_rope_tables_bit_exact(orc):
+    from ncmorph_b200 import ncm_model
+    pos = ncm_model.level_positions(1, (3, 5))
+    c, s = ncm_model.rope_tables(64, 500000.0, pos)
+    _, oc, os_ = orc.rope_default(64, 500000.0, int(pos.max()) + 1)
+    assert np.array_equal(c, oc[pos]) and np.array_equal(s, os_[pos])
+
+
+def test_rms_norm_within_one_ulp(orc, cuda_dev):
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(8)
+    rows, width = 300, 2048
+    x = gen_bf16(rng, (rows, width), 3.0)
+    w = gen_bf16(rng, (width,))
+    y = from_dev_bf16(ncm_model.rms_norm_bf16(to_dev_bf16(x, cuda_dev), to_dev_bf16(w, cuda_dev), 1e-5))
+    ref = np.stack([orc.bf16_bits(orc.rms_norm(orc.bf16_widen(x[r]), orc.bf16_widen(w), 1e-5, bf16_mode=True))
+                    for r in range(rows)])
+    diff = np.abs(y.astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.99
+
+
+def test_embedding_gather_and_range(cuda_dev):
+    from ncmorph_b200 import _lib, device, ncm_model
+    table = torch.randn((50, 16), device=cuda_dev).to(torch.bfloat16)
+    ids = torch.tensor([3, 0, 49, 7], dtype=torch.int32, device=cuda_dev)
+    out = ncm_model.embedding_gather(table, ids)
+    assert torch.equal(out.view(torch.int16), table[ids.long()].view(torch.int16))
+    ncm_model.embedding_gather(table, torch.tensor([50], dtype=torch.int32, device=cuda_dev))
+    with pytest.raises(_lib.NcmError) as ei:
+        device.sync(cuda_dev)
+    assert ei.value.status == _lib.NCM_ERANGE
+
+
+# --------------------------------------------------------- full forward
+def _rand_weights(cfg, dev, seed, layers):
+    from ncmorph_b200.ncm_model import LayerWeights, Weights
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def r(*shape, s=0.02):
+        return (torch.randn(shape, generator=g, device=dev) * s).to(torch.bfloat16)
+
+    def ones(n):
+        return (1.0 + 0.1 * torch.randn((n,), generator=g, device=dev)).to(torch.bfloat16)
+
+    Hd, V, F = cfg.hidden_size, cfg.vq_width, cfg.intermediate_size
+    qkvw = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * 64
+    Ls = [LayerWeights(ln_1=ones(Hd), qkv=r(qkvw, Hd), o=r(Hd, cfg.num_attention_heads * 64), ln_2=ones(Hd),
+                       gate_up=r(2 * F, Hd), down=r(Hd, F)) for _ in range(layers)]
+    return Weights(input_projection=r(Hd, V), input_projection_bias=r(Hd, s=0.1),
+                   level_embedding=r(len(cfg.level_lengths), Hd, s=0.1), final_norm=ones(Hd), layers=Ls)
+
+
+def oracle_ncm_forward(orc, cfg, w, inputs_bits):
+    """ncm_model.forward (src/ncm_model.zig:89-250) with the bf16 layer of decoder.zig:168-216."""
+    f = lambda t: orc.bf16_widen(from_dev_bf16(t))  # noqa: E731
+    rb = orc.round_bf16
+    T = cfg.seq_len
+    h = orc.matmul_bf16(orc.bf16_widen(inputs_bits), f(w.input_projection), f(w.input_projection_bias), threads=8)
+    emb = f(w.level_embedding)
+    off = cfg.prefix_length
+    for i, n in enumerate(cfg.level_lengths):
+        if cfg.use_level_encoding:
+            h[off:off + n] = rb(h[off:off + n] + emb[i])
+        off += n
+    pos = np.asarray(orc.fill_level_positions(cfg.prefix_length, list(cfg.level_lengths)), np.int64)
+    _, ct, st = orc.rope_default(64, cfg.rope_theta, int(pos.max()) + 1)
+    cos, sin = ct[pos], st[pos]
+    mask = (orc.block_causal_mask if cfg.mask == "block_causal" else orc.block_diagonal_mask)(
+        cfg.prefix_length, list(cfg.level_lengths))
+    H, Hkv, F = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size
+    eps = cfg.rms_norm_epsilon
+
+    def norm_rows(x, wt):
+        return np.stack([orc.rms_norm(x[i], wt, eps, bf16_mode=True) for i in range(x.shape[0])])
+
+    for L in w.layers:
+        n = norm_rows(h, f(L.ln_1))
+        qkv = f(L.qkv)
+        aw = {"q_w": qkv[: H * 64], "k_w": qkv[H * 64:(H + Hkv) * 64], "v_w": qkv[(H + Hkv) * 64:], "o_w": f(L.o)}
+        att = orc.attention(n, aw, H, Hkv, 64, eps, cos, sin, mask.astype(np.uint8), bf16_mode=True)
+        h = rb(h + att)
+        n = norm_rows(h, f(L.ln_2))
+        gu = f(L.gate_up)
+        g = orc.matmul_bf16(n, gu[:F], threads=8)
+        u = orc.matmul_bf16(n, gu[F:], threads=8)
+        act = rb(orc.silu_bf16(g) * u)
+        h = rb(h + orc.matmul_bf16(act, f(L.down), threads=8))
+    return norm_rows(h, f(w.final_norm))
+
+
+@pytest.mark.parametrize("mask,prefix,levels", [("block_causal", 0, (16, 16, 32, 64, 128)),
+                                                ("block_diagonal", 0, (32, 32, 64, 128))])
+def test_ncm_forward_small_matches_oracle(orc, cuda_dev, mask, prefix, levels):
+    from ncmorph_b200 import ncm_model
+    cfg = ncm_model.Config(hidden_size=256, vq_width=64, num_attention_heads=4, num_key_value_heads=2,
+                           intermediate_size=512, level_lengths=levels, prefix_length=prefix, mask=mask)
+    w = _rand_weights(cfg, cuda_dev, 5, layers=2)
+    rng = np.random.default_rng(6)
+    inputs = gen_bf16(rng, (cfg.seq_len, cfg.vq_width))
+    out = ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(out))
+    ref = oracle_ncm_forward(orc, cfg, w, inputs)
+    err = np.abs(got - ref)
+    rms = np.sqrt((ref ** 2).mean(axis=1, keepdims=True))
+    tol = 3e-2 * np.abs(ref) + 3e-2 * rms
+    frac_bad = (err > tol).mean()
+    print(f"ncm forward {mask}: max |err| {err.max():.3g}, mean {err.mean():.3g}, outside bar {frac_bad:.2e}")
+    assert frac_bad == 0.0
+
+
+def test_config4_forward_runs_and_is_normalised(cuda_dev):
+    """BASELINE config 4 shapes: 16 layers, d=2048, 32/8 heads, FFN 8192, 4096 positions, block-causal."""
+    from ncmorph_b200 import device, ncm_model
+    cfg = ncm_model.Config(hidden_size=2048, vq_width=1024, num_attention_heads=32, num_key_value_heads=8,
+                           intermediate_size=8192, level_lengths=(256, 256, 512, 1024, 2048), mask="block_causal")
+    w = _rand_weights(cfg, cuda_dev, 9, layers=16)
+    for L in w.layers:
+        L.ln_1.fill_(1.0)
+        L.ln_2.fill_(1.0)
+    w.final_norm.fill_(1.0)
+    codes = torch.randint(0, 4096, (cfg.seq_len,), dtype=torch.int32, device=cuda_dev)
+    table = (torch.randn((4096, cfg.vq_width), device=cuda_dev)).to(torch.bfloat16)
+    inputs = ncm_model.embedding_gather(table, codes)
+    out = ncm_model.forward(cfg, w, inputs)
+    device.sync(cuda_dev)
+    o = out.float()
+    assert torch.isfinite(o).all()
+    rms = o.pow(2).mean(dim=1).sqrt()
+    assert torch.allclose(rms, torch.ones_like(rms), atol=2e-2)
