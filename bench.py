@@ -46,6 +46,9 @@ def parse_args():
     p.add_argument("--codes", type=int, default=16384)
     p.add_argument("--cpu-rows", type=int, default=2048, help="rows per CPU-baseline sample")
     p.add_argument("--seed", type=int, default=20260)
+    p.add_argument("--workload", choices=["rvq", "tokenizer", "linear", "decoder"], default="rvq",
+                   help="rvq = BASELINE config 5 (the headline); tokenizer = config 2; linear = config 3 sweep; "
+                        "decoder = config 4")
     return p.parse_args()
 
 
@@ -327,8 +330,212 @@ def run_ours(a):
     return 0
 
 
+# ------------------------------------------------- secondary workloads
+# Configs 1-4 are parity cases; these modes measure them on one GPU with the
+# same timing rules (CUDA events, warm-up, clocks) for the records in DESIGN.md.
+
+def _timed_loop(fn, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / max(steps, 1)
+
+
+def _profile(lib, ctx, names):
+    import ctypes
+    out = {}
+    for n in names:
+        t = ctypes.c_double()
+        c = ctypes.c_int64()
+        lib.ncm_profile_read(ctx, n.encode(), ctypes.byref(t), ctypes.byref(c))
+        out[n] = (t.value, c.value)
+    return out
+
+
+def run_secondary(a):
+    import ctypes
+
+    import torch
+
+    from ncmorph_b200 import _lib, device as ndev, kernels, ncm_model, vq
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    ctx = ndev.context(dev)
+    peaks, peak_kind = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(a.seed)
+
+    def rnd(shape, scale=1.0):
+        return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    sampler = ClockSampler(0)
+    line = {"n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "bf16 operands, f32 accumulation", "data": "synthetic"}
+
+    if a.workload == "tokenizer":
+        B, T, Din, D, K, L = 8, 2048, 2048, 1024, 4096, 8
+        factors = [16, 8, 4, 2, 1]
+        x = rnd((B, T, Din))
+        w_in, w_out = rnd((D, Din), 0.02), rnd((Din, D), 0.02)
+        decay = torch.tensor([0.6 ** l for l in range(L)], device=dev).view(1, L, 1, 1)
+        cbs = (rnd((5, L, K, D)).float() * decay).to(torch.bfloat16)
+        sq = vq.code_sqnorm(cbs)
+        step = lambda: vq.tokenizer_forward(x, w_in, cbs, w_out, factors, sqnorms=sq)  # noqa: E731
+        _timed_loop(step, 0, a.warmup)
+        lib.ncm_profile_read(ctx, b"*", None, None)
+        lib.ncm_profile_enable(ctx, 1)
+        sampler.start()
+        ms = _timed_loop(step, a.steps, 0)
+        clocks = sampler.stop()
+        lib.ncm_profile_enable(ctx, 0)
+        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "*"])
+        rows = sum(B * T // f for f in factors)
+        dist_flops = 2.0 * rows * K * D * L
+        proj_flops = 2 * 2.0 * B * T * Din * D
+        am_ms, am_n = prof["rvq_argmin"]
+        ln_ms, _ = prof["linear_bf16"]
+        x_host = torch.empty_like(x, device="cpu").pin_memory()
+        x_host.copy_(x.cpu())
+        codes_host = torch.empty(L * rows, dtype=torch.int32).pin_memory()
+
+        def step_e2e():
+            x.copy_(x_host, non_blocking=True)
+            codes, _, _ = vq.tokenizer_forward(x, w_in, cbs, w_out, factors, sqnorms=sq)
+            codes_host.copy_(torch.cat([c.reshape(-1) for c in codes]), non_blocking=True)
+
+        ms_e2e = _timed_loop(step_e2e, a.steps, 1)
+        achieved = dist_flops / (am_ms / a.steps * 1e-3) / 1e12
+        line.update({
+            "metric": "tokenizer_vectors_per_s", "value": B * T / (ms * 1e-3), "unit": "vectors/s",
+            "ms_per_step": ms,
+            "config": {"workload": "multiscale tokenizer forward (BASELINE config 2)", "batch": B, "seq_len": T,
+                       "model_width": Din, "vq_width": D, "codebook_size": K, "levels_per_scale": L,
+                       "pool_factors": factors, "rows_quantised": rows},
+            "e2e": {"value": B * T / (ms_e2e * 1e-3), "unit": "vectors/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": codes_host.numel() * 4},
+            "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel (all 40 levels)", "achieved": achieved,
+                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                         "frac": achieved / float(peaks["bf16_tflops"]),
+                         "peak_source": f"{peak_kind} bf16_tflops (burst; a 2-3 ms step)",
+                         "argmin_ms_per_step": am_ms / a.steps, "linear_ms_per_step": ln_ms / a.steps,
+                         "linear_tflops": proj_flops / (ln_ms / a.steps * 1e-3) / 1e12,
+                         "share_argmin": am_ms / max(prof["*"][0] + am_ms + ln_ms, 1e-9)},
+            "gpu_launches": int(am_n + prof["linear_bf16"][1] + prof["*"][1]), "clocks": clocks})
+    elif a.workload == "linear":
+        Ms = [1, 64, 512, 4096, 8192]
+        KNs = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)]
+        rows, tot_flops, tot_ms = [], 0.0, 0.0
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: flushed between timed calls
+        sampler.start()
+        for M in Ms:
+            for (K, N) in KNs:
+                xx, ww = rnd((M, K)), rnd((N, K), 0.02)
+                yy = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                for _ in range(a.warmup):
+                    kernels.linear_bf16(xx, ww, out=yy)
+                times = []
+                for _ in range(a.steps):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    kernels.linear_bf16(xx, ww, out=yy)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1))
+                t = sorted(times)[len(times) // 2]
+                fl = 2.0 * M * N * K
+                by = 2.0 * (M * K + N * K + M * N)
+                tot_flops += fl
+                tot_ms += t
+                ai = fl / by
+                roof = min(float(peaks["bf16_tflops"]) * 1e12, float(peaks["hbm_gbs"]) * 1e9 * ai)
+                rows.append({"M": M, "K": K, "N": N, "us": t * 1e3, "tflops": fl / (t * 1e-3) / 1e12,
+                             "gbs": by / (t * 1e-3) / 1e9, "frac_of_roofline": fl / (t * 1e-3) / roof})
+                del xx, ww, yy
+        clocks = sampler.stop()
+        line.update({
+            "metric": "linear_sweep_tflops", "value": tot_flops / (tot_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": tot_ms,
+            "config": {"workload": "bf16 linear sweep, Llama-3.2-1B shapes (BASELINE config 3)",
+                       "l2": "256 MiB buffer written between timed calls", "shapes": rows},
+            "roofline": {"bound": "min(tensor, hbm x intensity) per shape",
+                         "peak_source": f"{peak_kind} bf16_tflops / hbm_gbs"},
+            "clocks": clocks})
+    else:  # decoder
+        cfg = ncm_model.Config(hidden_size=2048, vq_width=1024, num_attention_heads=32, num_key_value_heads=8,
+                               intermediate_size=8192, level_lengths=(256, 256, 512, 1024, 2048),
+                               mask="block_causal")
+        Hd, F = cfg.hidden_size, cfg.intermediate_size
+        layers = [ncm_model.LayerWeights(ln_1=rnd((Hd,), 0.0) + 1, qkv=rnd((3072, Hd), 0.02), o=rnd((Hd, 2048), 0.02),
+                                         ln_2=rnd((Hd,), 0.0) + 1, gate_up=rnd((2 * F, Hd), 0.02),
+                                         down=rnd((Hd, F), 0.02)) for _ in range(16)]
+        w = ncm_model.Weights(input_projection=rnd((Hd, cfg.vq_width), 0.02), input_projection_bias=rnd((Hd,), 0.02),
+                              level_embedding=rnd((5, Hd), 0.02), final_norm=rnd((Hd,), 0.0) + 1, layers=layers)
+        table = rnd((4096, cfg.vq_width))
+        codes = torch.randint(0, 4096, (cfg.seq_len,), generator=g, device=dev, dtype=torch.int32)
+        out = torch.empty((cfg.seq_len, Hd), dtype=torch.bfloat16, device=dev)
+
+        def step():
+            inputs = ncm_model.embedding_gather(table, codes)
+            ncm_model.forward(cfg, w, inputs, out=out)
+
+        _timed_loop(step, 0, a.warmup)
+        lib.ncm_profile_read(ctx, b"*", None, None)
+        lib.ncm_profile_enable(ctx, 1)
+        sampler.start()
+        ms = _timed_loop(step, a.steps, 0)
+        clocks = sampler.stop()
+        lib.ncm_profile_enable(ctx, 0)
+        prof = _profile(lib, ctx, ["linear_bf16", "attention", "*"])
+        T = cfg.seq_len
+        lin_flops = 16 * 2.0 * T * Hd * (3072 + 2048 + 3 * F) + 2.0 * T * cfg.vq_width * Hd
+        lv = list(cfg.level_lengths)
+        allowed = sum(n * sum(lv[: i + 1]) for i, n in enumerate(lv))
+        att_flops = 16 * 4.0 * allowed * 32 * 64
+        ln_ms, ln_n = prof["linear_bf16"]
+        at_ms, at_n = prof["attention"]
+        codes_host = codes.cpu().pin_memory()
+        out_host = torch.empty((T, Hd), dtype=torch.bfloat16).pin_memory()
+
+        def step_e2e():
+            codes.copy_(codes_host, non_blocking=True)
+            step()
+            out_host.copy_(out, non_blocking=True)
+
+        ms_e2e = _timed_loop(step_e2e, a.steps, 1)
+        lin_ach = lin_flops / (ln_ms / a.steps * 1e-3) / 1e12
+        line.update({
+            "metric": "decoder_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"workload": "NCM decoder forward (BASELINE config 4)", "layers": 16, "d_model": Hd,
+                       "heads": 32, "kv_heads": 8, "head_dim": 64, "ffn": F, "positions": T,
+                       "levels": lv, "mask": "block_causal", "flops_linear": lin_flops, "flops_attention": att_flops},
+            "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": T * Hd * 2},
+            "roofline": {"bound": "tensor", "kernel": "linear_bf16_kernel", "achieved": lin_ach,
+                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                         "frac": lin_ach / float(peaks["bf16_tflops"]), "peak_source": f"{peak_kind} bf16_tflops",
+                         "linear_ms_per_step": ln_ms / a.steps, "attention_ms_per_step": at_ms / a.steps,
+                         "attention_tflops": att_flops / (at_ms / a.steps * 1e-3) / 1e12,
+                         "other_ms_per_step": prof["*"][0] / a.steps},
+            "gpu_launches": int(ln_n + at_n + prof["*"][1]), "clocks": clocks})
+    ndev.sync(dev)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload != "rvq":
+        return run_secondary(a)
     if a.impl == "reference":
         return run_reference(a)
     return run_ours(a)

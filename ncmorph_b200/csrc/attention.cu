@@ -101,6 +101,10 @@ __device__ __forceinline__ bool tile_needed(int t, int P, int A, int B) {
   return k0 < P || (k0 < B && k0 + AT_K > A);
 }
 
+__device__ __forceinline__ bool key_allowed(int k, int P, int lo, int hi, unsigned long long pad_mask) {
+  return k < P ? !((pad_mask >> k) & 1ull) : (k >= lo && k < hi);
+}
+
 __device__ __forceinline__ void raise_abort_attn(volatile int* abort_flag, int* err) {
   *abort_flag = 1;
   atomicOr(err, kErrWaitTimeout);
@@ -254,6 +258,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
   } else {
     // ------------------------------------------------- softmax / epilogue
+    // Scores live in the log2 domain: t = bf16(q.k) * scale * log2(e), so
+    // p = 2^(t - max t) and alpha = 2^(old max - new max).
     const int qw = warp & 3;
     const int row = qw * 32 + lane;
     const int q = q0 + row;
@@ -268,7 +274,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       lo = args.mode == 2 ? args.prefix : args.level_start[lq];
     }
     const int Pq = args.mode == 0 ? 0 : args.prefix;
-    const float kLog2e = 1.4426950408889634f;
+    const float c_scale = args.scale * 1.4426950408889634f;
     float o[AT_D];
 #pragma unroll
     for (int d = 0; d < AT_D; ++d) o[d] = 0.f;
@@ -284,58 +290,81 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t sbase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + b * AT_K;
-      float s[AT_K];
-      float mt = -INFINITY;
       const int k0 = t * AT_K;
-#pragma unroll
+      // warp-uniform choice between the plain and the masked score path
+      const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + AT_K <= hi);
+      // pass 1 over 32-column chunks: masked log2-domain scores and their max
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll 1
       for (int c = 0; c < AT_K; c += 32) {
         uint32_t v[32];
         tmem_ld_x32(sbase + c, v);
         tmem_wait_ld();
+        if (unmasked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int k = k0 + c + i;
-          const bool allowed = k < Pq ? !((args.pad_mask >> k) & 1ull) : (k >= lo && k < hi);
-          // bf16(bf16(q.k) * scale), as the reference's bf16 attention rounds scores
-          const float sv = bf16_to_f32(f32_to_bf16(bf16_to_f32(f32_to_bf16(__uint_as_float(v[i]))) * args.scale));
-          s[c + i] = allowed ? sv : -INFINITY;
-          mt = fmaxf(mt, s[c + i]);
+          for (int i = 0; i < 32; i += 2) {
+            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+            mx0 = fmaxf(mx0, bf16lo(pr));
+            mx1 = fmaxf(mx1, bf16hi(pr));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+            const int ka = k0 + c + i;
+            mx0 = fmaxf(mx0, key_allowed(ka, Pq, lo, hi, args.pad_mask) ? bf16lo(pr) : -INFINITY);
+            mx1 = fmaxf(mx1, key_allowed(ka + 1, Pq, lo, hi, args.pad_mask) ? bf16hi(pr) : -INFINITY);
+          }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.s_empty[b]);
+      // the max over raw bf16 scores, moved to the log2 domain (scale > 0 keeps the order)
+      const float mt = fmaxf(mx0, mx1) * c_scale;
       const float m_new = fmaxf(m, mt);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f((m - m_use) * kLog2e);  // m = -inf -> 0
+      const float alpha = ex2_approx(m - m_use);  // m = -inf -> 0
       // P_j (bf16) into the swizzled A-operand tile; wait until P.V_{j-2} released it
       if (!mbar_wait(&S.p_empty[b], bp ^ 1u, abort_flag)) {
         ok = false;
         break;
       }
-      float rs = 0.f;
+      // pass 2: p = 2^(t - m), packed to bf16 and stored in the 128-byte-swizzled layout
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < AT_K; c += 32) {
+        uint32_t v[32];
+        tmem_ld_x32(sbase + c, v);
+        tmem_wait_ld();
+        uint8_t* prow = S.p[b][c >> 6] + row * 128;
+        const int ch0 = (c & 63) >> 3;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint8_t* prow = S.p[b][half] + row * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int q4 = 0; q4 < 4; ++q4) {  // four 16-byte chunks of 8 keys
           uint32_t w4[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int i = half * 64 + ch * 8 + e * 2;
-            const float p0 = exp2f((s[i] - m_use) * kLog2e);
-            const float p1 = exp2f((s[i + 1] - m_use) * kLog2e);
-            w4[e] = pack_bf16x2(p0, p1);
-            rs += bf16lo(w4[e]) + bf16hi(w4[e]);
+            const int i = q4 * 8 + e * 2;
+            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+            float t0 = fmaf(bf16lo(pr), c_scale, -m_use), t1 = fmaf(bf16hi(pr), c_scale, -m_use);
+            if (!unmasked) {
+              const int ka = k0 + c + i;
+              t0 = key_allowed(ka, Pq, lo, hi, args.pad_mask) ? t0 : -INFINITY;
+              t1 = key_allowed(ka + 1, Pq, lo, hi, args.pad_mask) ? t1 : -INFINITY;
+            }
+            const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+            w4[e] = cvt_bf16x2(p0, p1);
+            rs0 += p0;
+            rs1 += p1;
           }
-          const int sw = ch ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
+          const int sw = (ch0 + q4) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
           *reinterpret_cast<uint4*>(prow + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.s_empty[b]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.p_full[b]);
-      l = l * alpha + rs;
+      l = l * alpha + (rs0 + rs1);
       m = m_new;
       // fold in O_{j-1}
       if (j > 0) {
@@ -346,17 +375,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t obase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D;
-#pragma unroll
-        for (int c = 0; c < AT_D; c += 32) {
-          uint32_t v[32];
-          tmem_ld_x32(obase + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(v[i]));
-        }
+        uint32_t v[AT_D];
+        tmem_ld_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.o_empty[bo]);
+#pragma unroll
+        for (int i = 0; i < AT_D; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
       }
       alpha_prev = alpha;
       ++j;
@@ -368,17 +395,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       } else {
         tc_fence_after();
         const uint32_t obase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D;
-#pragma unroll
-        for (int c = 0; c < AT_D; c += 32) {
-          uint32_t v[32];
-          tmem_ld_x32(obase + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha_prev, __uint_as_float(v[i]));
-        }
+        uint32_t v[AT_D];
+        tmem_ld_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.o_empty[bo]);
+#pragma unroll
+        for (int i = 0; i < AT_D; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
       }
     }
     if (!ok) raise_abort_attn(abort_flag, args.err);
@@ -388,10 +413,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < AT_D; c += 8) {
         uint4 w;
-        w.x = pack_bf16x2(o[c + 0] * inv, o[c + 1] * inv);
-        w.y = pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
-        w.z = pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
-        w.w = pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
+        w.x = cvt_bf16x2(o[c + 0] * inv, o[c + 1] * inv);
+        w.y = cvt_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
+        w.z = cvt_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
+        w.w = cvt_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
         *reinterpret_cast<uint4*>(dst + c) = w;
       }
     }

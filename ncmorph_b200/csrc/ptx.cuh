@@ -220,6 +220,21 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
 }
 
+// Two f32 -> packed bf16x2 with the hardware's round-to-nearest-even
+// (lo in the low half). Equals the reference rule for every non-NaN input.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x on the special-function unit (PTX ex2.approx; ~2 ulp, -inf -> 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
