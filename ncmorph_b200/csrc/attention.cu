@@ -30,7 +30,7 @@ constexpr int AT_Q = 128;       // queries per CTA
 constexpr int AT_K = 128;       // keys per tile
 constexpr int AT_D = 64;        // head dim (fixed)
 constexpr int AT_STAGES = 3;
-constexpr int AT_THREADS = 192;
+constexpr int AT_THREADS = 320;  // w0 TMA, w1 MMA, w2-9 softmax
 constexpr uint32_t AT_TMEM_COLS = 512;  // S: 2 x 128 cols, O: 2 x 64 cols
 constexpr int kMaxLevels = 32;
 
@@ -48,7 +48,11 @@ struct __align__(1024) AttnSmem {
   uint64_t p_empty[2];
   uint64_t o_full[2];
   uint64_t o_empty[2];
+  uint64_t mx_ready[2];
+  uint64_t l_ready;
   uint64_t drain;
+  float mx[2][2][AT_Q];   // [tile parity][key half][row] partial row maxima
+  float lsum[2][AT_Q];    // [key half][row] final partial row sums
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -132,12 +136,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S.s_full[b], 1);
-      mbar_init(&S.s_empty[b], 4);
-      mbar_init(&S.p_full[b], 4);
+      mbar_init(&S.s_empty[b], 8);
+      mbar_init(&S.p_full[b], 8);
       mbar_init(&S.p_empty[b], 1);
       mbar_init(&S.o_full[b], 1);
-      mbar_init(&S.o_empty[b], 4);
+      mbar_init(&S.o_empty[b], 8);
+      mbar_init(&S.mx_ready[b], 8);
     }
+    mbar_init(&S.l_ready, 8);
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_mbar_init();
@@ -258,12 +264,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
   } else {
     // ------------------------------------------------- softmax / epilogue
+    // Eight warps: warp w reads TMEM lanes 32*(w%4).. (its 32 query rows) and
+    // owns key columns [64*hf, 64*hf + 64) of each S tile and output dims
+    // [32*hf, 32*hf + 32) of O, hf = (w - 2) / 4. The two warps of a row group
+    // swap their partial row maxima through shared memory each tile.
     // Scores live in the log2 domain: t = bf16(q.k) * scale * log2(e), so
     // p = 2^(t - max t) and alpha = 2^(old max - new max).
     const int qw = warp & 3;
+    const int hf = (warp - 2) >> 2;
     const int row = qw * 32 + lane;
     const int q = q0 + row;
-    // this query's allowed key interval beyond the prefix
     int lo = 0, hi = 0;
     if (args.mode == 0) {
       lo = 0;
@@ -275,9 +285,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     const int Pq = args.mode == 0 ? 0 : args.prefix;
     const float c_scale = args.scale * 1.4426950408889634f;
-    float o[AT_D];
+    constexpr int HK = AT_K / 2, HD = AT_D / 2;
+    float o[HD];
 #pragma unroll
-    for (int d = 0; d < AT_D; ++d) o[d] = 0.f;
+    for (int d = 0; d < HD; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
     bool ok = true;
     int j = 0;
@@ -289,14 +300,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t sbase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + b * AT_K;
-      const int k0 = t * AT_K;
-      // warp-uniform choice between the plain and the masked score path
-      const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + AT_K <= hi);
-      // pass 1 over 32-column chunks: masked log2-domain scores and their max
+      const uint32_t sbase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + b * AT_K + hf * HK;
+      const int k0 = t * AT_K + hf * HK;
+      const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + HK <= hi);
+      // pass 1: max of this warp's 64 raw bf16 scores per row
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < AT_K; c += 32) {
+      for (int c = 0; c < HK; c += 32) {
         uint32_t v[32];
         tmem_ld_x32(sbase + c, v);
         tmem_wait_ld();
@@ -317,25 +327,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           }
         }
       }
-      // the max over raw bf16 scores, moved to the log2 domain (scale > 0 keeps the order)
-      const float mt = fmaxf(mx0, mx1) * c_scale;
+      // swap partial maxima with the partner warp (same rows, other key half)
+      S.mx[b][hf][row] = fmaxf(mx0, mx1);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.mx_ready[b]);
+      if (!mbar_wait(&S.mx_ready[b], bp, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const float mt = fmaxf(S.mx[b][0][row], S.mx[b][1][row]) * c_scale;
       const float m_new = fmaxf(m, mt);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m - m_use);  // m = -inf -> 0
-      // P_j (bf16) into the swizzled A-operand tile; wait until P.V_{j-2} released it
+      // P_j (bf16): this warp's key half goes to P block hf; wait until P.V_{j-2} released it
       if (!mbar_wait(&S.p_empty[b], bp ^ 1u, abort_flag)) {
         ok = false;
         break;
       }
-      // pass 2: p = 2^(t - m), packed to bf16 and stored in the 128-byte-swizzled layout
       float rs0 = 0.f, rs1 = 0.f;
+      uint8_t* prow = S.p[b][hf] + row * 128;
 #pragma unroll 1
-      for (int c = 0; c < AT_K; c += 32) {
+      for (int c = 0; c < HK; c += 32) {
         uint32_t v[32];
         tmem_ld_x32(sbase + c, v);
         tmem_wait_ld();
-        uint8_t* prow = S.p[b][c >> 6] + row * 128;
-        const int ch0 = (c & 63) >> 3;
+        const int ch0 = c >> 3;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {  // four 16-byte chunks of 8 keys
           uint32_t w4[4];
@@ -359,14 +375,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
       }
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.s_empty[b]);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.p_full[b]);
-      l = l * alpha + (rs0 + rs1);
+      if (lane == 0) {
+        mbar_arrive(&S.s_empty[b]);
+        mbar_arrive(&S.p_full[b]);
+      }
+      l = l * alpha + (rs0 + rs1);  // this warp's half of the row sum
       m = m_new;
-      // fold in O_{j-1}
+      // fold in this warp's 32 columns of O_{j-1}
       if (j > 0) {
         const uint32_t bo = (j - 1) & 1, bop = ((j - 1) >> 1) & 1;
         if (!mbar_wait(&S.o_full[bo], bop, abort_flag)) {
@@ -374,16 +391,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t obase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D;
-        uint32_t v[AT_D];
-        tmem_ld_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        uint32_t v[HD];
+        tmem_ld_x32(tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D + hf * HD, v);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.o_empty[bo]);
 #pragma unroll
-        for (int i = 0; i < AT_D; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
+        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
       }
       alpha_prev = alpha;
       ++j;
@@ -394,24 +409,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         ok = false;
       } else {
         tc_fence_after();
-        const uint32_t obase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D;
-        uint32_t v[AT_D];
-        tmem_ld_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        uint32_t v[HD];
+        tmem_ld_x32(tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D + hf * HD, v);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.o_empty[bo]);
 #pragma unroll
-        for (int i = 0; i < AT_D; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
+        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
       }
+    }
+    // the full row sum is the sum of both halves' sums
+    if (ok) {
+      S.lsum[hf][row] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.l_ready);
+      ok = mbar_wait(&S.l_ready, 0, abort_flag);
     }
     if (!ok) raise_abort_attn(abort_flag, args.err);
     if (ok && q < args.T) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* dst = args.out + static_cast<size_t>(q) * args.H * AT_D + h * AT_D;
+      const float lt = S.lsum[0][row] + S.lsum[1][row];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      uint16_t* dst = args.out + static_cast<size_t>(q) * args.H * AT_D + h * AT_D + hf * HD;
 #pragma unroll
-      for (int c = 0; c < AT_D; c += 8) {
+      for (int c = 0; c < HD; c += 8) {
         uint4 w;
         w.x = cvt_bf16x2(o[c + 0] * inv, o[c + 1] * inv);
         w.y = cvt_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
