@@ -132,11 +132,15 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
   if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, D, 256))
     return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
                     (long long)D, (long long)K);
+  // with one code split the update runs inside the distance kernel
+  const bool fused = update && plan.splits == 1;
+  RvqFusedUpdate fu{resid, src_bf16, shadow, codebook};
   {
     Launch _launch(ctx, KID_RVQ_ARGMIN, stream);
-    NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream));
+    NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream,
+                                   fused ? &fu : nullptr));
   }
-  if (plan.splits > 1 || update) {
+  if (plan.splits > 1 || (update && !fused)) {
     Launch _launch(ctx, KID_RVQ_APPLY, stream);
     NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, src_bf16, resid, shadow, codebook, ctx->d_err, N, D, K, update,
                                   stream));

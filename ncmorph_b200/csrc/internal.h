@@ -123,11 +123,22 @@ struct RvqPlan {
 };
 RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K);
 
+// Residual update done inside the distance kernel (only when the plan has
+// one code split): resid = (src_bf16 ? f32(src_bf16) : resid) - e[code],
+// shadow = bf16(resid) when shadow is non-null.
+struct RvqFusedUpdate {
+  float* resid;
+  const uint16_t* src_bf16;
+  uint16_t* shadow;
+  const uint16_t* codebook;
+};
+
 // argmin_k (sqnorm[k] - 2 a_n . e_k) over bf16 rows `a` [N,D] (via tmA) and
-// codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials.
+// codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials, and
+// applies `fu` when given and the plan has one split.
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
-                              int64_t D, int64_t K, cudaStream_t stream);
+                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu = nullptr);
 
 // Final code per row (reducing partials when splits > 1), then
 // resid = (src_bf16 ? f32(src_bf16) : resid) - e[code]; shadow = bf16(resid).

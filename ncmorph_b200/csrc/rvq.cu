@@ -9,10 +9,13 @@
 // MMA and the argmin epilogue, and two 256-column TMEM accumulators let the
 // epilogue of code tile t run while the MMA of tile t+1 proceeds.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over work units):
+// Warp roles (320 threads, one CTA per SM, persistent over work units):
 //   warp 0     TMA producer (one elected lane)
 //   warp 1     TMEM allocator + MMA issuer (one elected lane)
 //   warps 2-5  argmin epilogue, one thread per accumulator row (TMEM lane)
+//   warps 6-9  residual update: when a row block's codes are final they
+//              apply r -= e[code] (f32) and write bf16(r) for the next level,
+//              while the tensor cores already work on the next row block
 //
 // A work unit is (row block of 128 residuals, range of code tiles). When the
 // rows alone cannot fill the GPU the code range is split, each split writes a
@@ -31,7 +34,7 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int STAGES = 4;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -45,6 +48,9 @@ struct __align__(1024) ArgminSmem {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
+  uint64_t upd_full[2];   // epilogue -> update warps: a row block's codes are in codes_s
+  uint64_t upd_empty[2];  // update warps -> epilogue: codes_s slot free again
+  int codes_s[2][BM];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -58,6 +64,12 @@ struct ArgminArgs {
   int* err;
   int N, D, K;
   int splits, tiles_per_split, code_tiles, n_units;
+  // fused residual update (splits == 1 only)
+  int fuse;
+  float* resid;
+  const uint16_t* src_bf16;  // level input in bf16 (level 0), else null: read resid
+  uint16_t* shadow;          // bf16(resid) for the next level, or null
+  const uint16_t* codebook;
 };
 
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err) {
@@ -84,6 +96,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S.tfull[b], 1);
       mbar_init(&S.tempty[b], 4);
+      mbar_init(&S.upd_full[b], 4);
+      mbar_init(&S.upd_empty[b], 4);
     }
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
@@ -193,11 +207,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_wait(&S.drain, 0, nullptr);
       }
     }
-  } else {
+  } else if (warp < 6) {
     // -------------------------------------------------- argmin epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     float* csq_s = S.csq[warp - 2];
     uint32_t acc_it = 0;
+    uint32_t uit = 0;  // units handed to the update warps
     bool ok = true;
     for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
       const int rb = unit / args.splits;
@@ -264,6 +279,65 @@ __global__ void __launch_bounds__(THREADS, 1)
           args.part[static_cast<size_t>(sp) * args.N + row] = RvqPartial{best, bidx};
         }
       }
+      if (args.fuse) {
+        const uint32_t ub = uit & 1u, up = (uit >> 1) & 1u;
+        if (!mbar_wait(&S.upd_empty[ub], up ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        S.codes_s[ub][q * 32 + lane] = row < args.N ? bidx : -1;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.upd_full[ub]);
+        ++uit;
+      }
+    }
+    if (!ok) raise_abort(abort_flag, args.err);
+  } else if (args.fuse) {
+    // ------------------------------------------------- residual update
+    // Warp uw updates rows uw*32.. of each finished row block: one row at a
+    // time, lanes striding the row in 16-byte (f32) / 8-byte (bf16) pieces.
+    const int uw = warp - 6;
+    uint32_t uit = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; unit < args.n_units; unit += gridDim.x) {
+      const uint32_t ub = uit & 1u, up = (uit >> 1) & 1u;
+      if (!mbar_wait(&S.upd_full[ub], up, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int rb = unit;  // splits == 1: one unit per row block
+      for (int r = 0; r < 32; ++r) {
+        const int code = S.codes_s[ub][uw * 32 + r];
+        if (code < 0) continue;
+        if (code >= args.K) {
+          if (lane == 0) atomicOr(args.err, kErrBadIndex);
+          continue;
+        }
+        const size_t ro = static_cast<size_t>(rb * BM + uw * 32 + r) * args.D;
+        const uint16_t* e = args.codebook + static_cast<size_t>(code) * args.D;
+#pragma unroll 4
+        for (int d = lane * 4; d < args.D; d += 128) {
+          float4 x;
+          if (args.src_bf16 != nullptr) {
+            const uint2 sv = *reinterpret_cast<const uint2*>(args.src_bf16 + ro + d);
+            x = make_float4(bf16lo(sv.x), bf16hi(sv.x), bf16lo(sv.y), bf16hi(sv.y));
+          } else {
+            x = *reinterpret_cast<const float4*>(args.resid + ro + d);
+          }
+          const uint2 ev = __ldg(reinterpret_cast<const uint2*>(e + d));
+          x.x -= bf16lo(ev.x);
+          x.y -= bf16hi(ev.x);
+          x.z -= bf16lo(ev.y);
+          x.w -= bf16hi(ev.y);
+          *reinterpret_cast<float4*>(args.resid + ro + d) = x;
+          if (args.shadow != nullptr)
+            *reinterpret_cast<uint2*>(args.shadow + ro + d) =
+                make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.upd_empty[ub]);
+      ++uit;
     }
     if (!ok) raise_abort(abort_flag, args.err);
   }
@@ -513,6 +587,16 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
   RvqPlan p{};
   p.row_blocks = ceil_div(N, BM);
   p.code_tiles = ceil_div(K, BN);
+  if (p.row_blocks >= num_sms) {
+    // enough row blocks for every SM: no code split, so the residual update
+    // can run inside the distance kernel
+    p.splits = 1;
+    p.tiles_per_split = p.code_tiles;
+    p.n_units = p.row_blocks;
+    p.grid = num_sms;
+    p.partial_bytes = 0;
+    return p;
+  }
   // Pick the split count that minimises (waves x tiles per unit); prefer fewer
   // splits on ties since every split adds a partial write and a reduction.
   long long best_cost = -1;
@@ -539,7 +623,7 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
 
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
-                              int64_t D, int64_t K, cudaStream_t stream) {
+                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu) {
   // the shared-memory opt-in is per device: remember which devices have it
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -562,6 +646,11 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.tiles_per_split = plan.tiles_per_split;
   a.code_tiles = plan.code_tiles;
   a.n_units = plan.n_units;
+  a.fuse = (fu != nullptr && plan.splits == 1) ? 1 : 0;
+  a.resid = fu ? fu->resid : nullptr;
+  a.src_bf16 = fu ? fu->src_bf16 : nullptr;
+  a.shadow = fu ? fu->shadow : nullptr;
+  a.codebook = fu ? fu->codebook : nullptr;
   rvq_argmin_kernel<<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
   return cudaGetLastError();
 }

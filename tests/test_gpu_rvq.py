@@ -84,6 +84,31 @@ def test_config1_encode_decode(orc, cuda_dev):
     assert clean.mean() > 0.5
 
 
+@pytest.mark.parametrize("N,D,K,L", [(148 * 128 + 37, 256, 512, 3), (300 * 128, 64, 300, 2)])
+def test_fused_update_path_matches_oracle(orc, cuda_dev, N, D, K, L):
+    """Row blocks >= SM count: one code split, so the residual update (f32 and
+    its bf16 shadow) runs inside the distance kernel."""
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(N + K)
+    x = gen_bf16(rng, (N, D))
+    cbs = _cbs(rng, L, K, D, 0.5)
+    codes_d, recon_d, resid_d = vq.rvq_encode(to_dev_bf16(x, cuda_dev), to_dev_bf16(cbs, cuda_dev),
+                                              want_residual=True)
+    codes = codes_d.cpu().numpy()
+    best, gaps, resid, recon = orc.rvq_encode(x, cbs, codes_in=codes)
+    for l in range(L):
+        check_codes(codes[l], best[l], gaps[l], f"fused level {l}")
+    assert np.array_equal(resid_d.cpu().numpy(), resid)
+    assert np.array_equal(from_dev_bf16(recon_d), orc.bf16_bits(recon))
+    # single-level entry point on the same rows (f32 residual in, no shadow out)
+    r = orc.bf16_widen(x).astype(np.float32).copy()
+    rd = torch.from_numpy(r).to(cuda_dev)
+    c0 = vq.rvq_level(rd, to_dev_bf16(cbs[0], cuda_dev)).cpu().numpy()
+    b0, g0 = orc.rvq_level(r, cbs[0], orc.code_sqnorm(cbs[0]), codes_in=c0)
+    check_codes(c0, b0, g0, "fused single level")
+    assert np.array_equal(rd.cpu().numpy(), r)
+
+
 def test_decode_rejects_out_of_range_codes(cuda_dev):
     from ncmorph_b200 import _lib, device, vq
     cbs = torch.zeros((2, 16, 8), dtype=torch.bfloat16, device=cuda_dev)
