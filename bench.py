@@ -274,15 +274,22 @@ def run_ours(a):
     argmin_avg_ms = max_over_ranks(argmin_ms / max(argmin_launches, 1))
     kernel_share = argmin_ms / max(argmin_ms + other_ms.value, 1e-9)
 
-    # ---- e2e: host rows in, gathered codes out, through the same C-ABI calls
+    # ---- e2e: host rows in, codes (and at N=1 the reconstructions) out.
+    # N=1: the host-buffer C-ABI entry (ncm_rvq_encode_host) with its chunked
+    # copy/compute pipeline. N>1: rows copied in, sharded encode + all-gather,
+    # gathered codes copied out.
     x_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(x.cpu())
     codes_host = torch.empty((L, a.rows), dtype=torch.int32).pin_memory()
+    recon_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory() if world == 1 else None
 
     def step_e2e():
-        x.copy_(x_host, non_blocking=True)
-        step()
-        codes_host.copy_(result["codes"], non_blocking=True)
+        if world == 1:
+            vq.rvq_encode_host(x_host, cbs, sq, codes_host=codes_host, recon_host=recon_host)
+        else:
+            x.copy_(x_host, non_blocking=True)
+            step()
+            codes_host.copy_(result["codes"], non_blocking=True)
 
     step_e2e()
     torch.cuda.synchronize()
@@ -314,7 +321,9 @@ def run_ours(a):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 operands, f32 accumulation", "data": "synthetic", "config": config_dict(a, world),
         "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": ms_e2e, "h2d_bytes_per_step": n * D * 2,
-                "d2h_bytes_per_step": int(codes_host.numel() * 4)},
+                "d2h_bytes_per_step": int(codes_host.numel() * 4 + (recon_host.numel() * 2 if recon_host is not None else 0)),
+                "path": "ncm_rvq_encode_host (chunked H2D/encode/D2H pipeline)" if world == 1
+                        else "H2D rows, sharded encode, NCCL all-gather, D2H codes"},
         "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",

@@ -121,6 +121,16 @@ NCM_API int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* co
                    int32_t* codes, uint16_t* recon, float* residual_out, int64_t N, int64_t D, int64_t K,
                    ncm_stream_t stream);
 
+/* Host-buffer form of ncm_rvq_encode, as a host caller with plain slices
+ * (the planned packages/vq) calls it: x_host [N,D] bf16 and codes_host [L,N],
+ * recon_host [N,D] (nullable) are HOST memory; codebooks/sqnorms are device
+ * buffers. Rows move in chunks so the host->device copies, the encode and the
+ * device->host copies of neighbouring chunks overlap (page-locked host memory
+ * gives full copy speed). Returns when the results are in host memory. */
+NCM_API int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* codebooks,
+                                const float* sqnorms, int32_t L, int32_t* codes_host, uint16_t* recon_host,
+                                int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
 /* Area pooling by an integer factor (F.interpolate mode="area" with T % factor == 0,
  * vq_forward_semantics.md:67,80): y[b,j,:] = (sum_{i<factor} x[b,j*factor+i,:]) / factor,
  * summed in increasing i in f32. x [B,T,D] f32, y [B,T/factor,D] f32. */

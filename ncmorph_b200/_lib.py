@@ -105,6 +105,7 @@ SIGNATURES: dict[str, list] = {
     "ncm_code_sqnorm": [c_vp, c_vp, c_vp, c_i64, c_i64, c_vp],
     "ncm_rvq_level": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_rvq_encode": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_rvq_encode_host": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_pool_avg": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_rvq_decode": [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_rms_norm_bf16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp],

@@ -148,6 +148,29 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
   return NCM_OK;
 }
 
+// L levels over bf16 rows x with every buffer supplied: resid (f32 [N,D]),
+// shadow (bf16 [N,D]), part (split partials). The last level updates resid
+// only when keep_resid.
+static int rvq_encode_core(ncm_ctx* ctx, const uint16_t* x, const uint16_t* codebooks, const float* sqnorms, int L,
+                           int32_t* codes, uint16_t* recon, float* resid, bool keep_resid, uint16_t* shadow,
+                           RvqPartial* part, const RvqPlan& plan, int64_t N, int64_t D, int64_t K,
+                           cudaStream_t st) {
+  for (int l = 0; l < L; ++l) {
+    const bool last = (l == L - 1);
+    const bool update = !last || keep_resid;
+    const uint16_t* a = (l == 0) ? x : shadow;
+    int rc = rvq_level_core(ctx, a, l == 0 ? x : nullptr, resid, last ? nullptr : shadow,
+                            codebooks + static_cast<size_t>(l) * K * D, sqnorms + static_cast<size_t>(l) * K,
+                            codes + static_cast<size_t>(l) * N, part, plan, N, D, K, update, st);
+    if (rc) return rc;
+  }
+  if (recon != nullptr) {
+    Launch _launch(ctx, KID_DECODE, st);
+    NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+  }
+  return NCM_OK;
+}
+
 }  // namespace ncm
 
 using namespace ncm;
@@ -205,6 +228,13 @@ int ncm_ctx_destroy(ncm_ctx_t* ctx) {
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
+  if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+  if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
+  for (int i = 0; i < 2; ++i) {
+    if (ctx->ev_in[i]) cudaEventDestroy(ctx->ev_in[i]);
+    if (ctx->ev_done[i]) cudaEventDestroy(ctx->ev_done[i]);
+    if (ctx->ev_out[i]) cudaEventDestroy(ctx->ev_out[i]);
+  }
   delete ctx;
   return NCM_OK;
 }
@@ -418,9 +448,6 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
   const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * K * L);
   uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_encode: workspace allocation failed");
-  uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
-  float* resid = residual_out ? residual_out : reinterpret_cast<float*>(ws + o_res);
-  RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
   if (sqnorms == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
     {
@@ -429,20 +456,92 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
     }
     sqnorms = sq;
   }
-  for (int l = 0; l < L; ++l) {
-    const bool last = (l == L - 1);
-    const bool update = !last || residual_out != nullptr;
-    const uint16_t* a = (l == 0) ? x : shadow;
-    rc = rvq_level_core(ctx, a, l == 0 ? x : nullptr, resid, last ? nullptr : shadow,
-                        codebooks + static_cast<size_t>(l) * K * D, sqnorms + static_cast<size_t>(l) * K,
-                        codes + static_cast<size_t>(l) * N, part, plan, N, D, K, update, st);
-    if (rc) return rc;
+  return rvq_encode_core(ctx, x, codebooks, sqnorms, L, codes, recon,
+                         residual_out ? residual_out : reinterpret_cast<float*>(ws + o_res), residual_out != nullptr,
+                         reinterpret_cast<uint16_t*>(ws + o_sh), reinterpret_cast<RvqPartial*>(ws + o_part), plan, N,
+                         D, K, st);
+}
+
+int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* codebooks, const float* sqnorms,
+                        int32_t L, int32_t* codes_host, uint16_t* recon_host, int64_t N, int64_t D, int64_t K,
+                        ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_rvq_shape(N, D, K))) return rc;
+  if (L <= 0 || L > 64) return ncm_fail(NCM_EINVAL, "rvq_encode_host: L=%d must be in [1,64]", L);
+  if (!x_host || !codebooks || !codes_host) return ncm_fail(NCM_EINVAL, "rvq_encode_host: null buffer");
+  if (!aligned16(codebooks) || (sqnorms && !aligned16(sqnorms)))
+    return ncm_fail(NCM_EINVAL, "rvq_encode_host: device buffers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Row chunks of about seven full waves of 128-row blocks, so chunking adds
+  // no wave-quantisation loss; two slots of device buffers alternate.
+  const int64_t wave_rows = static_cast<int64_t>(ctx->num_sms) * 128 * 7;
+  const int64_t nchunks = std::max<int64_t>(1, std::min<int64_t>(16, (N + wave_rows - 1) / wave_rows));
+  const int64_t C = ((N + nchunks - 1) / nchunks + 127) / 128 * 128;
+  const RvqPlan plan_c = rvq_plan(ctx->num_sms, C, K);
+  size_t part_bytes = plan_c.partial_bytes;
+  const int64_t last_rows = N - (nchunks - 1) * C;
+  if (last_rows > 0) part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, last_rows, K).partial_bytes);
+  WsCarver cv;
+  size_t o_x[2], o_codes[2], o_rec[2];
+  for (int i = 0; i < 2; ++i) {
+    o_x[i] = cv.take(2 * C * D);
+    o_codes[i] = cv.take(sizeof(int32_t) * L * C);
+    o_rec[i] = recon_host ? cv.take(2 * C * D) : 0;
   }
-  if (recon != nullptr) {
-    Launch _launch(ctx, KID_DECODE, st);
-    NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+  const size_t o_res = cv.take(sizeof(float) * C * D);
+  const size_t o_sh = cv.take(2 * C * D);
+  const size_t o_part = cv.take(part_bytes);
+  const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * K * L);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_encode_host: workspace allocation failed");
+  if (ctx->copy_in == nullptr) {
+    NCM_CUDA_TRY(cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking));
+    NCM_CUDA_TRY(cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+      NCM_CUDA_TRY(cudaEventCreateWithFlags(&ctx->ev_in[i], cudaEventDisableTiming));
+      NCM_CUDA_TRY(cudaEventCreateWithFlags(&ctx->ev_done[i], cudaEventDisableTiming));
+      NCM_CUDA_TRY(cudaEventCreateWithFlags(&ctx->ev_out[i], cudaEventDisableTiming));
+    }
   }
-  return NCM_OK;
+  if (sqnorms == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    Launch _launch(ctx, KID_SQNORM, st);
+    NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, K * L, D, st));
+    sqnorms = sq;
+  }
+  float* resid = reinterpret_cast<float*>(ws + o_res);
+  uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
+  RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int slot = static_cast<int>(c & 1);
+    const int64_t r0 = c * C;
+    const int64_t n = std::min(C, N - r0);
+    if (n <= 0) break;
+    uint16_t* xd = reinterpret_cast<uint16_t*>(ws + o_x[slot]);
+    int32_t* cd = reinterpret_cast<int32_t*>(ws + o_codes[slot]);
+    uint16_t* rd = recon_host ? reinterpret_cast<uint16_t*>(ws + o_rec[slot]) : nullptr;
+    // rows in: the slot's previous chunk must be done computing
+    if (c >= 2) NCM_CUDA_TRY(cudaStreamWaitEvent(ctx->copy_in, ctx->ev_done[slot], 0));
+    NCM_CUDA_TRY(cudaMemcpyAsync(xd, x_host + r0 * D, 2 * n * D, cudaMemcpyHostToDevice, ctx->copy_in));
+    NCM_CUDA_TRY(cudaEventRecord(ctx->ev_in[slot], ctx->copy_in));
+    // compute: rows landed, and the slot's previous results are copied out
+    NCM_CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[slot], 0));
+    if (c >= 2) NCM_CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_out[slot], 0));
+    const RvqPlan plan = rvq_plan(ctx->num_sms, n, K);
+    if ((rc = rvq_encode_core(ctx, xd, codebooks, sqnorms, L, cd, rd, resid, false, shadow, part, plan, n, D, K, st)))
+      return rc;
+    NCM_CUDA_TRY(cudaEventRecord(ctx->ev_done[slot], st));
+    // results out
+    NCM_CUDA_TRY(cudaStreamWaitEvent(ctx->copy_out, ctx->ev_done[slot], 0));
+    NCM_CUDA_TRY(cudaMemcpy2DAsync(codes_host + r0, sizeof(int32_t) * N, cd, sizeof(int32_t) * n,
+                                   sizeof(int32_t) * n, L, cudaMemcpyDeviceToHost, ctx->copy_out));
+    if (recon_host)
+      NCM_CUDA_TRY(cudaMemcpyAsync(recon_host + r0 * D, rd, 2 * n * D, cudaMemcpyDeviceToHost, ctx->copy_out));
+    NCM_CUDA_TRY(cudaEventRecord(ctx->ev_out[slot], ctx->copy_out));
+  }
+  NCM_CUDA_TRY(cudaStreamSynchronize(ctx->copy_out));
+  return ncm_sync(ctx, stream);
 }
 
 int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, int64_t T, int64_t D, int32_t factor,

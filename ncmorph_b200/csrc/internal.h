@@ -47,6 +47,12 @@ struct ncm_ctx {
   void* h_stage = nullptr;
   size_t h_stage_bytes = 0;
   ncm::ProfState prof;
+  // copy streams and events of the host-buffer pipeline (created on first use)
+  cudaStream_t copy_in = nullptr;
+  cudaStream_t copy_out = nullptr;
+  cudaEvent_t ev_in[2] = {nullptr, nullptr};
+  cudaEvent_t ev_done[2] = {nullptr, nullptr};
+  cudaEvent_t ev_out[2] = {nullptr, nullptr};
 };
 
 namespace ncm {

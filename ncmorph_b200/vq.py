@@ -81,6 +81,35 @@ def rvq_encode(x: torch.Tensor, codebooks: torch.Tensor, sqnorms: torch.Tensor |
     return codes, recon, residual
 
 
+def rvq_encode_host(x_host: torch.Tensor, codebooks: torch.Tensor, sqnorms: torch.Tensor | None = None, *,
+                    codes_host: torch.Tensor | None = None, recon_host: torch.Tensor | None = None,
+                    want_recon: bool = True):
+    """Host-buffer encode: x_host [N, D] bf16 in host memory (pin it for full
+    copy speed), codebooks [L, K, D] on the device. Copies and compute are
+    pipelined in row chunks inside the library; returns host tensors
+    (codes [L, N] int32, recon [N, D] bf16 or None) once they are filled."""
+    if x_host.is_cuda or not x_host.is_contiguous() or x_host.dtype != bf16:
+        raise ValueError("x_host must be a contiguous bf16 CPU tensor")
+    N, D = x_host.shape
+    L, K, D2 = codebooks.shape
+    if D2 != D:
+        raise ValueError("codebook width differs from x")
+    need(codebooks, bf16, "codebooks")
+    if sqnorms is not None:
+        need(sqnorms, torch.float32, "sqnorms", (L, K))
+    if codes_host is None:
+        codes_host = torch.empty((L, N), dtype=torch.int32, pin_memory=x_host.is_pinned())
+    if want_recon and recon_host is None:
+        recon_host = torch.empty((N, D), dtype=bf16, pin_memory=x_host.is_pinned())
+    for t, name in ((codes_host, "codes_host"), (recon_host, "recon_host")):
+        if t is not None and (t.is_cuda or not t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous CPU tensor")
+    dev = codebooks.device
+    _lib.call("ncm_rvq_encode_host", context(dev), ptr(x_host), ptr(codebooks), ptr(sqnorms), L, ptr(codes_host),
+              ptr(recon_host), N, D, K, stream_of(codebooks))
+    return codes_host, recon_host
+
+
 def rvq_decode(codes: torch.Tensor, codebooks: torch.Tensor) -> torch.Tensor:
     """recon[n] = bf16(sum_l e_l[codes[l, n]]) (R5)."""
     L, N = codes.shape

@@ -109,6 +109,25 @@ def test_fused_update_path_matches_oracle(orc, cuda_dev, N, D, K, L):
     assert np.array_equal(rd.cpu().numpy(), r)
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_pipelined_encode_matches_device_encode(cuda_dev, pinned):
+    """ncm_rvq_encode_host over several row chunks equals ncm_rvq_encode bit for bit."""
+    from ncmorph_b200 import vq
+    N, D, K, L = 300_000, 64, 256, 2   # > 2 chunks of ~7 waves of 128-row blocks
+    g = torch.Generator(device=cuda_dev).manual_seed(4)
+    x = torch.randn((N, D), generator=g, device=cuda_dev).to(torch.bfloat16)
+    cbs = (torch.randn((L, K, D), generator=g, device=cuda_dev)).to(torch.bfloat16)
+    codes_d, recon_d, _ = vq.rvq_encode(x, cbs)
+    x_host = x.cpu()
+    if pinned:
+        x_host = x_host.pin_memory()
+    codes_h, recon_h = vq.rvq_encode_host(x_host, cbs)
+    assert torch.equal(codes_h, codes_d.cpu())
+    assert torch.equal(recon_h.view(torch.int16), recon_d.cpu().view(torch.int16))
+    codes_only, none = vq.rvq_encode_host(x_host, cbs, want_recon=False)
+    assert none is None and torch.equal(codes_only, codes_d.cpu())
+
+
 def test_decode_rejects_out_of_range_codes(cuda_dev):
     from ncmorph_b200 import _lib, device, vq
     cbs = torch.zeros((2, 16, 8), dtype=torch.bfloat16, device=cuda_dev)
