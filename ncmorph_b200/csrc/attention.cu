@@ -303,30 +303,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const uint32_t sbase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + b * AT_K + hf * HK;
       const int k0 = t * AT_K + hf * HK;
       const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + HK <= hi);
-      // pass 1: max of this warp's 64 raw bf16 scores per row
+      // pass 1: max of this warp's 64 raw scores per row (rounding to bf16 is
+      // monotonic, so the max of the rounded scores is the rounded max); in a
+      // tile the mask touches, disallowed scores become -inf in TMEM first
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < HK; c += 32) {
         uint32_t v[32];
         tmem_ld_x32(sbase + c, v);
         tmem_wait_ld();
-        if (unmasked) {
+        if (!unmasked) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-            mx0 = fmaxf(mx0, bf16lo(pr));
-            mx1 = fmaxf(mx1, bf16hi(pr));
-          }
-        } else {
+          for (int i = 0; i < 32; ++i)
+            if (!key_allowed(k0 + c + i, Pq, lo, hi, args.pad_mask)) v[i] = __float_as_uint(-INFINITY);
+          tmem_st_x32(sbase + c, v);
+        }
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-            const int ka = k0 + c + i;
-            mx0 = fmaxf(mx0, key_allowed(ka, Pq, lo, hi, args.pad_mask) ? bf16lo(pr) : -INFINITY);
-            mx1 = fmaxf(mx1, key_allowed(ka + 1, Pq, lo, hi, args.pad_mask) ? bf16hi(pr) : -INFINITY);
-          }
+        for (int i = 0; i < 32; i += 2) {
+          mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+          mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
         }
       }
+      if (!unmasked) tmem_wait_st();
       // swap partial maxima with the partner warp (same rows, other key half)
       S.mx[b][hf][row] = fmaxf(mx0, mx1);
       __syncwarp();
@@ -335,7 +333,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         ok = false;
         break;
       }
-      const float mt = fmaxf(S.mx[b][0][row], S.mx[b][1][row]) * c_scale;
+      const float raw_max = fmaxf(S.mx[b][0][row], S.mx[b][1][row]);
+      const float mt = bf16lo(cvt_bf16x2(raw_max, 0.f)) * c_scale;
       const float m_new = fmaxf(m, mt);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m - m_use);  // m = -inf -> 0
@@ -344,7 +343,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         ok = false;
         break;
       }
-      float rs0 = 0.f, rs1 = 0.f;
+      // pass 2: t = bf16(s) * scale*log2e - m, p = 2^t, packed f32x2 arithmetic
+      const unsigned long long cs2 = f2_pack(c_scale, c_scale), nm2 = f2_pack(-m_use, -m_use);
+      unsigned long long rs2 = f2_pack(0.f, 0.f);
       uint8_t* prow = S.p[b][hf] + row * 128;
 #pragma unroll 1
       for (int c = 0; c < HK; c += 32) {
@@ -359,21 +360,19 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           for (int e = 0; e < 4; ++e) {
             const int i = q4 * 8 + e * 2;
             const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-            float t0 = fmaf(bf16lo(pr), c_scale, -m_use), t1 = fmaf(bf16hi(pr), c_scale, -m_use);
-            if (!unmasked) {
-              const int ka = k0 + c + i;
-              t0 = key_allowed(ka, Pq, lo, hi, args.pad_mask) ? t0 : -INFINITY;
-              t1 = key_allowed(ka + 1, Pq, lo, hi, args.pad_mask) ? t1 : -INFINITY;
-            }
+            const unsigned long long t2 = f2_fma(f2_pack(bf16lo(pr), bf16hi(pr)), cs2, nm2);
+            float t0, t1;
+            f2_unpack(t2, t0, t1);
             const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
             w4[e] = cvt_bf16x2(p0, p1);
-            rs0 += p0;
-            rs1 += p1;
+            rs2 = f2_add(rs2, f2_pack(p0, p1));
           }
           const int sw = (ch0 + q4) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
           *reinterpret_cast<uint4*>(prow + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
+      float rs0, rs1;
+      f2_unpack(rs2, rs0, rs1);
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
@@ -397,8 +396,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.o_empty[bo]);
+        const unsigned long long ap2 = f2_pack(alpha_prev, alpha_prev);
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
+        for (int i = 0; i < HD; i += 2) {
+          const unsigned long long r2 =
+              f2_fma(f2_pack(o[i], o[i + 1]), ap2, f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
+          f2_unpack(r2, o[i], o[i + 1]);
+        }
       }
       alpha_prev = alpha;
       ++j;
