@@ -53,6 +53,8 @@ struct LinearArgs {
   int tiles_a, tiles_b;  // tiles along the 128-row operand and the BN operand
   int a_fast;            // raster: 1 = consecutive tiles walk the A-operand tiles
   int vec_ok;            // y rows are 16-byte aligned (N % 8 == 0)
+  int mode;              // 0 plain, 1 SwiGLU (y[M,F]), 2 residual add into y
+  int F;                 // SwiGLU width (mode 1): gate rows [0,F), up rows [F,2F) of W
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& ta, int& tb) {
@@ -123,7 +125,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_BYTES);
           tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, ta * BM);
-          tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * BN);
+          if (args.mode == 1) {
+            // gate rows and the matching up rows side by side in one tile
+            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * (BN / 2));
+            tma_load_2d(&tmB, &S.full[stage], S.b[stage] + (BN / 2) * BK * 2, kc * BK, args.F + tb * (BN / 2));
+          } else {
+            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * BN);
+          }
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -201,6 +209,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
       const int arow = ta * BM + q * 32 + lane;  // row of the 128-row operand this thread owns
+      if (!SWAP && args.mode == 1) {
+        // SwiGLU (decoder.zig:205-210): y = bf16(bf16(silu(bf16(g))) * bf16(u))
+        const int m = arow;
+        const int n0 = tb * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld_x16(tbase + c, g);
+          tmem_ld_x16(tbase + BN / 2 + c, u);
+          tmem_wait_ld();
+          if (m < args.M) {
+            uint32_t w8[8];
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              const uint32_t gp = cvt_bf16x2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]));
+              const uint32_t up = cvt_bf16x2(__uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+              const float g0 = bf16lo(gp), g1 = bf16hi(gp);
+              // silu(g) = g / (1 + e^-g), e^-g = 2^(-g log2 e)
+              const float s0 = __fdividef(g0, 1.0f + ex2_approx(-1.4426950408889634f * g0));
+              const float s1 = __fdividef(g1, 1.0f + ex2_approx(-1.4426950408889634f * g1));
+              const uint32_t sp = cvt_bf16x2(s0, s1);
+              w8[j / 2] = cvt_bf16x2(bf16lo(sp) * bf16lo(up), bf16hi(sp) * bf16hi(up));
+            }
+            uint16_t* dst = args.y + static_cast<size_t>(m) * args.F + n0 + c;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+            *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          }
+        }
+      } else
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         uint32_t v[16];
@@ -220,19 +257,41 @@ __global__ void __launch_bounds__(THREADS, 1)
               f[j] = acc;
             }
             const size_t o = static_cast<size_t>(m) * args.N + n0;
+            if (args.mode == 2) {
+              // residual add (decoder.zig:310-313): y = bf16(y + bf16(acc + bias))
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                const uint32_t r = cvt_bf16x2(f[j], f[j + 1]);
+                f[j] = bf16lo(r);
+                f[j + 1] = bf16hi(r);
+              }
+              if (args.vec_ok && n0 + 16 <= args.N) {
+                const uint4 h0 = *reinterpret_cast<const uint4*>(args.y + o);
+                const uint4 h1 = *reinterpret_cast<const uint4*>(args.y + o + 8);
+                const uint32_t hp[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  f[2 * j] += bf16lo(hp[j]);
+                  f[2 * j + 1] += bf16hi(hp[j]);
+                }
+              } else {
+                for (int j = 0; j < 16; ++j)
+                  if (n0 + j < args.N) f[j] += bf16_to_f32(args.y[o + j]);
+              }
+            }
             if (args.y_f32 != nullptr) {
               for (int j = 0; j < 16; ++j)
                 if (n0 + j < args.N) args.y_f32[o + j] = f[j];
             } else if (args.vec_ok && n0 + 16 <= args.N) {
               uint4 w0, w1;
-              w0.x = pack_bf16x2(f[0], f[1]);
-              w0.y = pack_bf16x2(f[2], f[3]);
-              w0.z = pack_bf16x2(f[4], f[5]);
-              w0.w = pack_bf16x2(f[6], f[7]);
-              w1.x = pack_bf16x2(f[8], f[9]);
-              w1.y = pack_bf16x2(f[10], f[11]);
-              w1.z = pack_bf16x2(f[12], f[13]);
-              w1.w = pack_bf16x2(f[14], f[15]);
+              w0.x = cvt_bf16x2(f[0], f[1]);
+              w0.y = cvt_bf16x2(f[2], f[3]);
+              w0.z = cvt_bf16x2(f[4], f[5]);
+              w0.w = cvt_bf16x2(f[6], f[7]);
+              w1.x = cvt_bf16x2(f[8], f[9]);
+              w1.y = cvt_bf16x2(f[10], f[11]);
+              w1.z = cvt_bf16x2(f[12], f[13]);
+              w1.w = cvt_bf16x2(f[14], f[15]);
               *reinterpret_cast<uint4*>(args.y + o) = w0;
               *reinterpret_cast<uint4*>(args.y + o + 8) = w1;
             } else {
@@ -249,8 +308,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < 16; ++j) {
               const int m = tb * BN + c + j;
               if (m < args.M) {
-                const float acc = __uint_as_float(v[j]) + bv;
+                float acc = __uint_as_float(v[j]) + bv;
                 const size_t o = static_cast<size_t>(m) * args.N + n;
+                if (args.mode == 2) acc = bf16_to_f32(f32_to_bf16(acc)) + bf16_to_f32(args.y[o]);
                 if (args.y_f32 != nullptr)
                   args.y_f32[o] = acc;
                 else
@@ -303,7 +363,16 @@ cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
 
 int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, float* y_f32,
                 int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
+  return linear_bf16_ex(ctx, x, w, bias, y, y_f32, M, K, N, stream, 0, 0);
+}
+
+int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                   float* y_f32, int64_t M, int64_t K, int64_t N, cudaStream_t stream, int mode, int64_t F) {
+  if (mode == 1 && (M <= 64 || F % 128 != 0 || N != 2 * F))
+    return ncm_fail(NCM_EINVAL, "linear: fused SwiGLU needs M > 64, F %% 128 == 0, N == 2F");
   LinearArgs a{};
+  a.mode = mode;
+  a.F = static_cast<int>(F);
   a.bias = bias;
   a.y = y;
   a.y_f32 = y_f32;
@@ -326,17 +395,18 @@ int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16
   } else {
     const long long mt = ceil_div(M, BM);
     const int sms = ctx->num_sms;
-    if (mt * ceil_div(N, 256) >= sms)
+    if (mode == 1 || mt * ceil_div(N, 256) >= sms)
       bn = 256;
     else if (mt * ceil_div(N, 128) >= sms)
       bn = 128;
     else
       bn = 64;
-    if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, bn))
+    // SwiGLU tiles are two 128-row boxes (gate rows, up rows) of W
+    if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, mode == 1 ? bn / 2 : bn))
       return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
                       (long long)K, (long long)N);
     a.tiles_a = static_cast<int>(mt);
-    a.tiles_b = ceil_div(N, bn);
+    a.tiles_b = mode == 1 ? static_cast<int>(F / (bn / 2)) : ceil_div(N, bn);
     // Keep the smaller operand L2-resident: walk the tiles of the larger one
     // slowly, so concurrently running CTAs share its tile.
     const double a_bytes = double(M) * K * 2, b_bytes = double(N) * K * 2;

@@ -53,6 +53,12 @@ struct ncm_ctx {
   cudaEvent_t ev_in[2] = {nullptr, nullptr};
   cudaEvent_t ev_done[2] = {nullptr, nullptr};
   cudaEvent_t ev_out[2] = {nullptr, nullptr};
+  // RoPE tables and per-row levels of the last NCM forward configuration
+  uint64_t rope_key = 0;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  int* rope_row_level = nullptr;
+  int64_t rope_rows = 0;
 };
 
 namespace ncm {
@@ -167,5 +173,11 @@ cudaError_t launch_bf16_to_f32(const uint16_t* x, float* y, int64_t n, cudaStrea
 // accumulator (+bias) is written there instead of the bf16 output.
 int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, float* y_f32,
                 int64_t M, int64_t K, int64_t N, cudaStream_t stream);
+// Epilogue variants of the same GEMM. mode 1: SwiGLU — w is [2F, K] (gate rows,
+// then up rows), y [M, F] = bf16(bf16(silu(bf16(g))) * bf16(u)); needs M > 64
+// and F % 128 == 0. mode 2: residual — y [M, N] is read and overwritten with
+// bf16(y + bf16(x.w^T + bias)).
+int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
+                   float* y_f32, int64_t M, int64_t K, int64_t N, cudaStream_t stream, int mode, int64_t F);
 
 }  // namespace ncm

@@ -141,8 +141,8 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   WsCarver cv;
   const size_t o_h = cv.take(2 * T * Hd), o_n = cv.take(2 * T * Hd), o_qkv = cv.take(2 * T * QKV);
   const size_t o_vt = cv.take(2 * T * Hkv * 64), o_ctx = cv.take(2 * T * H * 64), o_a = cv.take(2 * T * Hd);
-  const size_t o_gu = cv.take(2 * T * 2 * F), o_act = cv.take(2 * T * F);
-  const size_t o_cos = cv.take(4 * T * 64), o_sin = cv.take(4 * T * 64), o_lv = cv.take(4 * T);
+  const bool fused_swiglu = T > 64 && F % 128 == 0;
+  const size_t o_gu = fused_swiglu ? 0 : cv.take(2 * T * 2 * F), o_act = cv.take(2 * T * F);
   uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "ncm_forward: workspace allocation failed");
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
@@ -150,28 +150,51 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   uint16_t* qkv = reinterpret_cast<uint16_t*>(ws + o_qkv);
   uint16_t* vt = reinterpret_cast<uint16_t*>(ws + o_vt);
   uint16_t* ctxb = reinterpret_cast<uint16_t*>(ws + o_ctx);
-  uint16_t* a = reinterpret_cast<uint16_t*>(ws + o_a);
   uint16_t* gu = reinterpret_cast<uint16_t*>(ws + o_gu);
   uint16_t* act = reinterpret_cast<uint16_t*>(ws + o_act);
-  float* cosd = reinterpret_cast<float*>(ws + o_cos);
-  float* sind = reinterpret_cast<float*>(ws + o_sin);
-  int* row_level = reinterpret_cast<int*>(ws + o_lv);
+  (void)o_a;
 
-  // positions restart at 0 per level (ncm_position.fill_level_positions), RoPE tables on the host
-  std::vector<int> pos(T), lev(T);
-  {
+  // RoPE tables at per-level restarting positions (ncm_position.fill_level_positions)
+  // and each row's level: built on the host once per configuration and kept
+  // on the device, so repeated forwards do no host work or synchronisation.
+  uint64_t key = 1469598103934665603ull;
+  auto mix = [&key](uint64_t v) { key = (key ^ v) * 1099511628211ull; };
+  mix(static_cast<uint64_t>(T));
+  uint32_t theta_bits;
+  std::memcpy(&theta_bits, &cfg->rope_theta, 4);
+  mix(theta_bits);
+  mix(static_cast<uint64_t>(m.prefix_length));
+  mix(static_cast<uint64_t>(cfg->use_level_encoding));
+  for (int i = 0; i < m.num_levels; ++i) mix(static_cast<uint64_t>(m.level_lengths[i]));
+  if (key != ctx->rope_key || ctx->rope_cos == nullptr) {
+    std::vector<int> pos(T), lev(T);
     int64_t t = 0;
     for (; t < m.prefix_length; ++t) pos[t] = static_cast<int>(t), lev[t] = -1;
     for (int i = 0; i < m.num_levels; ++i)
       for (int p = 0; p < m.level_lengths[i]; ++p, ++t) pos[t] = p, lev[t] = cfg->use_level_encoding ? i : -1;
+    std::vector<float> ch(T * 64), sh(T * 64);
+    rope_tables_host(64, cfg->rope_theta, pos.data(), static_cast<int>(T), ch.data(), sh.data());
+    NCM_CUDA_TRY(cudaStreamSynchronize(st));  // no forward in flight still reads the old tables
+    if (T > ctx->rope_rows) {
+      cudaFree(ctx->rope_cos);
+      cudaFree(ctx->rope_sin);
+      cudaFree(ctx->rope_row_level);
+      ctx->rope_cos = ctx->rope_sin = nullptr;
+      ctx->rope_row_level = nullptr;
+      ctx->rope_rows = 0;
+      NCM_CUDA_TRY(cudaMalloc(&ctx->rope_cos, 4 * T * 64));
+      NCM_CUDA_TRY(cudaMalloc(&ctx->rope_sin, 4 * T * 64));
+      NCM_CUDA_TRY(cudaMalloc(&ctx->rope_row_level, 4 * T));
+      ctx->rope_rows = T;
+    }
+    NCM_CUDA_TRY(cudaMemcpy(ctx->rope_cos, ch.data(), 4 * T * 64, cudaMemcpyHostToDevice));
+    NCM_CUDA_TRY(cudaMemcpy(ctx->rope_sin, sh.data(), 4 * T * 64, cudaMemcpyHostToDevice));
+    NCM_CUDA_TRY(cudaMemcpy(ctx->rope_row_level, lev.data(), 4 * T, cudaMemcpyHostToDevice));
+    ctx->rope_key = key;
   }
-  std::vector<float> ch(T * 64), sh(T * 64);
-  rope_tables_host(64, cfg->rope_theta, pos.data(), static_cast<int>(T), ch.data(), sh.data());
-  NCM_CUDA_TRY(cudaMemcpyAsync(cosd, ch.data(), 4 * T * 64, cudaMemcpyHostToDevice, st));
-  NCM_CUDA_TRY(cudaMemcpyAsync(sind, sh.data(), 4 * T * 64, cudaMemcpyHostToDevice, st));
-  NCM_CUDA_TRY(cudaMemcpyAsync(row_level, lev.data(), 4 * T, cudaMemcpyHostToDevice, st));
-  // the host vectors must outlive the asynchronous copies
-  NCM_CUDA_TRY(cudaStreamSynchronize(st));
+  const float* cosd = ctx->rope_cos;
+  const float* sind = ctx->rope_sin;
+  const int* row_level = ctx->rope_row_level;
 
   const int Ti = static_cast<int>(T);
   const float eps = cfg->rms_norm_epsilon;
@@ -199,22 +222,23 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
                                m.level_lengths, m.num_levels, st)))
         return rc;
     }
-    if ((rc = linear_bf16(ctx, ctxb, L.o, L.o_bias, a, nullptr, T, static_cast<int64_t>(H) * 64, Hd, st))) return rc;
+    // h = bf16(h + bf16(ctx . O^T + b)) in the projection's epilogue
+    if ((rc = linear_bf16_ex(ctx, ctxb, L.o, L.o_bias, h, nullptr, T, static_cast<int64_t>(H) * 64, Hd, st, 2, 0)))
+      return rc;
     {
       Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
-      NCM_CUDA_TRY(launch_add_bf16(h, a, T * Hd, st));
       NCM_CUDA_TRY(launch_rms_norm_bf16(h, L.ln_2, nullptr, nrm, Ti, static_cast<int>(Hd), eps, st));
     }
-    if ((rc = linear_bf16(ctx, nrm, L.gate_up, nullptr, gu, nullptr, T, Hd, 2 * F, st))) return rc;
-    {
+    if (fused_swiglu) {
+      // act = bf16(bf16(silu(g)) * u) straight from the gate|up projection's epilogue
+      if ((rc = linear_bf16_ex(ctx, nrm, L.gate_up, nullptr, act, nullptr, T, Hd, 2 * F, st, 1, F))) return rc;
+    } else {
+      if ((rc = linear_bf16(ctx, nrm, L.gate_up, nullptr, gu, nullptr, T, Hd, 2 * F, st))) return rc;
       Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
       NCM_CUDA_TRY(launch_silu_mul_bf16(gu, act, Ti, static_cast<int>(F), st));
     }
-    if ((rc = linear_bf16(ctx, act, L.down, nullptr, a, nullptr, T, F, Hd, st))) return rc;
-    {
-      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
-      NCM_CUDA_TRY(launch_add_bf16(h, a, T * Hd, st));
-    }
+    // h = bf16(h + bf16(act . down^T)) in the projection's epilogue
+    if ((rc = linear_bf16_ex(ctx, act, L.down, nullptr, h, nullptr, T, F, Hd, st, 2, 0))) return rc;
   }
   Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
   NCM_CUDA_TRY(launch_rms_norm_bf16(h, W->final_norm, W->final_norm_bias, out, Ti, static_cast<int>(Hd), eps, st));
