@@ -46,6 +46,8 @@ def parse_args():
     p.add_argument("--codes", type=int, default=16384)
     p.add_argument("--cpu-rows", type=int, default=2048, help="rows per CPU-baseline sample")
     p.add_argument("--seed", type=int, default=20260)
+    p.add_argument("--graph", action="store_true",
+                   help="secondary workloads: replay one captured CUDA graph per step")
     p.add_argument("--workload", choices=["rvq", "tokenizer", "linear", "decoder"], default="rvq",
                    help="rvq = BASELINE config 5 (the headline); tokenizer = config 2; linear = config 3 sweep; "
                         "decoder = config 4")
@@ -358,6 +360,21 @@ def _timed_loop(fn, steps, warmup):
     return e0.elapsed_time(e1) / max(steps, 1)
 
 
+def _graphed(fn, enabled):
+    """Returns fn itself, or a replay of one CUDA-graph capture of fn (after a
+    warm-up call, the library's calls allocate nothing and do no host sync)."""
+    import torch
+    if not enabled:
+        return fn
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g.replay
+
+
 def _profile(lib, ctx, names):
     import ctypes
     out = {}
@@ -402,11 +419,14 @@ def run_secondary(a):
         _timed_loop(step, 0, a.warmup)
         lib.ncm_profile_read(ctx, b"*", None, None)
         lib.ncm_profile_enable(ctx, 1)
-        sampler.start()
-        ms = _timed_loop(step, a.steps, 0)
-        clocks = sampler.stop()
+        _timed_loop(step, a.steps, 0)      # per-kernel breakdown (eager launches)
         lib.ncm_profile_enable(ctx, 0)
-        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "*"])
+        run = _graphed(step, a.graph)
+        _timed_loop(run, 0, a.warmup)
+        sampler.start()
+        ms = _timed_loop(run, a.steps, 0)
+        clocks = sampler.stop()
+        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "rvq_apply", "pool_avg", "scale_update", "cast", "*"])
         rows = sum(B * T // f for f in factors)
         dist_flops = 2.0 * rows * K * D * L
         proj_flops = 2 * 2.0 * B * T * Din * D
@@ -425,7 +445,7 @@ def run_secondary(a):
         achieved = dist_flops / (am_ms / a.steps * 1e-3) / 1e12
         line.update({
             "metric": "tokenizer_vectors_per_s", "value": B * T / (ms * 1e-3), "unit": "vectors/s",
-            "ms_per_step": ms,
+            "ms_per_step": ms, "cuda_graph": bool(a.graph),
             "config": {"workload": "multiscale tokenizer forward (BASELINE config 2)", "batch": B, "seq_len": T,
                        "model_width": Din, "vq_width": D, "codebook_size": K, "levels_per_scale": L,
                        "pool_factors": factors, "rows_quantised": rows},
@@ -437,7 +457,8 @@ def run_secondary(a):
                          "peak_source": f"{peak_kind} bf16_tflops (burst; a 2-3 ms step)",
                          "argmin_ms_per_step": am_ms / a.steps, "linear_ms_per_step": ln_ms / a.steps,
                          "linear_tflops": proj_flops / (ln_ms / a.steps * 1e-3) / 1e12,
-                         "share_argmin": am_ms / max(prof["*"][0] + am_ms + ln_ms, 1e-9)},
+                         "share_argmin": am_ms / max(prof["*"][0] + am_ms + ln_ms, 1e-9),
+                         "ms_per_step_by_kernel": {k: v[0] / a.steps for k, v in prof.items()}},
             "gpu_launches": int(am_n + prof["linear_bf16"][1] + prof["*"][1]), "clocks": clocks})
     elif a.workload == "linear":
         Ms = [1, 64, 512, 4096, 8192]
@@ -500,10 +521,13 @@ def run_secondary(a):
         _timed_loop(step, 0, a.warmup)
         lib.ncm_profile_read(ctx, b"*", None, None)
         lib.ncm_profile_enable(ctx, 1)
-        sampler.start()
-        ms = _timed_loop(step, a.steps, 0)
-        clocks = sampler.stop()
+        _timed_loop(step, a.steps, 0)      # per-kernel breakdown (eager launches)
         lib.ncm_profile_enable(ctx, 0)
+        run = _graphed(step, a.graph)
+        _timed_loop(run, 0, a.warmup)
+        sampler.start()
+        ms = _timed_loop(run, a.steps, 0)
+        clocks = sampler.stop()
         prof = _profile(lib, ctx, ["linear_bf16", "attention", "*"])
         T = cfg.seq_len
         lin_flops = 16 * 2.0 * T * Hd * (3072 + 2048 + 3 * F) + 2.0 * T * cfg.vq_width * Hd
@@ -524,6 +548,7 @@ def run_secondary(a):
         lin_ach = lin_flops / (ln_ms / a.steps * 1e-3) / 1e12
         line.update({
             "metric": "decoder_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "cuda_graph": bool(a.graph),
             "config": {"workload": "NCM decoder forward (BASELINE config 4)", "layers": 16, "d_model": Hd,
                        "heads": 32, "kv_heads": 8, "head_dim": 64, "ffn": F, "positions": T,
                        "levels": lv, "mask": "block_causal", "flops_linear": lin_flops, "flops_attention": att_flops},

@@ -610,7 +610,8 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
   WsCarver cv;
   const size_t o_h = cv.take(2 * N * D);
   const size_t o_r = cv.take(sizeof(float) * N * D);
-  const size_t o_acc = cv.take(sizeof(float) * N * D);
+  size_t o_q[16];
+  for (int s = 0; s < S; ++s) o_q[s] = cv.take(sizeof(float) * (N / cfg->pool_factors[s]) * D);
   const size_t o_u = cv.take(sizeof(float) * max_rows * D);
   const size_t o_ub = cv.take(2 * max_rows * D);
   const size_t o_rb = recon ? 0 : cv.take(2 * N * D);
@@ -620,7 +621,8 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "tokenizer: workspace allocation failed");
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
   float* r = reinterpret_cast<float*>(ws + o_r);
-  float* acc = reinterpret_cast<float*>(ws + o_acc);
+  float* q[16];
+  for (int s = 0; s < S; ++s) q[s] = reinterpret_cast<float*>(ws + o_q[s]);
   float* u = reinterpret_cast<float*>(ws + o_u);
   uint16_t* ub = reinterpret_cast<uint16_t*>(ws + o_ub);
   uint16_t* rb = recon ? recon : reinterpret_cast<uint16_t*>(ws + o_rb);
@@ -633,39 +635,47 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
     }
     sqnorms = sq;
   }
-  // input projection, then the f32 residual
+  // input projection, then the f32 residual and the first scale's pooled rows
   rc = linear_bf16(ctx, x, w_in, b_in, h, nullptr, N, Din, D, st);
   if (rc) return rc;
   {
     Launch _launch(ctx, KID_CAST, st);
     NCM_CUDA_TRY(launch_bf16_to_f32(h, r, N * D, st));
   }
-  NCM_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(float) * N * D, st));
+  {
+    Launch _launch(ctx, KID_POOL, st);
+    NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, cfg->pool_factors[0], st));
+  }
   int32_t* codes_s = codes;
   for (int s = 0; s < S; ++s) {
     const int f = cfg->pool_factors[s];
     const int64_t rows = N / f;
     const RvqPlan plan = rvq_plan(ctx->num_sms, rows, K);
-    {
-      Launch _launch(ctx, KID_POOL, st);
-      NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, f, st));
-    }
     for (int l = 0; l < L; ++l) {
       const size_t cb_off = (static_cast<size_t>(s) * L + l) * K;
       rc = rvq_level_core(ctx, ub, nullptr, u, l == L - 1 ? nullptr : ub, codebooks + cb_off * D, sqnorms + cb_off,
                           codes_s + static_cast<size_t>(l) * rows, part, plan, rows, D, K, l != L - 1, st);
       if (rc) return rc;
     }
+    // q_s, and r -= up(q_s) with the next scale's pooling in the same pass
+    const bool next = s + 1 < S;
+    const int g = next ? cfg->pool_factors[s + 1] : 0;
+    const bool fused_pool = next && f % g == 0;
     {
       Launch _launch(ctx, KID_SCALE_UPDATE, st);
-      NCM_CUDA_TRY(launch_scale_update(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, acc, B, T, D, K,
-                                     f, ctx->d_err, st));
+      NCM_CUDA_TRY(launch_scale_advance(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, q[s], u, ub,
+                                        rows, D, K, f, fused_pool ? g : 0, next, ctx->d_err, st));
+    }
+    if (next && !fused_pool) {
+      Launch _launch(ctx, KID_POOL, st);
+      NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, g, st));
     }
     codes_s += static_cast<size_t>(L) * rows;
   }
   {
+    // recon = bf16(sum_s up(q_s)), scales in order
     Launch _launch(ctx, KID_CAST, st);
-    NCM_CUDA_TRY(launch_f32_to_bf16(acc, rb, N * D, st));
+    NCM_CUDA_TRY(launch_multiscale_recon(q, cfg->pool_factors, S, rb, N, D, st));
   }
   return linear_bf16(ctx, rb, w_out, b_out, y, nullptr, N, D, Din, st);
 }

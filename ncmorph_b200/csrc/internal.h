@@ -163,8 +163,16 @@ cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, i
                               float* recon_f32, int64_t N, int64_t D, int64_t K, int* err, cudaStream_t stream);
 cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t B, int64_t T, int64_t D, int f,
                             cudaStream_t stream);
-cudaError_t launch_scale_update(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* recon,
-                                int64_t B, int64_t T, int64_t D, int64_t K, int f, int* err, cudaStream_t stream);
+// Scale s of the multiscale driver: q_out[p] = sum_l e_l[codes[l,p]]; with
+// update_r also resid -= up(q) over the f rows of each pooled row, and when
+// g > 0 (the next scale's factor, dividing f) u_next (+ bf16 shadow) =
+// pool(resid, g) in the same pass.
+cudaError_t launch_scale_advance(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* q_out,
+                                 float* u_next, uint16_t* u_next_bf16, int64_t rows_pooled, int64_t D, int64_t K, int f,
+                                 int g, bool update_r, int* err, cudaStream_t stream);
+// out[t] = bf16(sum_s q[s][t / f[s]]) in scale order.
+cudaError_t launch_multiscale_recon(const float* const* q, const int* f, int S, uint16_t* out, int64_t rows, int64_t D,
+                                    cudaStream_t stream);
 cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* x, float* y, int64_t n, cudaStream_t stream);
 

@@ -511,49 +511,96 @@ __global__ void __launch_bounds__(256) pool_avg_kernel(const float* __restrict__
     *reinterpret_cast<uint2*>(y_bf16 + orow * D + d) = make_uint2(pack_bf16x2(s.x, s.y), pack_bf16x2(s.z, s.w));
 }
 
-// ------------------------------------------------------ scale update (R6)
-// For each pooled row p of one scale: q = sum_l e_l[codes[l,p]] (f32, level
-// order); then for the f full-resolution rows it covers: r -= q, recon += q.
-__global__ void __launch_bounds__(256) scale_update_kernel(const int32_t* __restrict__ codes,
-                                                           const uint16_t* __restrict__ cbs, int L,
-                                                           float* __restrict__ resid, float* __restrict__ recon,
-                                                           long long rows_pooled, int D, int K, int f, int* err) {
-  const long long p = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+// ------------------------------------------------- scale advance (R4+R6)
+// One warp per pooled row p of scale s (factor f): q = sum_l e_l[codes[l,p]]
+// (f32, level order) is stored to q_out[p]; when a next scale exists (factor
+// g dividing f) the f full-resolution rows get r -= q and are pooled on the
+// fly into u_next (same summation order as pool_avg_kernel) with its bf16
+// shadow. The residual is updated only when a next scale needs it.
+__global__ void __launch_bounds__(256) scale_advance_kernel(const int32_t* __restrict__ codes,
+                                                            const uint16_t* __restrict__ cbs, int L,
+                                                            float* __restrict__ resid, float* __restrict__ q_out,
+                                                            float* __restrict__ u_next,
+                                                            uint16_t* __restrict__ u_next_bf16, long long rows_pooled,
+                                                            int D, int K, int f, int g, int update_r, int* err) {
+  // one warp per (pooled row, 128-channel chunk)
+  const int nch = (D + 127) / 128;
+  const long long wg = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const long long p = wg / nch;
+  const int ch = static_cast<int>(wg - p * nch);
   const int lane = threadIdx.x & 31;
   if (p >= rows_pooled) return;
   for (int l = 0; l < L; ++l) {
     const int c = codes[static_cast<size_t>(l) * rows_pooled + p];
     if (c < 0 || c >= K) {
-      if (lane == 0) atomicOr(err, kErrBadIndex);
+      if (lane == 0 && ch == 0) atomicOr(err, kErrBadIndex);
       return;
     }
   }
-  for (int d = lane * 4; d < D; d += 128) {
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int l = 0; l < L; ++l) {
-      const int c = __ldg(codes + static_cast<size_t>(l) * rows_pooled + p);
-      const uint2 ev = __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
-      q.x += bf16lo(ev.x);
-      q.y += bf16hi(ev.x);
-      q.z += bf16lo(ev.y);
-      q.w += bf16hi(ev.y);
+  const int d = ch * 128 + lane * 4;
+  if (d >= D) return;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int l = 0; l < L; ++l) {
+    const int c = __ldg(codes + static_cast<size_t>(l) * rows_pooled + p);
+    const uint2 ev = __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
+    q.x += bf16lo(ev.x);
+    q.y += bf16hi(ev.x);
+    q.z += bf16lo(ev.y);
+    q.w += bf16hi(ev.y);
+  }
+  *reinterpret_cast<float4*>(q_out + static_cast<size_t>(p) * D + d) = q;
+  if (!update_r) return;
+  float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int i = 0; i < f; ++i) {
+    const size_t row = static_cast<size_t>(p) * f + i;
+    float4 r = *reinterpret_cast<const float4*>(resid + row * D + d);
+    r.x -= q.x;
+    r.y -= q.y;
+    r.z -= q.z;
+    r.w -= q.w;
+    *reinterpret_cast<float4*>(resid + row * D + d) = r;
+    if (g <= 0) continue;
+    if (i % g == 0) {
+      sum = r;
+    } else {
+      sum.x += r.x;
+      sum.y += r.y;
+      sum.z += r.z;
+      sum.w += r.w;
     }
-    for (int i = 0; i < f; ++i) {
-      const size_t o = (static_cast<size_t>(p) * f + i) * D + d;
-      float4 r = *reinterpret_cast<float4*>(resid + o);
-      float4 a = *reinterpret_cast<float4*>(recon + o);
-      r.x -= q.x;
-      r.y -= q.y;
-      r.z -= q.z;
-      r.w -= q.w;
-      a.x += q.x;
-      a.y += q.y;
-      a.z += q.z;
-      a.w += q.w;
-      *reinterpret_cast<float4*>(resid + o) = r;
-      *reinterpret_cast<float4*>(recon + o) = a;
+    if (i % g == g - 1) {
+      const float gf = static_cast<float>(g);
+      const float4 u = make_float4(sum.x / gf, sum.y / gf, sum.z / gf, sum.w / gf);
+      const size_t urow = row / g;
+      *reinterpret_cast<float4*>(u_next + urow * D + d) = u;
+      *reinterpret_cast<uint2*>(u_next_bf16 + urow * D + d) = make_uint2(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w));
     }
   }
+}
+
+// recon[t] = bf16(sum_s q_s[t / f_s]) over scales in order (f32), one thread per 4 channels
+struct ReconArgs {
+  const float* q[16];
+  int f[16];
+  int S;
+};
+__global__ void __launch_bounds__(256) multiscale_recon_kernel(const ReconArgs a, uint16_t* __restrict__ out,
+                                                               long long rows, int D) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int d4 = D / 4;
+  if (idx >= rows * d4) return;
+  const long long t = idx / d4;
+  const int d = static_cast<int>(idx - t * d4) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < a.S; ++s) {
+    const float4 q = *reinterpret_cast<const float4*>(a.q[s] + (t / a.f[s]) * D + d);
+    acc.x += q.x;
+    acc.y += q.y;
+    acc.z += q.z;
+    acc.w += q.w;
+  }
+  *reinterpret_cast<uint2*>(out + t * D + d) = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
 }
 
 // ------------------------------------------------------------ casts (L7)
@@ -699,11 +746,27 @@ cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t 
   return cudaGetLastError();
 }
 
-cudaError_t launch_scale_update(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* recon,
-                                int64_t B, int64_t T, int64_t D, int64_t K, int f, int* err, cudaStream_t stream) {
-  const long long rows_pooled = B * (T / f);
-  scale_update_kernel<<<static_cast<unsigned>((rows_pooled + 7) / 8), 256, 0, stream>>>(
-      codes, codebooks, L, resid, recon, rows_pooled, static_cast<int>(D), static_cast<int>(K), f, err);
+cudaError_t launch_scale_advance(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* q_out,
+                                 float* u_next, uint16_t* u_next_bf16, int64_t rows_pooled, int64_t D, int64_t K, int f,
+                                 int g, bool update_r, int* err, cudaStream_t stream) {
+  const long long warps = rows_pooled * ((D + 127) / 128);
+  scale_advance_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
+      codes, codebooks, L, resid, q_out, u_next, u_next_bf16, rows_pooled, static_cast<int>(D), static_cast<int>(K), f,
+      g, update_r ? 1 : 0, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_multiscale_recon(const float* const* q, const int* f, int S, uint16_t* out, int64_t rows, int64_t D,
+                                    cudaStream_t stream) {
+  ReconArgs a{};
+  a.S = S;
+  for (int s = 0; s < S; ++s) {
+    a.q[s] = q[s];
+    a.f[s] = f[s];
+  }
+  const long long threads = rows * (D / 4);
+  multiscale_recon_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(a, out, rows,
+                                                                                           static_cast<int>(D));
   return cudaGetLastError();
 }
 
