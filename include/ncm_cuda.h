@@ -143,12 +143,48 @@ NCM_API int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, in
 NCM_API int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codebooks, int32_t L, uint16_t* recon,
                    int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
 
+/* Upsampling along time, F.interpolate(size=out_len) on [B, C, T] data as the
+ * quantiser's U_i (research/reference/vq_forward_semantics.md:82, :108):
+ * q [batch, in_len, width] f32 -> out [batch, out_len, width] f32.
+ * mode 0 nearest: src = min(floor(t * s), in_len - 1);
+ * mode 1 linear (align_corners=False): src = max(fma(s, t + 0.5, -0.5), 0),
+ *   i0 = trunc(src), l1 = src - i0, i1 = min(i0 + 1, in_len - 1),
+ *   out = fma(q[i0], 1 - l1, q[i1] * l1)   (PyTorch's CPU operation order);
+ * s = float(in_len) / float(out_len). width % 4 == 0. */
+NCM_API int ncm_upsample(ncm_ctx_t* ctx, const float* q, float* out, int64_t batch, int64_t in_len, int64_t out_len,
+                         int64_t width, int32_t mode, ncm_stream_t stream);
+
+/* Kernel-3, padding-1 convolution along rows with a blend, per segment of
+ * rows (each segment zero-padded on both ends; segment_lengths is a HOST
+ * array of num_segments entries summing to rows, NULL = one segment):
+ *   out[t,o] = alpha * x[t,o] + beta * (bias[o] + sum_{i,k} w[o,i,k] * x[t+k-1,i])
+ * alpha = beta = 1 is apply_post_upsample_conv (src/ncm_model.zig:296-326);
+ * alpha = 1 - r, beta = r is the quantiser's Phi (vq_forward_semantics.md:93-100).
+ * x, out [rows, width] f32 (out may be x); weight [width, width, 3] bf16 (the
+ * PyTorch Conv1d layout); bias [width] f32 or NULL. The sum runs on tcgen05
+ * with bf16(x) and bf16 weights, f32 accumulation. Unequal segment lengths
+ * allow at most 64 segments. */
+NCM_API int ncm_conv1d_k3(ncm_ctx_t* ctx, const float* x, const uint16_t* weight, const float* bias, float* out,
+                          int64_t rows, int64_t width, int32_t num_segments, const int64_t* segment_lengths,
+                          float alpha, float beta, ncm_stream_t stream);
+
+/* Host-slice form of ncm_model.apply_post_upsample_conv (src/ncm_model.zig:296-326):
+ * input [row_count, width] f32 HOST, updated in place to input + bias + conv(input);
+ * weight [width, width, 3] and bias [width] f32 HOST (bf16-representable values,
+ * as loaded checkpoints are). Synchronous. */
+NCM_API int ncm_post_upsample_conv_host_f32(ncm_ctx_t* ctx, float* input, const float* weight, const float* bias,
+                                            int64_t row_count, int64_t width);
+
 /* Multiscale tokenizer forward (research/ncm_facts.md:81; scales coarse -> fine):
  *   h = linear_bf16(x, w_in, b_in); r = f32(h); recon = 0
  *   for s: u = pool(r, f_s); L levels of ncm_rvq_level on u; q = sum_l e_{s,l}[code]
- *          r -= up(q, f_s); recon += up(q, f_s)       (nearest-repeat upsampling)
+ *          Q = up(q, T) (upsample_mode); with Phi weights Q = Phi_s(Q)
+ *          r -= Q; recon += Q                        (f32, scales in order)
  *   y = linear_bf16(bf16(recon), w_out, b_out)
- * Codes are written scale-major: scale s occupies L * B*T/f_s entries, level-major. */
+ * Phi_s(Q) = (1 - phi_ratio) * Q + phi_ratio * (phi_bias[s] + Conv1d_k3(Q; phi_weight[s]))
+ * per batch item (vq_forward_semantics.md:93-100, R_k = Phi o Up), computed as
+ * ncm_conv1d_k3 does. Codes are written scale-major: scale s occupies
+ * L * B*T/f_s entries, level-major. */
 typedef struct ncm_tokenizer_config {
   int64_t batch;            /* B */
   int64_t seq_len;          /* T */
@@ -158,12 +194,30 @@ typedef struct ncm_tokenizer_config {
   int32_t num_scales;       /* S (<= 16) */
   int32_t levels_per_scale; /* L */
   int32_t pool_factors[16]; /* f_s, coarse to fine; each divides seq_len */
+  int32_t upsample_mode;    /* 0 nearest repeat (default), 1 linear (ncm_upsample) */
+  float phi_ratio;          /* r of Phi; used only when Phi weights are passed */
 } ncm_tokenizer_config_t;
 
 NCM_API int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x, const uint16_t* w_in,
                           const uint16_t* b_in, const uint16_t* codebooks, const float* sqnorms,
                           const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
                           uint16_t* y, ncm_stream_t stream);
+
+/* ncm_tokenizer_forward with the quantiser's residual convolutions:
+ * phi_weight [S, D, D, 3] bf16 and phi_bias [S, D] f32 (both NULL: no Phi). */
+NCM_API int ncm_tokenizer_forward_ex(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x,
+                                     const uint16_t* w_in, const uint16_t* b_in, const uint16_t* codebooks,
+                                     const float* sqnorms, const uint16_t* phi_weight, const float* phi_bias,
+                                     const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
+                                     uint16_t* y, ncm_stream_t stream);
+
+/* Multiscale decode (R5 at every scale; vq_forward_semantics.md:70, :82):
+ * recon [B, T, D] = bf16( sum_s Phi_s(up(q_s, T)) ) from codes laid out as
+ * ncm_tokenizer_forward writes them; cfg->model_width is unused. Given the
+ * tokenizer's codes, this reproduces its recon bit for bit. */
+NCM_API int ncm_multiscale_decode(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const int32_t* codes,
+                                  const uint16_t* codebooks, const uint16_t* phi_weight, const float* phi_bias,
+                                  uint16_t* recon, ncm_stream_t stream);
 
 /* -------------------------------------- L3-L6: NCM decoder forward pieces */
 
@@ -248,6 +302,11 @@ typedef struct ncm_decoder_weights {
   const uint16_t* final_norm_bias;       /* nullable */
   int32_t num_layers;
   const ncm_decoder_layer_weights_t* layers; /* host array of num_layers entries (device pointers) */
+  /* post_upsample_convs (ncm_model.zig:71, :141-153), applied to each level's
+   * input rows before the input projection: [num_levels, vq_width, vq_width, 3]
+   * bf16 and [num_levels, vq_width] f32, or both NULL */
+  const uint16_t* post_conv_weight;
+  const float* post_conv_bias;
 } ncm_decoder_weights_t;
 
 /* inputs [T, vq_width] bf16: the assembled prefix + target rows (ncm_model.zig:128-140);
@@ -281,7 +340,7 @@ NCM_API int ncm_rvq_level_noalloc(float* residual, const uint16_t* codebook, con
  * and launch count of one family since the last read, and resets them.
  * Families: "rvq_argmin", "rvq_apply", "linear_bf16", "rvq_decode",
  * "code_sqnorm", "pool_avg", "scale_update", "cast", "attention",
- * "decoder_elementwise"; "*" = all of them. */
+ * "decoder_elementwise", "conv_k3", "upsample"; "*" = all of them. */
 NCM_API int ncm_profile_enable(ncm_ctx_t* ctx, int on);
 NCM_API int ncm_profile_read(ncm_ctx_t* ctx, const char* kernel, double* total_ms, int64_t* launches);
 

@@ -37,6 +37,8 @@ class TokenizerConfig(ctypes.Structure):
         ("num_scales", c_i32),
         ("levels_per_scale", c_i32),
         ("pool_factors", c_i32 * 16),
+        ("upsample_mode", c_i32),
+        ("phi_ratio", ctypes.c_float),
     ]
 
 
@@ -86,6 +88,8 @@ class DecoderWeights(ctypes.Structure):
         ("final_norm_bias", c_vp),
         ("num_layers", c_i32),
         ("layers", ctypes.POINTER(DecoderLayerWeights)),
+        ("post_conv_weight", c_vp),
+        ("post_conv_bias", c_vp),
     ]
 
 
@@ -118,6 +122,13 @@ SIGNATURES: dict[str, list] = {
     "ncm_profile_read": [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i64)],
     "ncm_tokenizer_forward": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                               c_vp, c_vp, c_vp, c_vp],
+    "ncm_tokenizer_forward_ex": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                 c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "ncm_multiscale_decode": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "ncm_upsample": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp],
+    "ncm_conv1d_k3": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, ctypes.c_float, ctypes.c_float,
+                      c_vp],
+    "ncm_post_upsample_conv_host_f32": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64],
 }
 _RESTYPES = {"ncm_status_string": ctypes.c_char_p, "ncm_last_error": ctypes.c_char_p}
 

@@ -60,7 +60,8 @@ namespace ncm {
 
 const char* const kKernelNames[KID_COUNT] = {"rvq_argmin", "rvq_apply",    "linear_bf16", "rvq_decode",
                                              "code_sqnorm", "pool_avg",     "scale_update", "cast",
-                                             "attention",   "decoder_elementwise"};
+                                             "attention",   "decoder_elementwise", "conv_k3",
+                                             "upsample"};
 
 Launch::Launch(ncm_ctx* ctx, KernelId id, cudaStream_t stream) : ctx_(ctx), id_(id), stream_(stream) {
   ProfState& p = ctx->prof;
@@ -578,22 +579,135 @@ int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codeboo
   return NCM_OK;
 }
 
-int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x, const uint16_t* w_in,
-                          const uint16_t* b_in, const uint16_t* codebooks, const float* sqnorms,
-                          const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon, uint16_t* y,
-                          ncm_stream_t stream) {
-  int rc = check_ctx(ctx);
-  if (rc) return rc;
+}  // extern "C"
+
+namespace {
+
+// Shape checks shared by the tokenizer and the multiscale decode.
+int check_tokenizer_cfg(const ncm_tokenizer_config_t* cfg, bool with_projections, const uint16_t* phi_weight,
+                        const float* phi_bias) {
   if (cfg == nullptr) return ncm_fail(NCM_EINVAL, "tokenizer: null config");
-  const int64_t B = cfg->batch, T = cfg->seq_len, Din = cfg->model_width, D = cfg->vq_width, K = cfg->codebook_size;
+  const int64_t B = cfg->batch, T = cfg->seq_len, Din = cfg->model_width;
   const int S = cfg->num_scales, L = cfg->levels_per_scale;
-  if (B <= 0 || T <= 0 || Din <= 0 || Din % 8 != 0 || S <= 0 || S > 16 || L <= 0 || L > 64)
+  if (B <= 0 || T <= 0 || S <= 0 || S > 16 || L <= 0 || L > 64 || (with_projections && (Din <= 0 || Din % 8 != 0)))
     return ncm_fail(NCM_EINVAL, "tokenizer: bad config");
-  if ((rc = check_rvq_shape(B * T, D, K))) return rc;
+  int rc = check_rvq_shape(B * T, cfg->vq_width, cfg->codebook_size);
+  if (rc) return rc;
   for (int s = 0; s < S; ++s)
     if (cfg->pool_factors[s] <= 0 || T % cfg->pool_factors[s] != 0)
       return ncm_fail(NCM_EINVAL, "tokenizer: pool factor %d does not divide T=%lld", cfg->pool_factors[s],
                       (long long)T);
+  if (cfg->upsample_mode != 0 && cfg->upsample_mode != 1)
+    return ncm_fail(NCM_EINVAL, "tokenizer: upsample_mode %d unknown", cfg->upsample_mode);
+  if ((phi_weight == nullptr) != (phi_bias == nullptr))
+    return ncm_fail(NCM_EINVAL, "tokenizer: pass both Phi weight and bias, or neither");
+  if (phi_weight != nullptr) {
+    if (!(cfg->phi_ratio >= 0.f && cfg->phi_ratio <= 1.f))
+      return ncm_fail(NCM_EINVAL, "tokenizer: phi_ratio must lie in [0, 1]");
+    if (B * (T + 1) + 1 > INT32_MAX / 2) return ncm_fail(NCM_EINVAL, "tokenizer: too many rows for Phi");
+    if ((reinterpret_cast<uintptr_t>(phi_weight) & 1u) || !aligned16(phi_bias))
+      return ncm_fail(NCM_EINVAL, "tokenizer: Phi buffers misaligned (bias must be 16-byte aligned)");
+  }
+  return NCM_OK;
+}
+
+// Workspace of the general per-scale step (linear upsampling and/or Phi).
+struct ScaleEmitWs {
+  float* acc = nullptr;        // [N, D] f32 reconstruction accumulator
+  float* qf = nullptr;         // [N, D] f32 upsampled q (Phi's blend input)
+  uint16_t* qpad = nullptr;    // padded bf16 copy of qf (Phi's GEMM operand)
+  uint16_t* w_pack = nullptr;  // [S, D, 3 * dp] tap-major Phi kernels
+  int64_t dp = 0;
+};
+
+// Q = up(q_s); with Phi Q = (1 - r) Q + r (bias + conv(Q)); resid -= Q (if
+// given); acc += Q.
+int scale_emit(ncm_ctx* ctx, const ncm_tokenizer_config_t* cfg, int s, const float* q, float* resid,
+               const ScaleEmitWs& w, const float* phi_bias, cudaStream_t st) {
+  const int64_t B = cfg->batch, T = cfg->seq_len, D = cfg->vq_width;
+  const int64_t Tq = T / cfg->pool_factors[s];
+  if (w.w_pack == nullptr) {
+    Launch _launch(ctx, KID_UPSAMPLE, st);
+    NCM_CUDA_TRY(launch_upsample(q, B, Tq, T, D, cfg->upsample_mode, nullptr, nullptr, 0, resid, w.acc, st));
+    return NCM_OK;
+  }
+  {
+    Launch _launch(ctx, KID_UPSAMPLE, st);
+    NCM_CUDA_TRY(launch_upsample(q, B, Tq, T, D, cfg->upsample_mode, w.qf, w.qpad, w.dp, nullptr, nullptr, st));
+  }
+  SegMap map{};
+  map.seg_len = static_cast<int>(T);
+  map.nseg = static_cast<int>(B);
+  ConvEpilogue ep{};
+  ep.x_f32 = w.qf;
+  ep.resid = resid;
+  ep.acc_f32 = w.acc;
+  ep.bias = phi_bias + s * D;
+  ep.alpha = 1.f - cfg->phi_ratio;
+  ep.beta = cfg->phi_ratio;
+  return conv3_gemm(ctx, w.qpad, w.w_pack + static_cast<size_t>(s) * D * 3 * w.dp, map, w.dp, D, ep, st);
+}
+
+// Carves the general step's buffers (nothing when nearest and no Phi).
+struct ScaleEmitCarve {
+  size_t o_acc = 0, o_qf = 0, o_qpad = 0, o_w = 0;
+  bool general = false, phi = false;
+};
+ScaleEmitCarve carve_scale_emit(WsCarver& cv, const ncm_tokenizer_config_t* cfg, bool phi) {
+  ScaleEmitCarve c;
+  c.general = cfg->upsample_mode != 0 || phi;
+  c.phi = phi;
+  if (!c.general) return c;
+  const int64_t N = cfg->batch * cfg->seq_len, D = cfg->vq_width, dp = (D + 63) / 64 * 64;
+  c.o_acc = cv.take(sizeof(float) * N * D);
+  if (phi) {
+    c.o_qf = cv.take(sizeof(float) * N * D);
+    c.o_qpad = cv.take(2 * (cfg->batch * (cfg->seq_len + 1) + 1) * dp);
+    c.o_w = cv.take(2 * static_cast<size_t>(cfg->num_scales) * D * 3 * dp);
+  }
+  return c;
+}
+int setup_scale_emit(ncm_ctx* ctx, const ScaleEmitCarve& c, uint8_t* ws, const ncm_tokenizer_config_t* cfg,
+                     const uint16_t* phi_weight, ScaleEmitWs* w, cudaStream_t st) {
+  if (!c.general) return NCM_OK;
+  const int64_t N = cfg->batch * cfg->seq_len, D = cfg->vq_width;
+  w->dp = (D + 63) / 64 * 64;
+  w->acc = reinterpret_cast<float*>(ws + c.o_acc);
+  NCM_CUDA_TRY(cudaMemsetAsync(w->acc, 0, sizeof(float) * N * D, st));
+  if (!c.phi) return NCM_OK;
+  w->qf = reinterpret_cast<float*>(ws + c.o_qf);
+  w->qpad = reinterpret_cast<uint16_t*>(ws + c.o_qpad);
+  w->w_pack = reinterpret_cast<uint16_t*>(ws + c.o_w);
+  for (int s = 0; s < cfg->num_scales; ++s) {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_conv_repack(phi_weight + static_cast<size_t>(s) * D * D * 3, nullptr,
+                                    w->w_pack + static_cast<size_t>(s) * D * 3 * w->dp, D, w->dp, st));
+  }
+  return NCM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x, const uint16_t* w_in,
+                          const uint16_t* b_in, const uint16_t* codebooks, const float* sqnorms,
+                          const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon, uint16_t* y,
+                          ncm_stream_t stream) {
+  return ncm_tokenizer_forward_ex(ctx, cfg, x, w_in, b_in, codebooks, sqnorms, nullptr, nullptr, w_out, b_out, codes,
+                                  recon, y, stream);
+}
+
+int ncm_tokenizer_forward_ex(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const uint16_t* x,
+                             const uint16_t* w_in, const uint16_t* b_in, const uint16_t* codebooks,
+                             const float* sqnorms, const uint16_t* phi_weight, const float* phi_bias,
+                             const uint16_t* w_out, const uint16_t* b_out, int32_t* codes, uint16_t* recon,
+                             uint16_t* y, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_tokenizer_cfg(cfg, true, phi_weight, phi_bias))) return rc;
+  const int64_t B = cfg->batch, T = cfg->seq_len, Din = cfg->model_width, D = cfg->vq_width, K = cfg->codebook_size;
+  const int S = cfg->num_scales, L = cfg->levels_per_scale;
   if (!x || !w_in || !codebooks || !w_out || !codes || !y)
     return ncm_fail(NCM_EINVAL, "tokenizer: null buffer");
   if (!aligned16(x) || !aligned16(w_in) || !aligned16(codebooks) || !aligned16(w_out) || !aligned16(codes) ||
@@ -617,6 +731,7 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
   const size_t o_rb = recon ? 0 : cv.take(2 * N * D);
   const size_t o_part = cv.take(part_bytes);
   const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * S * L * K);
+  const ScaleEmitCarve ec = carve_scale_emit(cv, cfg, phi_weight != nullptr);
   uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "tokenizer: workspace allocation failed");
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
@@ -627,6 +742,8 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
   uint16_t* ub = reinterpret_cast<uint16_t*>(ws + o_ub);
   uint16_t* rb = recon ? recon : reinterpret_cast<uint16_t*>(ws + o_rb);
   RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
+  ScaleEmitWs ew;
+  if ((rc = setup_scale_emit(ctx, ec, ws, cfg, phi_weight, &ew, st))) return rc;
   if (sqnorms == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
     {
@@ -657,27 +774,85 @@ int ncm_tokenizer_forward(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, con
                           codes_s + static_cast<size_t>(l) * rows, part, plan, rows, D, K, l != L - 1, st);
       if (rc) return rc;
     }
-    // q_s, and r -= up(q_s) with the next scale's pooling in the same pass
     const bool next = s + 1 < S;
     const int g = next ? cfg->pool_factors[s + 1] : 0;
-    const bool fused_pool = next && f % g == 0;
-    {
-      Launch _launch(ctx, KID_SCALE_UPDATE, st);
-      NCM_CUDA_TRY(launch_scale_advance(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, r, q[s], u, ub,
-                                        rows, D, K, f, fused_pool ? g : 0, next, ctx->d_err, st));
-    }
-    if (next && !fused_pool) {
-      Launch _launch(ctx, KID_POOL, st);
-      NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, g, st));
+    const uint16_t* cbs_s = codebooks + static_cast<size_t>(s) * L * K * D;
+    if (!ec.general) {
+      // q_s, and r -= up(q_s) with the next scale's pooling in the same pass
+      const bool fused_pool = next && f % g == 0;
+      {
+        Launch _launch(ctx, KID_SCALE_UPDATE, st);
+        NCM_CUDA_TRY(launch_scale_advance(codes_s, cbs_s, L, r, q[s], u, ub, rows, D, K, f, fused_pool ? g : 0, next,
+                                          ctx->d_err, st));
+      }
+      if (next && !fused_pool) {
+        Launch _launch(ctx, KID_POOL, st);
+        NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, g, st));
+      }
+    } else {
+      {
+        Launch _launch(ctx, KID_SCALE_UPDATE, st);
+        NCM_CUDA_TRY(launch_scale_advance(codes_s, cbs_s, L, nullptr, q[s], nullptr, nullptr, rows, D, K, f, 0, false,
+                                          ctx->d_err, st));
+      }
+      if ((rc = scale_emit(ctx, cfg, s, q[s], next ? r : nullptr, ew, phi_bias, st))) return rc;
+      if (next) {
+        Launch _launch(ctx, KID_POOL, st);
+        NCM_CUDA_TRY(launch_pool_avg(r, u, ub, B, T, D, g, st));
+      }
     }
     codes_s += static_cast<size_t>(L) * rows;
   }
   {
-    // recon = bf16(sum_s up(q_s)), scales in order
+    // recon = bf16(sum_s Q_s), scales in order
     Launch _launch(ctx, KID_CAST, st);
-    NCM_CUDA_TRY(launch_multiscale_recon(q, cfg->pool_factors, S, rb, N, D, st));
+    if (ec.general)
+      NCM_CUDA_TRY(launch_f32_to_bf16(ew.acc, rb, N * D, st));
+    else
+      NCM_CUDA_TRY(launch_multiscale_recon(q, cfg->pool_factors, S, rb, N, D, st));
   }
   return linear_bf16(ctx, rb, w_out, b_out, y, nullptr, N, D, Din, st);
+}
+
+int ncm_multiscale_decode(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, const int32_t* codes,
+                          const uint16_t* codebooks, const uint16_t* phi_weight, const float* phi_bias,
+                          uint16_t* recon, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_tokenizer_cfg(cfg, false, phi_weight, phi_bias))) return rc;
+  if (!codes || !codebooks || !recon) return ncm_fail(NCM_EINVAL, "multiscale_decode: null buffer");
+  if (!aligned16(codes) || !aligned16(codebooks) || !aligned16(recon))
+    return ncm_fail(NCM_EINVAL, "multiscale_decode: buffers must be 16-byte aligned");
+  const int64_t N = cfg->batch * cfg->seq_len, D = cfg->vq_width, K = cfg->codebook_size;
+  const int S = cfg->num_scales, L = cfg->levels_per_scale;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  WsCarver cv;
+  size_t o_q[16];
+  for (int s = 0; s < S; ++s) o_q[s] = cv.take(sizeof(float) * (N / cfg->pool_factors[s]) * D);
+  const ScaleEmitCarve ec = carve_scale_emit(cv, cfg, phi_weight != nullptr);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "multiscale_decode: workspace allocation failed");
+  float* q[16];
+  for (int s = 0; s < S; ++s) q[s] = reinterpret_cast<float*>(ws + o_q[s]);
+  ScaleEmitWs ew;
+  if ((rc = setup_scale_emit(ctx, ec, ws, cfg, phi_weight, &ew, st))) return rc;
+  const int32_t* codes_s = codes;
+  for (int s = 0; s < S; ++s) {
+    const int64_t rows = N / cfg->pool_factors[s];
+    {
+      Launch _launch(ctx, KID_SCALE_UPDATE, st);
+      NCM_CUDA_TRY(launch_scale_advance(codes_s, codebooks + static_cast<size_t>(s) * L * K * D, L, nullptr, q[s],
+                                        nullptr, nullptr, rows, D, K, cfg->pool_factors[s], 0, false, ctx->d_err, st));
+    }
+    if (ec.general && (rc = scale_emit(ctx, cfg, s, q[s], nullptr, ew, phi_bias, st))) return rc;
+    codes_s += static_cast<size_t>(L) * rows;
+  }
+  Launch _launch(ctx, KID_CAST, st);
+  if (ec.general)
+    NCM_CUDA_TRY(launch_f32_to_bf16(ew.acc, recon, N * D, st));
+  else
+    NCM_CUDA_TRY(launch_multiscale_recon(q, cfg->pool_factors, S, recon, N, D, st));
+  return NCM_OK;
 }
 
 int ncm_profile_enable(ncm_ctx_t* ctx, int on) {

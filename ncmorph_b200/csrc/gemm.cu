@@ -53,8 +53,13 @@ struct LinearArgs {
   int tiles_a, tiles_b;  // tiles along the 128-row operand and the BN operand
   int a_fast;            // raster: 1 = consecutive tiles walk the A-operand tiles
   int vec_ok;            // y rows are 16-byte aligned (N % 8 == 0)
-  int mode;              // 0 plain, 1 SwiGLU (y[M,F]), 2 residual add into y
+  int mode;              // 0 plain, 1 SwiGLU (y[M,F]), 2 residual add into y, 3 kernel-3 convolution
   int F;                 // SwiGLU width (mode 1): gate rows [0,F), up rows [F,2F) of W
+  // mode 3: K = 3 * nk_tap * BK; K-chunk kc reads tap kc / nk_tap, i.e. the
+  // A rows shifted by tap - 1 (the padded copy supplies the zeros)
+  int taps, nk_tap;
+  ConvEpilogue conv;
+  SegMap map;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& ta, int& tb) {
@@ -124,7 +129,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, ta * BM);
+          if (args.taps > 1) {
+            // row -1 of the first tile is outside the tensor: TMA fills it with zeros
+            const int tap = kc / args.nk_tap;
+            tma_load_2d(&tmA, &S.full[stage], S.a[stage], (kc - tap * args.nk_tap) * BK, ta * BM + tap - 1);
+          } else {
+            tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, ta * BM);
+          }
           if (args.mode == 1) {
             // gate rows and the matching up rows side by side in one tile
             tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * (BN / 2));
@@ -235,6 +246,76 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint16_t* dst = args.y + static_cast<size_t>(m) * args.F + n0 + c;
             *reinterpret_cast<uint4*>(dst) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
             *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          }
+        }
+      } else if (!SWAP && args.mode == 3) {
+        // val = alpha * X + beta * (acc + bias), scattered to the real row
+        const long long m = arow < args.M ? args.map.real_row(arow) : -1;
+        const ConvEpilogue& ep = args.conv;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          tmem_ld_x16(tbase + c, v);
+          tmem_wait_ld();
+          if (m < 0) continue;
+          const int n0 = tb * BN + c;
+          const size_t o = static_cast<size_t>(m) * args.N + n0;
+          if (args.vec_ok && n0 + 16 <= args.N) {
+            // 16-byte accesses (N % 4 == 0 and every buffer 16-byte aligned)
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (ep.x_f32 != nullptr) {
+                x = *reinterpret_cast<const float4*>(ep.x_f32 + o + j);
+              } else if (ep.x_bf16 != nullptr) {
+                const uint2 h = *reinterpret_cast<const uint2*>(ep.x_bf16 + o + j);
+                x = make_float4(bf16lo(h.x), bf16hi(h.x), bf16lo(h.y), bf16hi(h.y));
+              }
+              float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (ep.bias != nullptr) b = __ldg(reinterpret_cast<const float4*>(ep.bias + n0 + j));
+              float4 val;
+              val.x = fmaf(ep.alpha, x.x, ep.beta * (__uint_as_float(v[j]) + b.x));
+              val.y = fmaf(ep.alpha, x.y, ep.beta * (__uint_as_float(v[j + 1]) + b.y));
+              val.z = fmaf(ep.alpha, x.z, ep.beta * (__uint_as_float(v[j + 2]) + b.z));
+              val.w = fmaf(ep.alpha, x.w, ep.beta * (__uint_as_float(v[j + 3]) + b.w));
+              if (ep.out_f32 != nullptr) *reinterpret_cast<float4*>(ep.out_f32 + o + j) = val;
+              if (ep.out_bf16 != nullptr)
+                *reinterpret_cast<uint2*>(ep.out_bf16 + o + j) =
+                    make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
+              if (ep.resid != nullptr) {
+                float4 r = *reinterpret_cast<const float4*>(ep.resid + o + j);
+                r.x -= val.x;
+                r.y -= val.y;
+                r.z -= val.z;
+                r.w -= val.w;
+                *reinterpret_cast<float4*>(ep.resid + o + j) = r;
+              }
+              if (ep.acc_f32 != nullptr) {
+                float4 a = *reinterpret_cast<const float4*>(ep.acc_f32 + o + j);
+                a.x += val.x;
+                a.y += val.y;
+                a.z += val.z;
+                a.w += val.w;
+                *reinterpret_cast<float4*>(ep.acc_f32 + o + j) = a;
+              }
+            }
+            continue;
+          }
+#pragma unroll 1
+          for (int j = 0; j < 16; ++j) {
+            const int n = n0 + j;
+            if (n >= args.N) break;
+            const float cb = __uint_as_float(v[j]) + (ep.bias != nullptr ? __ldg(ep.bias + n) : 0.f);
+            float x = 0.f;
+            if (ep.x_f32 != nullptr)
+              x = ep.x_f32[o + j];
+            else if (ep.x_bf16 != nullptr)
+              x = bf16_to_f32(ep.x_bf16[o + j]);
+            const float val = fmaf(ep.alpha, x, ep.beta * cb);
+            if (ep.out_f32 != nullptr) ep.out_f32[o + j] = val;
+            if (ep.out_bf16 != nullptr) ep.out_bf16[o + j] = f32_to_bf16(val);
+            if (ep.resid != nullptr) ep.resid[o + j] -= val;
+            if (ep.acc_f32 != nullptr) ep.acc_f32[o + j] += val;
           }
         }
       } else
@@ -371,6 +452,7 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
   if (mode == 1 && (M <= 64 || F % 128 != 0 || N != 2 * F))
     return ncm_fail(NCM_EINVAL, "linear: fused SwiGLU needs M > 64, F %% 128 == 0, N == 2F");
   LinearArgs a{};
+  a.taps = 1;
   a.mode = mode;
   a.F = static_cast<int>(F);
   a.bias = bias;
@@ -428,6 +510,52 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
       case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
       default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
     }
+  }
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  return NCM_OK;
+}
+
+int conv3_gemm(ncm_ctx* ctx, const uint16_t* a_pad, const uint16_t* w_pack, const SegMap& map, int64_t dp,
+               int64_t width, const ConvEpilogue& ep, cudaStream_t stream) {
+  const int64_t Mp = map.padded_rows();
+  if (dp % BK != 0 || width <= 0 || Mp <= 0)
+    return ncm_fail(NCM_EINVAL, "conv: padded width %lld must be a multiple of 64", (long long)dp);
+  LinearArgs a{};
+  a.mode = 3;
+  a.err = ctx->d_err;
+  a.M = static_cast<int>(Mp);
+  a.N = static_cast<int>(width);
+  a.K = static_cast<int>(3 * dp);
+  a.taps = 3;
+  a.nk_tap = static_cast<int>(dp / BK);
+  a.conv = ep;
+  a.map = map;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  a.vec_ok = width % 4 == 0 && al(ep.x_f32) && al(ep.x_bf16) && al(ep.out_f32) && al(ep.out_bf16) &&
+             al(ep.resid) && al(ep.acc_f32) && al(ep.bias);
+  const long long mt = ceil_div(Mp, BM);
+  int bn;
+  if (mt * ceil_div(width, 256) >= ctx->num_sms)
+    bn = 256;
+  else if (mt * ceil_div(width, 128) >= ctx->num_sms)
+    bn = 128;
+  else
+    bn = 64;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_bf16_2d(&tmA, a_pad, Mp, dp, BM) || !make_tmap_bf16_2d(&tmB, w_pack, width, 3 * dp, bn))
+    return ncm_fail(NCM_EINVAL, "conv: tensor map encoding failed (rows=%lld width=%lld)", (long long)Mp,
+                    (long long)width);
+  a.tiles_a = static_cast<int>(mt);
+  a.tiles_b = ceil_div(width, bn);
+  const double a_bytes = double(Mp) * dp * 2, b_bytes = double(width) * 3 * dp * 2;
+  a.a_fast = a_bytes <= b_bytes ? 1 : 0;
+  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
+  cudaError_t e;
+  Launch _launch(ctx, KID_CONV, stream);
+  switch (bn) {
+    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
+    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
+    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
   }
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
   return NCM_OK;

@@ -25,6 +25,8 @@ enum KernelId {
   KID_CAST,
   KID_ATTENTION,
   KID_DECODER_ELEMENTWISE,
+  KID_CONV,
+  KID_UPSAMPLE,
   KID_COUNT
 };
 extern const char* const kKernelNames[KID_COUNT];
@@ -187,5 +189,71 @@ int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16
 // bf16(y + bf16(x.w^T + bias)).
 int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
                    float* y_f32, int64_t M, int64_t K, int64_t N, cudaStream_t stream, int mode, int64_t F);
+
+// ---- kernel-3 convolution over row segments (conv.cu, gemm.cu)
+//
+// Rows are grouped into independent segments (batch items, NCM levels); the
+// convolution zero-pads each segment on both ends. The GEMM reads a bf16 copy
+// of the input in "padded" row order: one zero row before every segment and
+// one after the last, so segment s (real rows [r_s, r_s + n_s)) occupies
+// padded rows [r_s + s + 1, r_s + s + 1 + n_s), and the rows a tap reads past
+// a segment's end are zeros. Columns are padded with zeros to a multiple of 64.
+constexpr int kMaxConvSegments = 64;
+struct SegMap {
+  int seg_len;  // > 0: every segment has seg_len rows (the tables are unused)
+  int nseg;
+  int rstart[kMaxConvSegments + 1];  // real first row of each segment; rstart[nseg] = rows
+  // padded row -> real row, or -1 for a pad row (or past the end)
+  __host__ __device__ __forceinline__ long long real_row(long long p) const {
+    if (seg_len > 0) {
+      if (p < 1) return -1;
+      const long long s = (p - 1) / (seg_len + 1);
+      const long long off = p - 1 - s * (seg_len + 1);
+      if (s >= nseg || off >= seg_len) return -1;
+      return s * seg_len + off;
+    }
+    for (int s = 0; s < nseg; ++s) {
+      const long long ps = rstart[s] + s + 1;
+      if (p >= ps && p < ps + (rstart[s + 1] - rstart[s])) return rstart[s] + (p - ps);
+    }
+    return -1;
+  }
+  __host__ __device__ __forceinline__ long long padded_rows() const {
+    return seg_len > 0 ? static_cast<long long>(nseg) * (seg_len + 1) + 1 : rstart[nseg] + nseg + 1;
+  }
+};
+// Builds the map for `nseg` segments of the given lengths (nullptr: one
+// segment of `rows`); uniform lengths use the closed form. false if too many.
+bool make_segmap(SegMap* m, int64_t rows, int nseg, const int64_t* lengths);
+
+// The GEMM's epilogue: val = alpha * X + beta * (acc + bias) with X the f32
+// (or bf16) input row, then any of: out_f32 = val, out_bf16 = bf16(val),
+// resid -= val, acc_f32 += val. All [rows, width] in real row order.
+struct ConvEpilogue {
+  const float* x_f32;
+  const uint16_t* x_bf16;
+  float* out_f32;
+  uint16_t* out_bf16;
+  float* resid;
+  float* acc_f32;
+  const float* bias;  // [width] f32 or null
+  float alpha, beta;
+};
+// a_pad: [padded rows, dp] bf16 (the padded copy), w_pack: [width, 3*dp] bf16
+// (tap-major repack of a [width, width, 3] kernel).
+int conv3_gemm(ncm_ctx* ctx, const uint16_t* a_pad, const uint16_t* w_pack, const SegMap& map, int64_t dp,
+               int64_t width, const ConvEpilogue& ep, cudaStream_t stream);
+// [width_out, width_in, 3] kernel (bf16 bits or f32 values) -> [width_out, 3, dp] bf16, zero-padded.
+cudaError_t launch_conv_repack(const uint16_t* w_bf16, const float* w_f32, uint16_t* out, int64_t width, int64_t dp,
+                               cudaStream_t stream);
+// x [rows, width] (f32 or bf16) -> padded bf16 copy [map.padded_rows(), dp].
+cudaError_t launch_conv_pad(const float* x_f32, const uint16_t* x_bf16, uint16_t* out, const SegMap& map,
+                            int64_t width, int64_t dp, cudaStream_t stream);
+// Upsampling along time of q [B, Tq, D] to T = Tq * f rows per item
+// (F.interpolate(size=T); mode 0 nearest, 1 linear with align_corners=False):
+// Q -> out_f32 (nullable), bf16(Q) -> out_pad (the conv's padded copy with
+// segments of T rows, nullable), resid -= Q and acc += Q (nullable).
+cudaError_t launch_upsample(const float* q, int64_t B, int64_t Tq, int64_t T, int64_t D, int mode, float* out_f32,
+                            uint16_t* out_pad, int64_t dp, float* resid, float* acc, cudaStream_t stream);
 
 }  // namespace ncm

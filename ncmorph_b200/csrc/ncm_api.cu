@@ -143,6 +143,18 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   const size_t o_vt = cv.take(2 * T * Hkv * 64), o_ctx = cv.take(2 * T * H * 64), o_a = cv.take(2 * T * Hd);
   const bool fused_swiglu = T > 64 && F % 128 == 0;
   const size_t o_gu = fused_swiglu ? 0 : cv.take(2 * T * 2 * F), o_act = cv.take(2 * T * F);
+  // post-upsample convolutions: convolved input rows, one level's padded copy, one packed kernel
+  const bool post_conv = W->post_conv_weight != nullptr;
+  if (post_conv != (W->post_conv_bias != nullptr))
+    return ncm_fail(NCM_EINVAL, "ncm_forward: pass both post-conv weight and bias, or neither");
+  if (post_conv && !a16(W->post_conv_bias))
+    return ncm_fail(NCM_EINVAL, "ncm_forward: post-conv bias must be 16-byte aligned");
+  const int64_t Vp = (V + 63) / 64 * 64;
+  int64_t max_level = 0;
+  for (int i = 0; i < m.num_levels; ++i) max_level = std::max<int64_t>(max_level, m.level_lengths[i]);
+  const size_t o_xin = post_conv ? cv.take(2 * T * V) : 0;
+  const size_t o_cpad = post_conv ? cv.take(2 * (max_level + 2) * Vp) : 0;
+  const size_t o_cw = post_conv ? cv.take(2 * V * 3 * Vp) : 0;
   uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "ncm_forward: workspace allocation failed");
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + o_h);
@@ -198,6 +210,35 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
 
   const int Ti = static_cast<int>(T);
   const float eps = cfg->rms_norm_epsilon;
+  if (post_conv) {
+    // ncm_model.zig:141-153: each level's rows get x + bias + conv(x) with that level's kernel
+    uint16_t* xin = reinterpret_cast<uint16_t*>(ws + o_xin);
+    uint16_t* cpad = reinterpret_cast<uint16_t*>(ws + o_cpad);
+    uint16_t* cw = reinterpret_cast<uint16_t*>(ws + o_cw);
+    NCM_CUDA_TRY(cudaMemcpyAsync(xin, inputs, 2 * T * V, cudaMemcpyDeviceToDevice, st));
+    int64_t row0 = m.prefix_length;
+    for (int i = 0; i < m.num_levels; ++i) {
+      const int64_t n = m.level_lengths[i];
+      SegMap map{};
+      map.seg_len = static_cast<int>(n);
+      map.nseg = 1;
+      {
+        Launch _l(ctx, KID_CAST, st);
+        NCM_CUDA_TRY(launch_conv_repack(W->post_conv_weight + static_cast<size_t>(i) * V * V * 3, nullptr, cw, V, Vp,
+                                        st));
+        NCM_CUDA_TRY(launch_conv_pad(nullptr, inputs + row0 * V, cpad, map, V, Vp, st));
+      }
+      ConvEpilogue ep{};
+      ep.x_bf16 = inputs + row0 * V;
+      ep.out_bf16 = xin + row0 * V;
+      ep.bias = W->post_conv_bias + i * V;
+      ep.alpha = 1.f;
+      ep.beta = 1.f;
+      if ((rc = conv3_gemm(ctx, cpad, cw, map, Vp, V, ep, st))) return rc;
+      row0 += n;
+    }
+    inputs = xin;
+  }
   rc = linear_bf16(ctx, inputs, W->input_projection, W->input_projection_bias, h, nullptr, T, V, Hd, st);
   if (rc) return rc;
   if (cfg->use_level_encoding) {

@@ -107,6 +107,9 @@ class Weights:
     final_norm: torch.Tensor
     layers: list = field(default_factory=list)
     final_norm_bias: torch.Tensor | None = None
+    # post_upsample_convs (ncm_model.zig:71): [levels, vq, vq, 3] bf16 and [levels, vq] f32
+    post_conv_weight: torch.Tensor | None = None
+    post_conv_bias: torch.Tensor | None = None
 
 
 @dataclass
@@ -156,8 +159,30 @@ def forward(cfg: Config, w: Weights, inputs: torch.Tensor, out: torch.Tensor | N
     W.final_norm_bias = _vp(w.final_norm_bias)
     W.num_layers = len(w.layers)
     W.layers = layers
+    if w.post_conv_weight is not None:
+        L, V = len(cfg.level_lengths), cfg.vq_width
+        need(w.post_conv_weight, bf16, "post_conv_weight", (L, V, V, 3))
+        need(w.post_conv_bias, torch.float32, "post_conv_bias", (L, V))
+    W.post_conv_weight = _vp(w.post_conv_weight)
+    W.post_conv_bias = _vp(w.post_conv_bias)
     if out is None:
         out = torch.empty((T, cfg.hidden_size), dtype=bf16, device=inputs.device)
     _lib.call("ncm_ncm_forward", context(inputs.device), ctypes.byref(c), ctypes.byref(W), ptr(inputs), ptr(out),
               stream_of(inputs))
     return out
+
+
+def apply_post_upsample_conv(input: np.ndarray, weight: np.ndarray, bias: np.ndarray, row_count: int, width: int,
+                             device: int = 0) -> None:
+    """ncm_model.apply_post_upsample_conv (src/ncm_model.zig:296-326) on the GPU:
+    input [row_count, width] f32 (host) becomes input + bias + Conv1d_k3(input)
+    in place; weight [width, width, 3] and bias [width] are f32 host arrays
+    holding bf16 values. The convolution runs on tcgen05 with bf16 operands."""
+    for a, n, name in ((input, row_count * width, "input"), (weight, width * width * 3, "weight"),
+                       (bias, width, "bias")):
+        if not isinstance(a, np.ndarray) or a.dtype != np.float32 or not a.flags.c_contiguous:
+            raise TypeError(f"{name} must be a C-contiguous float32 numpy array")
+        if a.size != n:
+            raise ValueError(f"{name} has {a.size} elements, expected {n}")
+    _lib.call("ncm_post_upsample_conv_host_f32", context(device), ctypes.c_void_p(input.ctypes.data),
+              ctypes.c_void_p(weight.ctypes.data), ctypes.c_void_p(bias.ctypes.data), row_count, width)

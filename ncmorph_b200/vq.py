@@ -133,8 +133,49 @@ def pool_avg(x: torch.Tensor, factor: int) -> torch.Tensor:
     return y
 
 
+UPSAMPLE_MODES = {"nearest": 0, "linear": 1}
+
+
+def upsample(q: torch.Tensor, out_len: int, mode: str = "linear") -> torch.Tensor:
+    """F.interpolate(size=out_len) along time of q [B, Tq, D] f32 (the
+    quantiser's U_i, vq_forward_semantics.md:82): nearest or linear
+    (align_corners=False). Returns f32 [B, out_len, D]."""
+    B, Tq, D = q.shape
+    need(q, torch.float32, "q")
+    out = torch.empty((B, out_len, D), dtype=torch.float32, device=q.device)
+    _lib.call("ncm_upsample", context(q.device), ptr(q), ptr(out), B, Tq, out_len, D, UPSAMPLE_MODES[mode],
+              stream_of(q))
+    return out
+
+
+def conv1d_k3(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+              segments: list[int] | None = None, alpha: float = 1.0, beta: float = 1.0,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = alpha * x + beta * (bias + Conv1d(x; weight, kernel 3, padding 1))
+    along the rows of x [rows, width] f32, each segment zero-padded on its own.
+    weight [width, width, 3] bf16 (the Conv1d layout). alpha = beta = 1 is
+    ncm_model.apply_post_upsample_conv; alpha = 1 - r, beta = r is Phi."""
+    rows, width = x.shape
+    need(x, torch.float32, "x")
+    need(weight, bf16, "weight", (width, width, 3))
+    if bias is not None:
+        need(bias, torch.float32, "bias", (width,))
+    if out is None:
+        out = torch.empty_like(x)
+    need(out, torch.float32, "out", (rows, width))
+    lens = None
+    nseg = 1
+    if segments is not None:
+        nseg = len(segments)
+        lens = (ctypes.c_int64 * nseg)(*[int(n) for n in segments])
+    _lib.call("ncm_conv1d_k3", context(x.device), ptr(x), ptr(weight), ptr(bias), ptr(out), rows, width, nseg, lens,
+              float(alpha), float(beta), stream_of(x))
+    return out
+
+
 def tokenizer_config(batch: int, seq_len: int, model_width: int, vq_width: int, codebook_size: int,
-                     pool_factors: list[int], levels_per_scale: int) -> _lib.TokenizerConfig:
+                     pool_factors: list[int], levels_per_scale: int, upsample: str = "nearest",
+                     phi_ratio: float = 0.5) -> _lib.TokenizerConfig:
     cfg = _lib.TokenizerConfig()
     cfg.batch, cfg.seq_len, cfg.model_width, cfg.vq_width = batch, seq_len, model_width, vq_width
     cfg.codebook_size = codebook_size
@@ -142,15 +183,37 @@ def tokenizer_config(batch: int, seq_len: int, model_width: int, vq_width: int, 
     cfg.levels_per_scale = levels_per_scale
     for i, f in enumerate(pool_factors):
         cfg.pool_factors[i] = int(f)
+    cfg.upsample_mode = UPSAMPLE_MODES[upsample]
+    cfg.phi_ratio = float(phi_ratio)
     return cfg
+
+
+def _check_phi(phi_weight, phi_bias, S, D):
+    if (phi_weight is None) != (phi_bias is None):
+        raise ValueError("pass both phi_weight and phi_bias, or neither")
+    if phi_weight is not None:
+        need(phi_weight, bf16, "phi_weight", (S, D, D, 3))
+        need(phi_bias, torch.float32, "phi_bias", (S, D))
+
+
+def _split_codes(codes_flat, L, rows):
+    codes, off = [], 0
+    for r in rows:
+        codes.append(codes_flat[off:off + L * r].view(L, r))
+        off += L * r
+    return codes
 
 
 def tokenizer_forward(x: torch.Tensor, w_in: torch.Tensor, codebooks: torch.Tensor, w_out: torch.Tensor,
                       pool_factors: list[int], *, b_in: torch.Tensor | None = None,
-                      b_out: torch.Tensor | None = None, sqnorms: torch.Tensor | None = None):
+                      b_out: torch.Tensor | None = None, sqnorms: torch.Tensor | None = None,
+                      upsample: str = "nearest", phi_weight: torch.Tensor | None = None,
+                      phi_bias: torch.Tensor | None = None, phi_ratio: float = 0.5):
     """Multiscale RVQ tokenizer forward (R6).
 
     x [B, T, Din] bf16; w_in [D, Din]; codebooks [S, L, K, D]; w_out [Din, D].
+    upsample: "nearest" (default) or "linear"; phi_weight [S, D, D, 3] bf16 and
+    phi_bias [S, D] f32 add the quantiser's Phi after each scale's upsampling.
     Returns (codes: list over scales of int32 [L, B*T/f_s], recon bf16 [B, T, D], y bf16 [B, T, Din]).
     """
     B, T, Din = x.shape
@@ -163,17 +226,35 @@ def tokenizer_forward(x: torch.Tensor, w_in: torch.Tensor, codebooks: torch.Tens
     need(w_out, bf16, "w_out", (Din, D))
     if sqnorms is not None:
         need(sqnorms, torch.float32, "sqnorms", (S, L, K))
+    _check_phi(phi_weight, phi_bias, S, D)
     dev = x.device
     rows = [B * T // f for f in pool_factors]
     codes_flat = torch.empty(sum(L * r for r in rows), dtype=torch.int32, device=dev)
     recon = torch.empty((B, T, D), dtype=bf16, device=dev)
     y = torch.empty((B, T, Din), dtype=bf16, device=dev)
-    cfg = tokenizer_config(B, T, Din, D, K, pool_factors, L)
-    _lib.call("ncm_tokenizer_forward", context(dev), ctypes.byref(cfg), ptr(x), ptr(w_in), ptr(b_in),
-              ptr(codebooks), ptr(sqnorms), ptr(w_out), ptr(b_out), ptr(codes_flat), ptr(recon), ptr(y),
-              stream_of(x))
-    codes, off = [], 0
-    for r in rows:
-        codes.append(codes_flat[off:off + L * r].view(L, r))
-        off += L * r
-    return codes, recon, y
+    cfg = tokenizer_config(B, T, Din, D, K, pool_factors, L, upsample, phi_ratio)
+    _lib.call("ncm_tokenizer_forward_ex", context(dev), ctypes.byref(cfg), ptr(x), ptr(w_in), ptr(b_in),
+              ptr(codebooks), ptr(sqnorms), ptr(phi_weight), ptr(phi_bias), ptr(w_out), ptr(b_out),
+              ptr(codes_flat), ptr(recon), ptr(y), stream_of(x))
+    return _split_codes(codes_flat, L, rows), recon, y
+
+
+def multiscale_decode(codes: list[torch.Tensor], codebooks: torch.Tensor, batch: int, seq_len: int,
+                      pool_factors: list[int], *, upsample: str = "nearest", phi_weight: torch.Tensor | None = None,
+                      phi_bias: torch.Tensor | None = None, phi_ratio: float = 0.5) -> torch.Tensor:
+    """recon [B, T, D] bf16 = bf16(sum_s Phi_s(up(q_s))) from per-scale codes
+    [L, B*T/f_s] as tokenizer_forward returns them (R5 at every scale)."""
+    S, L, K, D = codebooks.shape
+    if len(pool_factors) != S or len(codes) != S:
+        raise ValueError("one pool factor and one code tensor per scale are required")
+    need(codebooks, bf16, "codebooks")
+    _check_phi(phi_weight, phi_bias, S, D)
+    for s, c in enumerate(codes):
+        need(c, torch.int32, f"codes[{s}]", (L, batch * seq_len // pool_factors[s]))
+    dev = codebooks.device
+    flat = torch.cat([c.reshape(-1) for c in codes])
+    recon = torch.empty((batch, seq_len, D), dtype=bf16, device=dev)
+    cfg = tokenizer_config(batch, seq_len, 0, D, K, pool_factors, L, upsample, phi_ratio)
+    _lib.call("ncm_multiscale_decode", context(dev), ctypes.byref(cfg), ptr(flat), ptr(codebooks), ptr(phi_weight),
+              ptr(phi_bias), ptr(recon), stream_of(codebooks))
+    return recon

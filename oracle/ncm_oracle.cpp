@@ -5,6 +5,7 @@
 // the reference calls @mulAdd (written here as fmaf).
 #include "ncm_oracle.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -711,6 +712,106 @@ void orc_scale_update(const int32_t* codes, const uint16_t* cbs, size_t L, float
         recon[row * D + d] += q[d];
       }
     }
+  }
+}
+
+// Upsampling along time as F.interpolate(size=T) on [B, C, T] data
+// (research/reference/vq_forward_semantics.md:82, :108; PyTorch's
+// upsample_linear1d / upsample_nearest1d CPU kernels), in their operation
+// order: s = float(Tq) / float(T); nearest: i = min(floor(t * s), Tq - 1);
+// linear: src = max(fma(s, t + 0.5, -0.5), 0), i0 = trunc(src),
+// l1 = clamp(src - i0, 0, 1), out = fma(q[i0], 1 - l1, q[i1] * l1).
+void orc_upsample(const float* q, float* out, size_t B, size_t Tq, size_t T, size_t D, int mode) {
+  const float s = static_cast<float>(Tq) / static_cast<float>(T);
+  for (size_t b = 0; b < B; ++b)
+    for (size_t t = 0; t < T; ++t) {
+      const float* qb = q + b * Tq * D;
+      float* o = out + (b * T + t) * D;
+      if (mode == 0) {
+        size_t i0 = static_cast<size_t>(std::floor(static_cast<float>(t) * s));
+        if (i0 > Tq - 1) i0 = Tq - 1;
+        for (size_t d = 0; d < D; ++d) o[d] = qb[i0 * D + d];
+      } else {
+        float src = std::fma(s, static_cast<float>(t) + 0.5f, -0.5f);
+        if (src < 0.f) src = 0.f;
+        const size_t i0 = static_cast<size_t>(src);
+        const float l1 = std::min(std::max(src - static_cast<float>(i0), 0.f), 1.f);
+        const float l0 = 1.f - l1;
+        const size_t i1 = i0 < Tq - 1 ? i0 + 1 : i0;
+        for (size_t d = 0; d < D; ++d) {
+          const float x1 = qb[i1 * D + d] * l1;
+          o[d] = std::fma(qb[i0 * D + d], l0, x1);
+        }
+      }
+    }
+}
+
+// Kernel-3 convolution with blend, per segment (zero padding at each
+// segment's ends): out[t,o] = fma(alpha, x_blend[t,o], beta * (float(C) + b[o]))
+// with C = sum_{i,k} w[o,i,k] * x_op[t+k-1,i] accumulated in f64 (the
+// products of bf16 values are exact). Callers pass bf16-rounded x_op and w to
+// mirror the tensor-core operands; apply_post_upsample_conv is alpha = beta = 1.
+void orc_conv1d_k3(const float* x_op, const float* x_blend, const float* w, const float* b, float* out, size_t rows,
+                   size_t width, const size_t* seg_lengths, size_t nseg, float alpha, float beta) {
+  std::vector<size_t> seg_of(rows), seg_start(nseg ? nseg : 1), seg_end(nseg ? nseg : 1);
+  if (seg_lengths == nullptr || nseg == 0) {
+    seg_start[0] = 0, seg_end[0] = rows;
+    for (size_t t = 0; t < rows; ++t) seg_of[t] = 0;
+  } else {
+    size_t at = 0;
+    for (size_t s = 0; s < nseg; ++s) {
+      seg_start[s] = at;
+      for (size_t i = 0; i < seg_lengths[s]; ++i) seg_of[at + i] = s;
+      at += seg_lengths[s];
+      seg_end[s] = at;
+    }
+  }
+  std::vector<float> res(rows * width);
+#pragma omp parallel for schedule(static)
+  for (long tt = 0; tt < static_cast<long>(rows); ++tt) {
+    const size_t t = static_cast<size_t>(tt);
+    const size_t s = seg_of[t];
+    for (size_t o = 0; o < width; ++o) {
+      double c = 0.0;
+      for (int k = 0; k < 3; ++k) {
+        const long src = static_cast<long>(t) + k - 1;
+        if (src < static_cast<long>(seg_start[s]) || src >= static_cast<long>(seg_end[s])) continue;
+        const float* xr = x_op + static_cast<size_t>(src) * width;
+        const float* wr = w + o * width * 3 + k;
+        for (size_t i = 0; i < width; ++i) c += static_cast<double>(wr[i * 3]) * static_cast<double>(xr[i]);
+      }
+      const float cb = static_cast<float>(c) + (b != nullptr ? b[o] : 0.f);
+      res[t * width + o] = std::fma(alpha, x_blend != nullptr ? x_blend[t * width + o] : 0.f, beta * cb);
+    }
+  }
+  std::memcpy(out, res.data(), sizeof(float) * rows * width);
+}
+
+// General multiscale step: q = sum_l e_l[code] per pooled row (f32, level
+// order); Q = up(q) (mode 0 nearest, 1 linear); with Phi (phi_w non-null,
+// [D, D, 3] bf16 values as f32) Q = fma(1 - r, Q, r * (C + b)) where C is the
+// convolution of bf16(Q) within each batch item; resid -= Q; acc += Q.
+void orc_scale_update_ex(const int32_t* codes, const uint16_t* cbs, size_t L, float* resid, float* acc, size_t B,
+                         size_t T, size_t D, size_t K, size_t f, int mode, const float* phi_w, const float* phi_b,
+                         float ratio) {
+  const size_t Tq = T / f, P = B * Tq;
+  std::vector<float> q(P * D), Q(B * T * D);
+  for (size_t p = 0; p < P; ++p)
+    for (size_t d = 0; d < D; ++d) {
+      float a = 0.0f;
+      for (size_t l = 0; l < L; ++l) a += bf16_to(cbs[(l * K + static_cast<size_t>(codes[l * P + p])) * D + d]);
+      q[p * D + d] = a;
+    }
+  orc_upsample(q.data(), Q.data(), B, Tq, T, D, mode);
+  if (phi_w != nullptr) {
+    std::vector<float> Qb(Q.size());
+    for (size_t i = 0; i < Q.size(); ++i) Qb[i] = bf16_to(bf16_from(Q[i]));
+    std::vector<size_t> segs(B, T);
+    orc_conv1d_k3(Qb.data(), Q.data(), phi_w, phi_b, Q.data(), B * T, D, segs.data(), B, 1.f - ratio, ratio);
+  }
+  for (size_t i = 0; i < B * T * D; ++i) {
+    if (resid != nullptr) resid[i] -= Q[i];
+    acc[i] += Q[i];
   }
 }
 

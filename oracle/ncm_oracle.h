@@ -99,6 +99,12 @@ void orc_rvq_level(float* resid, const uint16_t* cb, const float* sqnorm, const 
 void orc_rvq_decode(const int32_t* codes, const uint16_t* cbs, size_t L, float* recon_f32, size_t N, size_t D,
                     size_t K);
 void orc_pool_avg(const float* x, float* y, size_t B, size_t T, size_t D, size_t f);
+void orc_upsample(const float* q, float* out, size_t B, size_t Tq, size_t T, size_t D, int mode);
+void orc_conv1d_k3(const float* x_op, const float* x_blend, const float* w, const float* b, float* out, size_t rows,
+                   size_t width, const size_t* seg_lengths, size_t nseg, float alpha, float beta);
+void orc_scale_update_ex(const int32_t* codes, const uint16_t* cbs, size_t L, float* resid, float* acc, size_t B,
+                         size_t T, size_t D, size_t K, size_t f, int mode, const float* phi_w, const float* phi_b,
+                         float ratio);
 void orc_scale_update(const int32_t* codes, const uint16_t* cbs, size_t L, float* resid, float* recon, size_t B,
                       size_t T, size_t D, size_t K, size_t f);
 

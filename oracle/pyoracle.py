@@ -94,6 +94,11 @@ def lib() -> ctypes.CDLL:
         "orc_rvq_decode": ([i32p, u16p, sz, f32p, sz, sz, sz], None),
         "orc_pool_avg": ([f32p, f32p, sz, sz, sz, sz], None),
         "orc_scale_update": ([i32p, u16p, sz, f32p, f32p, sz, sz, sz, sz, sz], None),
+        "orc_upsample": ([f32p, f32p, sz, sz, sz, sz, ctypes.c_int], None),
+        "orc_conv1d_k3": ([f32p, ctypes.c_void_p, f32p, ctypes.c_void_p, f32p, sz, sz, ctypes.c_void_p, sz,
+                           ctypes.c_float, ctypes.c_float], None),
+        "orc_scale_update_ex": ([i32p, u16p, sz, ctypes.c_void_p, f32p, sz, sz, sz, sz, sz, ctypes.c_int,
+                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -326,6 +331,44 @@ def scale_update(codes: np.ndarray, cbs_bits: np.ndarray, resid: np.ndarray, rec
     _, K, D = cbs_bits.shape
     assert resid.dtype == np.float32 and recon.dtype == np.float32
     lib().orc_scale_update(_c(codes, np.int32), _c(cbs_bits, np.uint16), L, resid, recon, B, T, D, K, f)
+
+
+def _ptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def upsample(q: np.ndarray, T: int, mode: str = "linear") -> np.ndarray:
+    """F.interpolate(size=T) along axis 1 of q [B, Tq, D] (nearest / linear, align_corners=False)."""
+    q = _c(q, np.float32)
+    B, Tq, D = q.shape
+    out = np.empty((B, T, D), np.float32)
+    lib().orc_upsample(q, out, B, Tq, T, D, {"nearest": 0, "linear": 1}[mode])
+    return out
+
+
+def conv1d_k3(x_op, w, b, segments=None, alpha=1.0, beta=1.0, x_blend=None):
+    """out = alpha * x_blend + beta * (b + conv(x_op; w)) per row segment (f64 accumulation)."""
+    x_op = _c(x_op, np.float32)
+    rows, width = x_op.shape
+    x_blend = x_op if x_blend is None else _c(x_blend, np.float32)
+    w = _c(w, np.float32)
+    b = None if b is None else _c(b, np.float32)
+    segs = None if segments is None else np.ascontiguousarray(segments, dtype=np.uintp)
+    out = np.empty((rows, width), np.float32)
+    lib().orc_conv1d_k3(x_op, _ptr(x_blend), w, _ptr(b), out, rows, width, _ptr(segs),
+                        0 if segs is None else len(segs), alpha, beta)
+    return out
+
+
+def scale_update_ex(codes, cbs_bits, resid, acc, B, T, f, mode="nearest", phi_w=None, phi_b=None, ratio=0.5):
+    """General multiscale step (upsampling mode, optional Phi); updates resid (may be None) and acc in place."""
+    L, P = codes.shape
+    _, K, D = cbs_bits.shape
+    assert acc.dtype == np.float32 and (resid is None or resid.dtype == np.float32)
+    phi_w = None if phi_w is None else _c(phi_w, np.float32)
+    phi_b = None if phi_b is None else _c(phi_b, np.float32)
+    lib().orc_scale_update_ex(_c(codes, np.int32), _c(cbs_bits, np.uint16), L, _ptr(resid), acc, B, T, D, K, f,
+                              {"nearest": 0, "linear": 1}[mode], _ptr(phi_w), _ptr(phi_b), ratio)
 
 
 def rvq_encode(x_bits: np.ndarray, cbs_bits: np.ndarray, codes_in: np.ndarray | None = None, threads: int = 0):

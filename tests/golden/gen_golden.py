@@ -9,6 +9,10 @@ Outputs
                    packages/bf16/vectors.zig (PyTorch-generated, read as data)
   pool_area.npz    torch F.interpolate(mode="area") outputs on seeded inputs,
                    pinning the pooling semantics R4 restates
+  upsample.npz     torch F.interpolate(mode="linear"/"nearest", size=T) outputs
+                   (the quantiser's U_i, vq_forward_semantics.md:82)
+  conv1d_k3.npz    torch F.conv1d(kernel 3, padding 1) in float64 on seeded
+                   inputs (the Phi / post-upsample convolution)
 """
 from __future__ import annotations
 
@@ -46,8 +50,42 @@ def pool_area() -> None:
     np.savez_compressed(HERE / "pool_area.npz", **out)
 
 
+def upsample() -> None:
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(4321)
+    out = {}
+    for (B, Tq, D, T) in [(2, 16, 24, 256), (1, 37, 8, 100), (3, 16, 16, 32), (2, 5, 8, 5), (1, 1, 8, 16)]:
+        q = torch.randn(B, Tq, D, generator=g, dtype=torch.float32)
+        out[f"q_{B}_{Tq}_{D}_{T}"] = q.numpy()
+        for mode in ("linear", "nearest"):
+            y = F.interpolate(q.transpose(1, 2), size=T, mode=mode).transpose(1, 2).contiguous()
+            out[f"{mode}_{B}_{Tq}_{D}_{T}"] = y.numpy()
+    np.savez_compressed(HERE / "upsample.npz", **out)
+
+
+def conv1d_k3() -> None:
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(99)
+    out = {}
+    for (T, C) in [(50, 24), (7, 3), (1, 8), (33, 64)]:
+        x = torch.randn(T, C, generator=g, dtype=torch.float32)
+        w = torch.randn(C, C, 3, generator=g, dtype=torch.float32) * 0.1
+        b = torch.randn(C, generator=g, dtype=torch.float32)
+        y = F.conv1d(x.T[None].double(), w.double(), b.double(), padding=1)[0].T.contiguous()
+        out[f"x_{T}_{C}"], out[f"w_{T}_{C}"], out[f"b_{T}_{C}"] = x.numpy(), w.numpy(), b.numpy()
+        out[f"y_{T}_{C}"] = y.numpy()
+    np.savez_compressed(HERE / "conv1d_k3.npz", **out)
+
+
 if __name__ == "__main__":
-    ref = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
-    bf16_pairs(ref)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/gen_golden.py <path-to-ncmorph-checkout>")
+    bf16_pairs(pathlib.Path(sys.argv[1]))
     pool_area()
+    upsample()
+    conv1d_k3()
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".txt", ".npz")))

@@ -167,7 +167,16 @@ def oracle_ncm_forward(orc, cfg, w, inputs_bits):
     f = lambda t: orc.bf16_widen(from_dev_bf16(t))  # noqa: E731
     rb = orc.round_bf16
     T = cfg.seq_len
-    h = orc.matmul_bf16(orc.bf16_widen(inputs_bits), f(w.input_projection), f(w.input_projection_bias), threads=8)
+    x = orc.bf16_widen(inputs_bits).astype(np.float32)
+    if w.post_conv_weight is not None:
+        # ncm_model.zig:141-153: each level's rows get apply_post_upsample_conv with its own kernel
+        pw = f(w.post_conv_weight)
+        pb = w.post_conv_bias.cpu().numpy()
+        off = cfg.prefix_length
+        for i, n in enumerate(cfg.level_lengths):
+            x[off:off + n] = orc.apply_post_upsample_conv(x[off:off + n], pw[i], pb[i])
+            off += n
+    h = orc.matmul_bf16(x, f(w.input_projection), f(w.input_projection_bias), threads=8)
     emb = f(w.level_embedding)
     off = cfg.prefix_length
     for i, n in enumerate(cfg.level_lengths):
@@ -218,6 +227,33 @@ def test_ncm_forward_small_matches_oracle(orc, cuda_dev, mask, prefix, levels):
     frac_bad = (err > tol).mean()
     print(f"ncm forward {mask}: max |err| {err.max():.3g}, mean {err.mean():.3g}, outside bar {frac_bad:.2e}")
     assert frac_bad == 0.0
+
+
+def test_ncm_forward_post_upsample_convs_match_oracle(orc, cuda_dev):
+    """weights.post_upsample_convs (ncm_model.zig:141-153): each level's input
+    rows pass through x + bias + Conv1d_k3(x) with that level's kernel first."""
+    from ncmorph_b200 import ncm_model
+    levels = (16, 16, 32, 64, 128)
+    cfg = ncm_model.Config(hidden_size=256, vq_width=64, num_attention_heads=4, num_key_value_heads=2,
+                           intermediate_size=512, level_lengths=levels, prefix_length=0, mask="block_causal")
+    w = _rand_weights(cfg, cuda_dev, 7, layers=2)
+    g = torch.Generator(device=cuda_dev).manual_seed(8)
+    w.post_conv_weight = (torch.randn((len(levels), 64, 64, 3), generator=g, device=cuda_dev) * 0.05).to(
+        torch.bfloat16)
+    w.post_conv_bias = torch.randn((len(levels), 64), generator=g, device=cuda_dev) * 0.1
+    rng = np.random.default_rng(9)
+    inputs = gen_bf16(rng, (cfg.seq_len, cfg.vq_width))
+    out = ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(out))
+    ref = oracle_ncm_forward(orc, cfg, w, inputs)
+    err = np.abs(got - ref)
+    rms = np.sqrt((ref ** 2).mean(axis=1, keepdims=True))
+    assert (err > 3e-2 * np.abs(ref) + 3e-2 * rms).mean() == 0.0
+    # the convolutions change the result (they are not skipped)
+    w.post_conv_weight.zero_()
+    w.post_conv_bias.zero_()
+    plain = orc.bf16_widen(from_dev_bf16(ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))))
+    assert np.abs(plain - got).max() > 0.1
 
 
 def test_config4_forward_runs_and_is_normalised(cuda_dev):

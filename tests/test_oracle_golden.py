@@ -209,3 +209,58 @@ def test_tiny_decoder_attention_context(orc):
     out = orc.attention(x, w, 1, 1, 2, 1e-5, c, s, mask)
     assert np.allclose(out[0], x[0], atol=1e-6)
     assert np.allclose(out[1], (x[0] + x[1]) / 2, atol=1e-6)
+
+
+def _golden_npz(name):
+    return np.load(GOLDEN / name)
+
+
+def test_upsample_matches_torch_bit_exact(orc):
+    """U_i of the quantiser (vq_forward_semantics.md:82): F.interpolate(size=T),
+    linear (align_corners=False) and nearest, against committed torch outputs."""
+    z = _golden_npz("upsample.npz")
+    cases = [k[2:] for k in z.files if k.startswith("q_")]
+    assert len(cases) == 5
+    for c in cases:
+        B, Tq, D, T = map(int, c.split("_"))
+        q = z[f"q_{c}"]
+        for mode in ("linear", "nearest"):
+            got = orc.upsample(q, T, mode)
+            assert np.array_equal(got.view(np.uint32), z[f"{mode}_{c}"].view(np.uint32)), (mode, c)
+
+
+def test_conv1d_k3_matches_torch(orc):
+    """Phi / post-upsample convolution: kernel 3, padding 1, against torch's
+    float64 F.conv1d; both the f64-accumulating checker and the restatement of
+    apply_post_upsample_conv (src/ncm_model.zig:296-326, f32 in reference order)."""
+    z = _golden_npz("conv1d_k3.npz")
+    for c in sorted(k[2:] for k in z.files if k.startswith("x_")):
+        x, w, b, y = z[f"x_{c}"], z[f"w_{c}"], z[f"b_{c}"], z[f"y_{c}"]
+        scale = np.abs(x) @ np.abs(w).sum(axis=2).T + np.abs(b)
+        got = orc.conv1d_k3(x, w, b, alpha=0.0, beta=1.0)
+        assert np.all(np.abs(got - y) <= 1e-6 * scale + 1e-7), c
+        post = orc.apply_post_upsample_conv(x, w, b)
+        assert np.all(np.abs(post - (x + y)) <= 1e-5 * (scale + np.abs(x))), c
+
+
+def test_conv1d_k3_segments_are_independent(orc):
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((30, 8)).astype(np.float32)
+    w = (rng.standard_normal((8, 8, 3)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(8).astype(np.float32)
+    whole = orc.conv1d_k3(x, w, b, segments=[10, 5, 15], alpha=0.5, beta=0.5)
+    parts = [orc.conv1d_k3(x[a:e], w, b, alpha=0.5, beta=0.5) for a, e in ((0, 10), (10, 15), (15, 30))]
+    assert np.array_equal(whole, np.concatenate(parts))
+
+
+def test_scale_update_ex_nearest_without_phi_is_scale_update(orc):
+    rng = np.random.default_rng(2)
+    B, T, D, K, L, f = 2, 32, 16, 64, 3, 4
+    cbs = orc.bf16_bits(rng.standard_normal((L, K, D)).astype(np.float32))
+    codes = rng.integers(0, K, size=(L, B * T // f)).astype(np.int32)
+    r0 = rng.standard_normal((B * T, D)).astype(np.float32)
+    r1, a1 = r0.copy(), np.zeros_like(r0)
+    r2, a2 = r0.copy(), np.zeros_like(r0)
+    orc.scale_update(codes, cbs, r1, a1, B, T, f)
+    orc.scale_update_ex(codes, cbs, r2, a2, B, T, f, mode="nearest")
+    assert np.array_equal(r1, r2) and np.array_equal(a1, a2)
