@@ -48,6 +48,10 @@ def parse_args():
     p.add_argument("--seed", type=int, default=20260)
     p.add_argument("--graph", action="store_true",
                    help="secondary workloads: replay one captured CUDA graph per step")
+    p.add_argument("--upsample", choices=["nearest", "linear"], default="nearest",
+                   help="tokenizer workload: upsampling mode of each scale's reconstruction")
+    p.add_argument("--phi", action="store_true",
+                   help="tokenizer workload: apply the quantiser's Phi convolution after each upsampling")
     p.add_argument("--workload", choices=["rvq", "tokenizer", "linear", "decoder"], default="rvq",
                    help="rvq = BASELINE config 5 (the headline); tokenizer = config 2; linear = config 3 sweep; "
                         "decoder = config 4")
@@ -415,7 +419,14 @@ def run_secondary(a):
         decay = torch.tensor([0.6 ** l for l in range(L)], device=dev).view(1, L, 1, 1)
         cbs = (rnd((5, L, K, D)).float() * decay).to(torch.bfloat16)
         sq = vq.code_sqnorm(cbs)
-        step = lambda: vq.tokenizer_forward(x, w_in, cbs, w_out, factors, sqnorms=sq)  # noqa: E731
+        S = len(factors)
+        pw = pb = None
+        if a.phi:
+            bound = 1.0 / (3 * D) ** 0.5
+            pw = ((torch.rand((S, D, D, 3), generator=g, device=dev) * 2 - 1) * bound).to(torch.bfloat16)
+            pb = (torch.rand((S, D), generator=g, device=dev) * 2 - 1) * bound
+        tok = dict(sqnorms=sq, upsample=a.upsample, phi_weight=pw, phi_bias=pb, phi_ratio=0.5)
+        step = lambda: vq.tokenizer_forward(x, w_in, cbs, w_out, factors, **tok)  # noqa: E731
         _timed_loop(step, 0, a.warmup)
         lib.ncm_profile_read(ctx, b"*", None, None)
         lib.ncm_profile_enable(ctx, 1)
@@ -426,7 +437,8 @@ def run_secondary(a):
         sampler.start()
         ms = _timed_loop(run, a.steps, 0)
         clocks = sampler.stop()
-        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "rvq_apply", "pool_avg", "scale_update", "cast", "*"])
+        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "rvq_apply", "pool_avg", "scale_update", "cast",
+                                   "conv_k3", "upsample", "*"])
         rows = sum(B * T // f for f in factors)
         dist_flops = 2.0 * rows * K * D * L
         proj_flops = 2 * 2.0 * B * T * Din * D
@@ -438,7 +450,7 @@ def run_secondary(a):
 
         def step_e2e():
             x.copy_(x_host, non_blocking=True)
-            codes, _, _ = vq.tokenizer_forward(x, w_in, cbs, w_out, factors, sqnorms=sq)
+            codes, _, _ = vq.tokenizer_forward(x, w_in, cbs, w_out, factors, **tok)
             codes_host.copy_(torch.cat([c.reshape(-1) for c in codes]), non_blocking=True)
 
         ms_e2e = _timed_loop(step_e2e, a.steps, 1)
@@ -448,7 +460,8 @@ def run_secondary(a):
             "ms_per_step": ms, "cuda_graph": bool(a.graph),
             "config": {"workload": "multiscale tokenizer forward (BASELINE config 2)", "batch": B, "seq_len": T,
                        "model_width": Din, "vq_width": D, "codebook_size": K, "levels_per_scale": L,
-                       "pool_factors": factors, "rows_quantised": rows},
+                       "pool_factors": factors, "rows_quantised": rows, "upsample": a.upsample,
+                       "phi": bool(a.phi)},
             "e2e": {"value": B * T / (ms_e2e * 1e-3), "unit": "vectors/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": codes_host.numel() * 4},
             "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel (all 40 levels)", "achieved": achieved,
@@ -457,9 +470,11 @@ def run_secondary(a):
                          "peak_source": f"{peak_kind} bf16_tflops (burst; a 2-3 ms step)",
                          "argmin_ms_per_step": am_ms / a.steps, "linear_ms_per_step": ln_ms / a.steps,
                          "linear_tflops": proj_flops / (ln_ms / a.steps * 1e-3) / 1e12,
-                         "share_argmin": am_ms / max(prof["*"][0] + am_ms + ln_ms, 1e-9),
+                         "conv_tflops": (2.0 * B * T * 3 * D * D * S / (prof["conv_k3"][0] / a.steps * 1e-3) / 1e12
+                                         if a.phi and prof["conv_k3"][0] > 0 else None),
+                         "share_argmin": am_ms / max(sum(v[0] for v in prof.values()), 1e-9),
                          "ms_per_step_by_kernel": {k: v[0] / a.steps for k, v in prof.items()}},
-            "gpu_launches": int(am_n + prof["linear_bf16"][1] + prof["*"][1]), "clocks": clocks})
+            "gpu_launches": int(sum(v[1] for v in prof.values())), "clocks": clocks})
     elif a.workload == "linear":
         Ms = [1, 64, 512, 4096, 8192]
         KNs = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)]

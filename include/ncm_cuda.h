@@ -112,6 +112,15 @@ NCM_API int ncm_code_sqnorm(ncm_ctx_t* ctx, const uint16_t* codebook, float* sqn
 NCM_API int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, const float* sqnorm,
                   int32_t* codes, int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
 
+/* ncm_rvq_level that also reports each row's top-2 distance gap (the near-tie
+ * measure of the parity rule; vq_forward_semantics.md:81):
+ *   top2_gap[n] = (d2 - d1) / (||bf16(r_n)||^2 + d1)
+ * where d1 <= d2 are the two smallest GEMM distances sqnorm[k] - 2 bf16(r_n) . e_k
+ * of row n (so ||bf16(r_n)||^2 + d1 is the best full squared distance). Codes
+ * and the residual update equal ncm_rvq_level's. top2_gap [N] f32 device. */
+NCM_API int ncm_rvq_level_top2(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, const float* sqnorm,
+                               int32_t* codes, float* top2_gap, int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
 /* L residual levels over x (vq_forward_semantics.md:59-82 at a single scale):
  * residual = f32(x); for l: ncm_rvq_level(codebooks[l]).
  * x [N,D] bf16; codebooks [L,K,D] bf16; sqnorms [L,K] f32 or NULL (computed);

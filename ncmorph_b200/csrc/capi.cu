@@ -128,7 +128,7 @@ bool make_tmap_bf16_2d_strided(CUtensorMap* map, const void* base, uint64_t rows
 static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* src_bf16, float* resid,
                           uint16_t* shadow, const uint16_t* codebook, const float* sqnorm, int32_t* codes,
                           RvqPartial* part, const RvqPlan& plan, int64_t N, int64_t D, int64_t K, bool update,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const RvqTop2* top2 = nullptr) {
   CUtensorMap tmA, tmB;
   if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, D, 256))
     return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
@@ -139,12 +139,12 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
   {
     Launch _launch(ctx, KID_RVQ_ARGMIN, stream);
     NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, sqnorm, codes, part, ctx->d_err, N, D, K, stream,
-                                   fused ? &fu : nullptr));
+                                   fused ? &fu : nullptr, top2));
   }
   if (plan.splits > 1 || (update && !fused)) {
     Launch _launch(ctx, KID_RVQ_APPLY, stream);
     NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, src_bf16, resid, shadow, codebook, ctx->d_err, N, D, K, update,
-                                  stream));
+                                  stream, top2));
   }
   return NCM_OK;
 }
@@ -430,6 +430,49 @@ int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, con
   }
   return rvq_level_core(ctx, shadow, nullptr, residual, nullptr, codebook, sqnorm, codes,
                         reinterpret_cast<RvqPartial*>(ws + o_part), plan, N, D, K, true, st);
+}
+
+int ncm_rvq_level_top2(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, const float* sqnorm,
+                       int32_t* codes, float* top2_gap, int64_t N, int64_t D, int64_t K, ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if ((rc = check_rvq_shape(N, D, K))) return rc;
+  if (!residual || !codebook || !codes || !top2_gap) return ncm_fail(NCM_EINVAL, "rvq_level_top2: null buffer");
+  if (!aligned16(residual) || !aligned16(codebook) || !aligned16(codes) || (sqnorm && !aligned16(sqnorm)) ||
+      (reinterpret_cast<uintptr_t>(top2_gap) & 3u))
+    return ncm_fail(NCM_EINVAL, "rvq_level_top2: misaligned buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K);
+  WsCarver cv;
+  const size_t o_sh = cv.take(2 * N * D);
+  const size_t o_part = cv.take(plan.partial_bytes);
+  const size_t o_sq = cv.take(sizeof(float) * K);
+  const size_t o_a2 = cv.take(sizeof(float) * N);
+  const size_t o_d2 = cv.take(plan.splits > 1 ? sizeof(float) * plan.splits * N : 0);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_level_top2: workspace allocation failed");
+  uint16_t* shadow = reinterpret_cast<uint16_t*>(ws + o_sh);
+  if (sqnorm == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    {
+      Launch _launch(ctx, KID_SQNORM, st);
+      NCM_CUDA_TRY(launch_code_sqnorm(codebook, sq, K, D, st));
+    }
+    sqnorm = sq;
+  }
+  {
+    Launch _launch(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(residual, shadow, N * D, st));
+  }
+  float* a2 = reinterpret_cast<float*>(ws + o_a2);
+  {
+    // ||bf16(r)||^2 per row: the same exact f64 sum of squares as the code norms
+    Launch _launch(ctx, KID_SQNORM, st);
+    NCM_CUDA_TRY(launch_code_sqnorm(shadow, a2, N, D, st));
+  }
+  RvqTop2 top2{top2_gap, a2, reinterpret_cast<float*>(ws + o_d2)};
+  return rvq_level_core(ctx, shadow, nullptr, residual, nullptr, codebook, sqnorm, codes,
+                        reinterpret_cast<RvqPartial*>(ws + o_part), plan, N, D, K, true, st, &top2);
 }
 
 int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks, const float* sqnorms, int32_t L,

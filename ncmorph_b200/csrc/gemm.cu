@@ -3,8 +3,10 @@
 // Same pipeline skeleton as the RVQ distance kernel: persistent CTAs (one per
 // SM), warp 0 issues TMA loads of 128-byte-swizzled K-major tiles into a
 // multi-stage mbarrier ring, warp 1 issues tcgen05.mma (bf16 x bf16 -> f32 in
-// tensor memory), warps 2-5 drain the double-buffered TMEM accumulator, add
-// the bias in f32, round once to bf16 and store.
+// tensor memory), warps 2-9 drain the double-buffered TMEM accumulator (two
+// warps per TMEM lane quarter, alternating 16-column chunks, so twice the
+// global accesses are in flight), add the bias in f32, round once to bf16 and
+// store.
 //
 // Skinny problems (M <= 64 tokens: decode-time GEMV shapes) run "swapped":
 // the 128-row MMA operand is the weight and the token rows form the narrow N
@@ -20,7 +22,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, interleaving 16-column chunks
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
 
 template <int BN>
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S.tfull[b], 1);
-      mbar_init(&S.tempty[b], 4);
+      mbar_init(&S.tempty[b], EPI_WARPS);
     }
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     const int q = warp & 3;
+    const int c0 = ((warp - 2) >> 2) * 16;  // first 16-column chunk of this warp; chunks step by 32
     uint32_t acc_it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int m = arow;
         const int n0 = tb * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
+        for (int c = c0; c < BN / 2; c += 32) {
           uint32_t g[16], u[16];
           tmem_ld_x16(tbase + c, g);
           tmem_ld_x16(tbase + BN / 2 + c, u);
@@ -253,26 +257,40 @@ __global__ void __launch_bounds__(THREADS, 1)
         const long long m = arow < args.M ? args.map.real_row(arow) : -1;
         const ConvEpilogue& ep = args.conv;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = c0; c < BN; c += 32) {
           uint32_t v[16];
           tmem_ld_x16(tbase + c, v);
+          const int n0 = tb * BN + c;
+          const size_t o = static_cast<size_t>(m < 0 ? 0 : m) * args.N + n0;
+          const bool vec = m >= 0 && args.vec_ok && n0 + 16 <= args.N;
+          // issue this chunk's global reads before waiting for the tensor-memory load
+          float4 xv[4], rv[4], av[4], bv[4];
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              xv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (ep.x_f32 != nullptr) {
+                xv[j] = *reinterpret_cast<const float4*>(ep.x_f32 + o + 4 * j);
+              } else if (ep.x_bf16 != nullptr) {
+                const uint2 h = *reinterpret_cast<const uint2*>(ep.x_bf16 + o + 4 * j);
+                xv[j] = make_float4(bf16lo(h.x), bf16hi(h.x), bf16lo(h.y), bf16hi(h.y));
+              }
+              rv[j] = ep.resid != nullptr ? *reinterpret_cast<const float4*>(ep.resid + o + 4 * j)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+              av[j] = ep.acc_f32 != nullptr ? *reinterpret_cast<const float4*>(ep.acc_f32 + o + 4 * j)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+              bv[j] = ep.bias != nullptr ? __ldg(reinterpret_cast<const float4*>(ep.bias + n0 + 4 * j))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
           tmem_wait_ld();
           if (m < 0) continue;
-          const int n0 = tb * BN + c;
-          const size_t o = static_cast<size_t>(m) * args.N + n0;
-          if (args.vec_ok && n0 + 16 <= args.N) {
+          if (vec) {
             // 16-byte accesses (N % 4 == 0 and every buffer 16-byte aligned)
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (ep.x_f32 != nullptr) {
-                x = *reinterpret_cast<const float4*>(ep.x_f32 + o + j);
-              } else if (ep.x_bf16 != nullptr) {
-                const uint2 h = *reinterpret_cast<const uint2*>(ep.x_bf16 + o + j);
-                x = make_float4(bf16lo(h.x), bf16hi(h.x), bf16lo(h.y), bf16hi(h.y));
-              }
-              float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (ep.bias != nullptr) b = __ldg(reinterpret_cast<const float4*>(ep.bias + n0 + j));
+            for (int j4 = 0; j4 < 4; ++j4) {
+              const int j = 4 * j4;
+              const float4 x = xv[j4], b = bv[j4];
               float4 val;
               val.x = fmaf(ep.alpha, x.x, ep.beta * (__uint_as_float(v[j]) + b.x));
               val.y = fmaf(ep.alpha, x.y, ep.beta * (__uint_as_float(v[j + 1]) + b.y));
@@ -283,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 *reinterpret_cast<uint2*>(ep.out_bf16 + o + j) =
                     make_uint2(pack_bf16x2(val.x, val.y), pack_bf16x2(val.z, val.w));
               if (ep.resid != nullptr) {
-                float4 r = *reinterpret_cast<const float4*>(ep.resid + o + j);
+                float4 r = rv[j4];
                 r.x -= val.x;
                 r.y -= val.y;
                 r.z -= val.z;
@@ -291,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 *reinterpret_cast<float4*>(ep.resid + o + j) = r;
               }
               if (ep.acc_f32 != nullptr) {
-                float4 a = *reinterpret_cast<const float4*>(ep.acc_f32 + o + j);
+                float4 a = av[j4];
                 a.x += val.x;
                 a.y += val.y;
                 a.z += val.z;
@@ -320,24 +338,46 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       } else
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = c0; c < BN; c += 32) {
         uint32_t v[16];
         tmem_ld_x16(tbase + c, v);
+        // non-swapped rows: issue the bias and residual reads before waiting for the TMEM load
+        const int n0 = tb * BN + c;
+        const bool vrow = !SWAP && arow < args.M && args.vec_ok && n0 + 16 <= args.N;
+        const size_t o = static_cast<size_t>(arow) * args.N + n0;
+        uint4 h0 = make_uint4(0u, 0u, 0u, 0u), h1 = h0, bb0 = h0, bb1 = h0;
+        if (vrow) {
+          if (args.mode == 2) {
+            h0 = *reinterpret_cast<const uint4*>(args.y + o);
+            h1 = *reinterpret_cast<const uint4*>(args.y + o + 8);
+          }
+          if (args.bias != nullptr) {
+            bb0 = __ldg(reinterpret_cast<const uint4*>(args.bias + n0));
+            bb1 = __ldg(reinterpret_cast<const uint4*>(args.bias + n0 + 8));
+          }
+        }
         tmem_wait_ld();
         if (!SWAP) {
           // arow = token m, columns = outputs n
           const int m = arow;
-          const int n0 = tb * BN + c;
           if (m < args.M) {
             float f[16];
+            if (vrow) {
+              const uint32_t bp[8] = {bb0.x, bb0.y, bb0.z, bb0.w, bb1.x, bb1.y, bb1.z, bb1.w};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = n0 + j;
-              float acc = __uint_as_float(v[j]);
-              if (args.bias != nullptr && n < args.N) acc += bf16_to_f32(__ldg(args.bias + n));
-              f[j] = acc;
+              for (int j = 0; j < 8; ++j) {
+                f[2 * j] = __uint_as_float(v[2 * j]) + bf16lo(bp[j]);
+                f[2 * j + 1] = __uint_as_float(v[2 * j + 1]) + bf16hi(bp[j]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int n = n0 + j;
+                float acc = __uint_as_float(v[j]);
+                if (args.bias != nullptr && n < args.N) acc += bf16_to_f32(__ldg(args.bias + n));
+                f[j] = acc;
+              }
             }
-            const size_t o = static_cast<size_t>(m) * args.N + n0;
             if (args.mode == 2) {
               // residual add (decoder.zig:310-313): y = bf16(y + bf16(acc + bias))
 #pragma unroll
@@ -346,9 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 f[j] = bf16lo(r);
                 f[j + 1] = bf16hi(r);
               }
-              if (args.vec_ok && n0 + 16 <= args.N) {
-                const uint4 h0 = *reinterpret_cast<const uint4*>(args.y + o);
-                const uint4 h1 = *reinterpret_cast<const uint4*>(args.y + o + 8);
+              if (vrow) {
                 const uint32_t hp[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -462,7 +500,8 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
-  a.vec_ok = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+  a.vec_ok = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0) &&
+             ((reinterpret_cast<uintptr_t>(bias) & 15) == 0);
   const bool swap = M <= 64;
   CUtensorMap tmA, tmB;
   int bn;

@@ -147,18 +147,28 @@ struct RvqFusedUpdate {
   const uint16_t* codebook;
 };
 
+// Optional top-2 gap output: gap[n] = (d2 - d1) / (a2[n] + d1) with d1 <= d2
+// the two smallest GEMM distances of row n and a2 = ||bf16(r_n)||^2;
+// part_d2 ([splits, N] f32) carries each split's second-smallest distance.
+struct RvqTop2 {
+  float* gap;
+  const float* a2;
+  float* part_d2;
+};
+
 // argmin_k (sqnorm[k] - 2 a_n . e_k) over bf16 rows `a` [N,D] (via tmA) and
 // codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials, and
 // applies `fu` when given and the plan has one split.
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
-                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu = nullptr);
+                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu = nullptr,
+                              const RvqTop2* top2 = nullptr);
 
 // Final code per row (reducing partials when splits > 1), then
 // resid = (src_bf16 ? f32(src_bf16) : resid) - e[code]; shadow = bf16(resid).
 cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_t* codes, const uint16_t* src_bf16,
                              float* resid, uint16_t* shadow, const uint16_t* codebook, int* err, int64_t N,
-                             int64_t D, int64_t K, bool update, cudaStream_t stream);
+                             int64_t D, int64_t K, bool update, cudaStream_t stream, const RvqTop2* top2 = nullptr);
 
 cudaError_t launch_code_sqnorm(const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D, cudaStream_t stream);
 cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, int L, uint16_t* recon_bf16,

@@ -70,13 +70,25 @@ struct ArgminArgs {
   const uint16_t* src_bf16;  // level input in bf16 (level 0), else null: read resid
   uint16_t* shadow;          // bf16(resid) for the next level, or null
   const uint16_t* codebook;
+  // top-2 gap (the GAP instantiation only)
+  float* gap;        // [N] relative gap, splits == 1
+  const float* a2;   // [N] ||bf16(r)||^2
+  float* part_d2;    // [splits, N] second-smallest distance of each split
 };
+
+// (second - best) / (||a||^2 + best): the top-2 gap relative to the best full
+// squared distance (||r||^2 is the constant the GEMM distance leaves out).
+__device__ __forceinline__ float rel_gap(float s1, float s2, float a2) {
+  return (s2 - s1) / fmaxf(a2 + s1, 1e-30f);
+}
 
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err) {
   *abort_flag = 1;
   atomicOr(err, kErrWaitTimeout);
 }
 
+// GAP: also track the second-smallest distance per row for the top-2 gap.
+template <bool GAP>
 __global__ void __launch_bounds__(THREADS, 1)
     rvq_argmin_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const ArgminArgs args) {
@@ -222,6 +234,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = rb * BM + q * 32 + lane;
       float best = INFINITY;
       int bidx = t0 * BN;
+      float s1 = INFINITY, s2 = INFINITY;  // GAP: smallest and second-smallest distance
       for (int t = t0; t < t1; ++t) {
         const uint32_t b = acc_it & 1u;
         const uint32_t ap = (acc_it >> 1) & 1u;
@@ -257,6 +270,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[4 * j4 + 2] = __float_as_uint(d2);
             v[4 * j4 + 3] = __float_as_uint(d3);
             m = fminf(m, fminf(fminf(d0, d1), fminf(d2, d3)));
+            if constexpr (GAP) {
+              s2 = fminf(s2, fmaxf(s1, d0));
+              s1 = fminf(s1, d0);
+              s2 = fminf(s2, fmaxf(s1, d1));
+              s1 = fminf(s1, d1);
+              s2 = fminf(s2, fmaxf(s1, d2));
+              s1 = fminf(s1, d2);
+              s2 = fminf(s2, fmaxf(s1, d3));
+              s1 = fminf(s1, d3);
+            }
           }
           if (m < best) {  // strict: an equal distance from a lower code keeps its place
             int jj = 0;
@@ -275,8 +298,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (row < args.N) {
         if (args.splits == 1) {
           args.codes[row] = bidx;
+          if constexpr (GAP) args.gap[row] = rel_gap(s1, s2, args.a2[row]);
         } else {
           args.part[static_cast<size_t>(sp) * args.N + row] = RvqPartial{best, bidx};
+          if constexpr (GAP) args.part_d2[static_cast<size_t>(sp) * args.N + row] = s2;
         }
       }
       if (args.fuse) {
@@ -365,6 +390,9 @@ struct ApplyArgs {
   int* err;
   int N, D, K;
   int update;
+  float* gap;            // [N] relative top-2 gap, or null
+  const float* a2;       // [N] ||bf16(r)||^2 (with gap)
+  const float* part_d2;  // [splits, N] second-smallest distance per split (with gap)
 };
 
 __global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
@@ -394,6 +422,24 @@ __global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
     code = bi;
     if (code == INT_MAX) code = a.part[row].idx;  // every distance was NaN/inf
     if (lane == 0) a.codes[row] = code;
+    if (a.gap != nullptr) {
+      // the two smallest distances over all splits: merge (smallest, second) pairs
+      float s1 = INFINITY, s2 = INFINITY;
+      for (int s = lane; s < a.splits; s += 32) {
+        const float d1 = a.part[static_cast<size_t>(s) * a.N + row].d;
+        const float d2 = a.part_d2[static_cast<size_t>(s) * a.N + row];
+        s2 = fminf(fmaxf(s1, d1), fminf(s2, d2));
+        s1 = fminf(s1, d1);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float o1 = __shfl_xor_sync(0xffffffffu, s1, o);
+        const float o2 = __shfl_xor_sync(0xffffffffu, s2, o);
+        s2 = fminf(fmaxf(s1, o1), fminf(s2, o2));
+        s1 = fminf(s1, o1);
+      }
+      if (lane == 0) a.gap[row] = rel_gap(s1, s2, a.a2[row]);
+    }
   } else {
     code = a.codes[row];
   }
@@ -670,18 +716,23 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
 
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
-                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu) {
-  // the shared-memory opt-in is per device: remember which devices have it
-  static unsigned long long attr_set = 0;
+                              int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu,
+                              const RvqTop2* top2) {
+  // the shared-memory opt-in is per device and per instantiation: remember which devices have it
+  static unsigned long long attr_set[2] = {0, 0};
+  const int gi = top2 != nullptr ? 1 : 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 64 || !(attr_set & (1ull << dev))) {
-    e = cudaFuncSetAttribute(rvq_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ARGMIN_SMEM);
+  if (dev >= 64 || !(attr_set[gi] & (1ull << dev))) {
+    e = gi ? cudaFuncSetAttribute(rvq_argmin_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)ARGMIN_SMEM)
+           : cudaFuncSetAttribute(rvq_argmin_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)ARGMIN_SMEM);
     if (e != cudaSuccess) return e;
-    if (dev < 64) attr_set |= 1ull << dev;
+    if (dev < 64) attr_set[gi] |= 1ull << dev;
   }
-  ArgminArgs a;
+  ArgminArgs a{};
   a.csq = sqnorm;
   a.codes = codes;
   a.part = part;
@@ -698,15 +749,27 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.src_bf16 = fu ? fu->src_bf16 : nullptr;
   a.shadow = fu ? fu->shadow : nullptr;
   a.codebook = fu ? fu->codebook : nullptr;
-  rvq_argmin_kernel<<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+  if (top2 != nullptr) {
+    a.gap = top2->gap;
+    a.a2 = top2->a2;
+    a.part_d2 = top2->part_d2;
+    rvq_argmin_kernel<true><<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+  } else {
+    rvq_argmin_kernel<false><<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_t* codes, const uint16_t* src_bf16,
                              float* resid, uint16_t* shadow, const uint16_t* codebook, int* err, int64_t N,
-                             int64_t D, int64_t K, bool update, cudaStream_t stream) {
+                             int64_t D, int64_t K, bool update, cudaStream_t stream, const RvqTop2* top2) {
   if (plan.splits == 1 && !update) return cudaSuccess;
-  ApplyArgs a;
+  ApplyArgs a{};
+  if (top2 != nullptr && plan.splits > 1) {
+    a.gap = top2->gap;
+    a.a2 = top2->a2;
+    a.part_d2 = top2->part_d2;
+  }
   a.part = part;
   a.splits = plan.splits;
   a.codes = codes;

@@ -52,6 +52,22 @@ def rvq_level(residual: torch.Tensor, codebook: torch.Tensor, sqnorm: torch.Tens
     return codes
 
 
+def rvq_level_top2(residual: torch.Tensor, codebook: torch.Tensor, sqnorm: torch.Tensor | None = None):
+    """rvq_level that also returns each row's relative top-2 distance gap
+    (d2 - d1) / (||bf16(r)||^2 + d1). Returns (codes int32 [N], gap f32 [N])."""
+    N, D = residual.shape
+    K = codebook.shape[0]
+    need(residual, torch.float32, "residual")
+    need(codebook, bf16, "codebook", (K, D))
+    if sqnorm is not None:
+        need(sqnorm, torch.float32, "sqnorm", (K,))
+    codes = torch.empty(N, dtype=torch.int32, device=residual.device)
+    gap = torch.empty(N, dtype=torch.float32, device=residual.device)
+    _lib.call("ncm_rvq_level_top2", context(residual.device), ptr(residual), ptr(codebook), ptr(sqnorm), ptr(codes),
+              ptr(gap), N, D, K, stream_of(residual))
+    return codes, gap
+
+
 def rvq_encode(x: torch.Tensor, codebooks: torch.Tensor, sqnorms: torch.Tensor | None = None, *,
                want_recon: bool = True, want_residual: bool = False,
                codes: torch.Tensor | None = None, recon: torch.Tensor | None = None):

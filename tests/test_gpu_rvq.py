@@ -156,3 +156,36 @@ def test_argument_validation(cuda_dev):
     with pytest.raises(_lib.NcmError) as ei:
         vq.rvq_level(r, cb)
     assert ei.value.status == _lib.NCM_EINVAL
+
+
+@pytest.mark.parametrize("N,D,K", [(300, 64, 5000), (148 * 128 + 37, 128, 512), (1000, 136, 700)])
+def test_rvq_level_top2_gap_matches_oracle(orc, cuda_dev, N, D, K):
+    """Top-2 gap output (code-split and fused plans): the same codes and residual
+    as ncm_rvq_level, and the oracle's relative gap within accumulation noise."""
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(N + 3 * K)
+    r = rng.standard_normal((N, D)).astype(np.float32)
+    cb = gen_bf16(rng, (K, D))
+    cbd = to_dev_bf16(cb, cuda_dev)
+    r1 = torch.from_numpy(r).to(cuda_dev)
+    r2 = r1.clone()
+    codes, gap = vq.rvq_level_top2(r1, cbd)
+    plain = vq.rvq_level(r2, cbd)
+    assert torch.equal(codes, plain) and torch.equal(r1, r2)
+    r_orc = r.copy()
+    best, ogap = orc.rvq_level(r_orc, cb, orc.code_sqnorm(cb), codes_in=codes.cpu().numpy())
+    g = gap.cpu().numpy()
+    assert np.all(g >= 0)
+    assert np.abs(g - ogap).max() <= 1e-4, np.abs(g - ogap).max()
+
+
+def test_rvq_level_top2_duplicate_codeword_gap_is_zero(cuda_dev):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(6)
+    base = gen_bf16(rng, (300, 64))
+    cb = np.concatenate([base, base[[7]]])
+    from oracle import pyoracle as orc
+    r = orc.bf16_widen(base[[7, 7, 3]]).astype(np.float32).copy()
+    codes, gap = vq.rvq_level_top2(torch.from_numpy(r).to(cuda_dev), to_dev_bf16(cb, cuda_dev))
+    assert codes.tolist()[:2] == [7, 7]
+    assert gap.tolist()[:2] == [0.0, 0.0] and gap.tolist()[2] > 0
