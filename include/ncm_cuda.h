@@ -228,6 +228,25 @@ NCM_API int ncm_multiscale_decode(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                                   const uint16_t* codebooks, const uint16_t* phi_weight, const float* phi_bias,
                                   uint16_t* recon, ncm_stream_t stream);
 
+/* ------------------------------------------- codebook-tied output head */
+
+/* _TiedCodebookHead (PROJECT.md:222, decision D18): per predicted level,
+ *   logits[t,k] = (2 z_t . E_k - E_sq[k]) / d_scale * exp(log_inv_T) + bias[k]
+ * with E_sq[k] = sum_d E[k,d]^2 and d_scale = mean_k E_sq[k]. z [T, d] bf16 (the
+ * head's Linear(n_embd -> d) output, e.g. from ncm_linear_bf16), codebook E
+ * [K, d] bf16, esq [K] f32 or NULL (computed), bias [K] f32 or NULL. The dot
+ * products run on tcgen05 (bf16 operands, f32 accumulation). d % 8 == 0. */
+NCM_API int ncm_tied_head_logits(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
+                                 const float* bias, float log_inv_T, float* logits, int64_t T, int64_t d, int64_t K,
+                                 ncm_stream_t stream);
+
+/* codes[t] = argmax_k logits[t,k] (lowest k among equal values), the
+ * temperature-0 pick of _sample_level_raw, without materialising the logits:
+ * the argmin runs in the distance GEMM's epilogue as in ncm_rvq_level. */
+NCM_API int ncm_tied_head_argmax(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
+                                 const float* bias, float log_inv_T, int32_t* codes, int64_t T, int64_t d, int64_t K,
+                                 ncm_stream_t stream);
+
 /* -------------------------------------- L3-L6: NCM decoder forward pieces */
 
 /* Row-wise bf16 RMSNorm: y = bf16(bf16(x * inv) * bf16(w)), inv = 1/sqrt(mean(x^2) + eps)

@@ -126,6 +126,8 @@ SIGNATURES: dict[str, list] = {
                                  c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "ncm_multiscale_decode": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "ncm_rvq_level_top2": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_tied_head_logits": [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_tied_head_argmax": [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_upsample": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_conv1d_k3": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, ctypes.c_float, ctypes.c_float,
                       c_vp],

@@ -63,6 +63,11 @@ struct LinearArgs {
   int taps, nk_tap;
   ConvEpilogue conv;
   SegMap map;
+  // mode 4 (codebook-tied head logits into y_f32): esq [N], bias [N] or null,
+  // scal = {d_scale, exp(log_inv_T)} on the device
+  const float* head_esq;
+  const float* head_bias;
+  const float* head_scal;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& ta, int& tb) {
@@ -250,6 +255,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint16_t* dst = args.y + static_cast<size_t>(m) * args.F + n0 + c;
             *reinterpret_cast<uint4*>(dst) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
             *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          }
+        }
+      } else if (!SWAP && args.mode == 4) {
+        // logits = (2 acc - esq) / d_scale * exp(log_inv_T) + bias (_TiedCodebookHead)
+        const float dsc = __ldg(args.head_scal), esc = __ldg(args.head_scal + 1);
+        const int m = arow;
+#pragma unroll 1
+        for (int c = c0; c < BN; c += 32) {
+          uint32_t v[16];
+          tmem_ld_x16(tbase + c, v);
+          tmem_wait_ld();
+          if (m >= args.M) continue;
+          const int n0 = tb * BN + c;
+          float* dst = args.y_f32 + static_cast<size_t>(m) * args.N + n0;
+          if (args.vec_ok && n0 + 16 <= args.N) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 e = __ldg(reinterpret_cast<const float4*>(args.head_esq + n0 + j));
+              const float4 bb = args.head_bias != nullptr
+                                    ? __ldg(reinterpret_cast<const float4*>(args.head_bias + n0 + j))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+              float4 l;
+              l.x = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j]), -e.x), dsc), esc) + bb.x;
+              l.y = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 1]), -e.y), dsc), esc) + bb.y;
+              l.z = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 2]), -e.z), dsc), esc) + bb.z;
+              l.w = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 3]), -e.w), dsc), esc) + bb.w;
+              *reinterpret_cast<float4*>(dst + j) = l;
+            }
+          } else {
+            for (int j = 0; j < 16 && n0 + j < args.N; ++j) {
+              const float t = fmaf(2.f, __uint_as_float(v[j]), -__ldg(args.head_esq + n0 + j));
+              dst[j] = __fmul_rn(__fdiv_rn(t, dsc), esc) +
+                       (args.head_bias != nullptr ? __ldg(args.head_bias + n0 + j) : 0.f);
+            }
           }
         }
       } else if (!SWAP && args.mode == 3) {
@@ -549,6 +588,49 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
       case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
       default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
     }
+  }
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  return NCM_OK;
+}
+
+int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
+                          const float* bias, const float* scal, float* logits, int64_t T, int64_t d, int64_t K,
+                          cudaStream_t stream) {
+  LinearArgs a{};
+  a.mode = 4;
+  a.taps = 1;
+  a.err = ctx->d_err;
+  a.M = static_cast<int>(T);
+  a.N = static_cast<int>(K);
+  a.K = static_cast<int>(d);
+  a.y_f32 = logits;
+  a.head_esq = esq;
+  a.head_bias = bias;
+  a.head_scal = scal;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  a.vec_ok = K % 4 == 0 && al(logits) && al(esq) && al(bias);
+  const long long mt = ceil_div(T, BM);
+  int bn;
+  if (mt * ceil_div(K, 256) >= ctx->num_sms)
+    bn = 256;
+  else if (mt * ceil_div(K, 128) >= ctx->num_sms)
+    bn = 128;
+  else
+    bn = 64;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_bf16_2d(&tmA, z, T, d, BM) || !make_tmap_bf16_2d(&tmB, codebook, K, d, bn))
+    return ncm_fail(NCM_EINVAL, "tied head: tensor map encoding failed (T=%lld d=%lld K=%lld)", (long long)T,
+                    (long long)d, (long long)K);
+  a.tiles_a = static_cast<int>(mt);
+  a.tiles_b = ceil_div(K, bn);
+  a.a_fast = double(T) <= double(K) ? 1 : 0;
+  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
+  cudaError_t e;
+  Launch _launch(ctx, KID_LINEAR, stream);
+  switch (bn) {
+    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
+    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
+    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
   }
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
   return NCM_OK;

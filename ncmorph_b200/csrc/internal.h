@@ -157,12 +157,13 @@ struct RvqTop2 {
 };
 
 // argmin_k (sqnorm[k] - 2 a_n . e_k) over bf16 rows `a` [N,D] (via tmA) and
+// (with mul_dev: argmin_k fmaf(*mul_dev, a_n . e_k, sqnorm[k]), the tied head's form)
 // codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials, and
 // applies `fu` when given and the plan has one split.
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu = nullptr,
-                              const RvqTop2* top2 = nullptr);
+                              const RvqTop2* top2 = nullptr, const float* mul_dev = nullptr);
 
 // Final code per row (reducing partials when splits > 1), then
 // resid = (src_bf16 ? f32(src_bf16) : resid) - e[code]; shadow = bf16(resid).
@@ -199,6 +200,13 @@ int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16
 // bf16(y + bf16(x.w^T + bias)).
 int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
                    float* y_f32, int64_t M, int64_t K, int64_t N, cudaStream_t stream, int mode, int64_t F);
+
+// ---- codebook-tied head (head.cu, gemm.cu)
+// logits [T, K] f32 = (2 z.E^T - esq) / scal[0] * scal[1] + bias, z [T, d] and
+// E [K, d] bf16; scal = {d_scale, exp(log_inv_T)} in device memory.
+int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
+                          const float* bias, const float* scal, float* logits, int64_t T, int64_t d, int64_t K,
+                          cudaStream_t stream);
 
 // ---- kernel-3 convolution over row segments (conv.cu, gemm.cu)
 //

@@ -70,6 +70,8 @@ struct ArgminArgs {
   const uint16_t* src_bf16;  // level input in bf16 (level 0), else null: read resid
   uint16_t* shadow;          // bf16(resid) for the next level, or null
   const uint16_t* codebook;
+  // dist = fmaf(mul, acc, csq[k]); mul = -2 (RVQ) or *mul_dev when given (tied head)
+  const float* mul_dev;
   // top-2 gap (the GAP instantiation only)
   float* gap;        // [N] relative gap, splits == 1
   const float* a2;   // [N] ||bf16(r)||^2
@@ -223,6 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // -------------------------------------------------- argmin epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     float* csq_s = S.csq[warp - 2];
+    const float mul = args.mul_dev != nullptr ? __ldg(args.mul_dev) : -2.f;
     uint32_t acc_it = 0;
     uint32_t uit = 0;  // units handed to the update warps
     bool ok = true;
@@ -261,10 +264,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 cv = cs4[j4];
-            const float d0 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 0]), cv.x);
-            const float d1 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 1]), cv.y);
-            const float d2 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 2]), cv.z);
-            const float d3 = fmaf(-2.f, __uint_as_float(v[4 * j4 + 3]), cv.w);
+            const float d0 = fmaf(mul, __uint_as_float(v[4 * j4 + 0]), cv.x);
+            const float d1 = fmaf(mul, __uint_as_float(v[4 * j4 + 1]), cv.y);
+            const float d2 = fmaf(mul, __uint_as_float(v[4 * j4 + 2]), cv.z);
+            const float d3 = fmaf(mul, __uint_as_float(v[4 * j4 + 3]), cv.w);
             v[4 * j4 + 0] = __float_as_uint(d0);
             v[4 * j4 + 1] = __float_as_uint(d1);
             v[4 * j4 + 2] = __float_as_uint(d2);
@@ -717,7 +720,7 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu,
-                              const RvqTop2* top2) {
+                              const RvqTop2* top2, const float* mul_dev) {
   // the shared-memory opt-in is per device and per instantiation: remember which devices have it
   static unsigned long long attr_set[2] = {0, 0};
   const int gi = top2 != nullptr ? 1 : 0;
@@ -749,6 +752,7 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.src_bf16 = fu ? fu->src_bf16 : nullptr;
   a.shadow = fu ? fu->shadow : nullptr;
   a.codebook = fu ? fu->codebook : nullptr;
+  a.mul_dev = mul_dev;
   if (top2 != nullptr) {
     a.gap = top2->gap;
     a.a2 = top2->a2;

@@ -186,3 +186,36 @@ def apply_post_upsample_conv(input: np.ndarray, weight: np.ndarray, bias: np.nda
             raise ValueError(f"{name} has {a.size} elements, expected {n}")
     _lib.call("ncm_post_upsample_conv_host_f32", context(device), ctypes.c_void_p(input.ctypes.data),
               ctypes.c_void_p(weight.ctypes.data), ctypes.c_void_p(bias.ctypes.data), row_count, width)
+
+
+def tied_head_logits(z: torch.Tensor, codebook: torch.Tensor, log_inv_T: float = 0.0,
+                     bias: torch.Tensor | None = None, esq: torch.Tensor | None = None) -> torch.Tensor:
+    """_TiedCodebookHead (PROJECT.md:222): logits [T, K] f32 =
+    (2 z.E^T - E_sq) / mean(E_sq) * exp(log_inv_T) + bias, z [T, d] bf16, E [K, d] bf16."""
+    T, d = z.shape
+    K = codebook.shape[0]
+    need(z, bf16, "z")
+    need(codebook, bf16, "codebook", (K, d))
+    for t, name in ((bias, "bias"), (esq, "esq")):
+        if t is not None:
+            need(t, torch.float32, name, (K,))
+    out = torch.empty((T, K), dtype=torch.float32, device=z.device)
+    _lib.call("ncm_tied_head_logits", context(z.device), ptr(z), ptr(codebook), ptr(esq), ptr(bias),
+              float(log_inv_T), ptr(out), T, d, K, stream_of(z))
+    return out
+
+
+def tied_head_argmax(z: torch.Tensor, codebook: torch.Tensor, log_inv_T: float = 0.0,
+                     bias: torch.Tensor | None = None, esq: torch.Tensor | None = None) -> torch.Tensor:
+    """argmax_k of tied_head_logits (lowest k on ties) without materialising the logits -> int32 [T]."""
+    T, d = z.shape
+    K = codebook.shape[0]
+    need(z, bf16, "z")
+    need(codebook, bf16, "codebook", (K, d))
+    for t, name in ((bias, "bias"), (esq, "esq")):
+        if t is not None:
+            need(t, torch.float32, name, (K,))
+    codes = torch.empty(T, dtype=torch.int32, device=z.device)
+    _lib.call("ncm_tied_head_argmax", context(z.device), ptr(z), ptr(codebook), ptr(esq), ptr(bias),
+              float(log_inv_T), ptr(codes), T, d, K, stream_of(z))
+    return codes

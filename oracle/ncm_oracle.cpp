@@ -815,4 +815,48 @@ void orc_scale_update_ex(const int32_t* codes, const uint16_t* cbs, size_t L, fl
   }
 }
 
+// Codebook-tied head (_TiedCodebookHead, PROJECT.md:222), in the module's
+// operation order: neg_d2 = (2 z.E^T - E_sq) / d_scale; logits = neg_d2 *
+// exp(log_inv_T) + bias. d_scale = mean(E_sq) (f64 sum of the f32 norms);
+// each dot product is an exact f64 sum of bf16 products rounded to f32.
+// With codes/gap non-null also the argmax (lowest k on ties) and the top-2
+// logit gap per row.
+void orc_tied_head(const float* z, const uint16_t* cb, const float* esq_in, const float* bias, float log_inv_T,
+                   float* logits, int32_t* codes, float* gap, size_t T, size_t d, size_t K) {
+  std::vector<float> esq(K);
+  if (esq_in != nullptr)
+    std::memcpy(esq.data(), esq_in, sizeof(float) * K);
+  else
+    orc_code_sqnorm(cb, esq.data(), K, d);
+  double tot = 0.0;
+  for (size_t k = 0; k < K; ++k) tot += static_cast<double>(esq[k]);
+  const float dsc = static_cast<float>(tot / static_cast<double>(K));
+  const float e = std::exp(log_inv_T);
+  std::vector<float> eb(K * d);
+  for (size_t i = 0; i < K * d; ++i) eb[i] = bf16_to(cb[i]);
+#pragma omp parallel for schedule(static)
+  for (long tt = 0; tt < static_cast<long>(T); ++tt) {
+    const size_t t = static_cast<size_t>(tt);
+    float best = -std::numeric_limits<float>::infinity(), second = best;
+    int32_t bi = 0;
+    for (size_t k = 0; k < K; ++k) {
+      double acc = 0.0;
+      for (size_t i = 0; i < d; ++i) acc += static_cast<double>(z[t * d + i]) * static_cast<double>(eb[k * d + i]);
+      const float a = static_cast<float>(acc);
+      const float neg = (2.0f * a - esq[k]) / dsc;
+      const float l = neg * e + (bias != nullptr ? bias[k] : 0.0f);
+      if (logits != nullptr) logits[t * K + k] = l;
+      if (l > best) {
+        second = best;
+        best = l;
+        bi = static_cast<int32_t>(k);
+      } else if (l > second) {
+        second = l;
+      }
+    }
+    if (codes != nullptr) codes[t] = bi;
+    if (gap != nullptr) gap[t] = best - second;
+  }
+}
+
 }  // extern "C"

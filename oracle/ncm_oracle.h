@@ -99,6 +99,8 @@ void orc_rvq_level(float* resid, const uint16_t* cb, const float* sqnorm, const 
 void orc_rvq_decode(const int32_t* codes, const uint16_t* cbs, size_t L, float* recon_f32, size_t N, size_t D,
                     size_t K);
 void orc_pool_avg(const float* x, float* y, size_t B, size_t T, size_t D, size_t f);
+void orc_tied_head(const float* z, const uint16_t* cb, const float* esq_in, const float* bias, float log_inv_T,
+                   float* logits, int32_t* codes, float* gap, size_t T, size_t d, size_t K);
 void orc_upsample(const float* q, float* out, size_t B, size_t Tq, size_t T, size_t D, int mode);
 void orc_conv1d_k3(const float* x_op, const float* x_blend, const float* w, const float* b, float* out, size_t rows,
                    size_t width, const size_t* seg_lengths, size_t nseg, float alpha, float beta);

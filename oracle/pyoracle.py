@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
         "orc_rvq_decode": ([i32p, u16p, sz, f32p, sz, sz, sz], None),
         "orc_pool_avg": ([f32p, f32p, sz, sz, sz, sz], None),
         "orc_scale_update": ([i32p, u16p, sz, f32p, f32p, sz, sz, sz, sz, sz], None),
+        "orc_tied_head": ([f32p, u16p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
+                           ctypes.c_void_p, ctypes.c_void_p, sz, sz, sz], None),
         "orc_upsample": ([f32p, f32p, sz, sz, sz, sz, ctypes.c_int], None),
         "orc_conv1d_k3": ([f32p, ctypes.c_void_p, f32p, ctypes.c_void_p, f32p, sz, sz, ctypes.c_void_p, sz,
                            ctypes.c_float, ctypes.c_float], None),
@@ -335,6 +337,21 @@ def scale_update(codes: np.ndarray, cbs_bits: np.ndarray, resid: np.ndarray, rec
 
 def _ptr(a):
     return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def tied_head(z, cb_bits, log_inv_T=0.0, bias=None, esq=None, want_logits=True):
+    """_TiedCodebookHead: returns (logits [T, K] or None, argmax codes [T], top-2 logit gap [T])."""
+    z = _c(z, np.float32)
+    T, d = z.shape
+    cb_bits = _c(cb_bits, np.uint16)
+    K = cb_bits.shape[0]
+    bias = None if bias is None else _c(bias, np.float32)
+    esq = None if esq is None else _c(esq, np.float32)
+    logits = np.empty((T, K), np.float32) if want_logits else None
+    codes = np.empty(T, np.int32)
+    gap = np.empty(T, np.float32)
+    lib().orc_tied_head(z, cb_bits, _ptr(esq), _ptr(bias), log_inv_T, _ptr(logits), _ptr(codes), _ptr(gap), T, d, K)
+    return logits, codes, gap
 
 
 def upsample(q: np.ndarray, T: int, mode: str = "linear") -> np.ndarray:
