@@ -140,6 +140,27 @@ NCM_API int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const ui
                                 const float* sqnorms, int32_t L, int32_t* codes_host, uint16_t* recon_host,
                                 int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
 
+/* ------------------------------------------- (e) row-sharded encode */
+
+/* Token rows shard across GPUs with the codebooks replicated; the only
+ * exchange is an NCCL all-gather of codes and reconstructions over NVLink.
+ * One context per GPU (one process or thread each). ncm_comm_unique_id
+ * fills 128 bytes on one rank, the caller ships them to every rank, and each
+ * rank calls ncm_ctx_comm_init (collective; the context owns the
+ * communicator and frees it in ncm_ctx_destroy). NCCL (libnccl.so.2) is
+ * loaded on first use; NCM_ENOTSUP when it cannot be. */
+NCM_API int ncm_comm_unique_id(uint8_t* id_out /* [128] */);
+NCM_API int ncm_ctx_comm_init(ncm_ctx_t* ctx, const uint8_t* id /* [128] */, int32_t rank, int32_t nranks);
+
+/* Rank r holds rows [r*n_local, (r+1)*n_local) of an N = nranks * n_local row
+ * problem (pad N to a multiple of nranks). Each rank encodes its rows as
+ * ncm_rvq_encode does and all-gathers: on return (stream-ordered) every rank
+ * holds codes_all [L, N] int32 and, when recon_all is non-NULL, recon_all
+ * [N, D] bf16. Collective: every rank calls it with the same L, n_local, D, K. */
+NCM_API int ncm_rvq_encode_sharded(ncm_ctx_t* ctx, const uint16_t* x_local, const uint16_t* codebooks,
+                                   const float* sqnorms, int32_t L, int32_t* codes_all, uint16_t* recon_all,
+                                   int64_t n_local, int64_t D, int64_t K, ncm_stream_t stream);
+
 /* Area pooling by an integer factor (F.interpolate mode="area" with T % factor == 0,
  * vq_forward_semantics.md:67,80): y[b,j,:] = (sum_{i<factor} x[b,j*factor+i,:]) / factor,
  * summed in increasing i in f32. x [B,T,D] f32, y [B,T/factor,D] f32. */

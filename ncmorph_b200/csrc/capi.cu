@@ -226,6 +226,7 @@ int ncm_ctx_destroy(ncm_ctx_t* ctx) {
   if (ctx == nullptr) return NCM_OK;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  comm_release(ctx);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
@@ -507,6 +508,55 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
                          residual_out ? residual_out : reinterpret_cast<float*>(ws + o_res), residual_out != nullptr,
                          reinterpret_cast<uint16_t*>(ws + o_sh), reinterpret_cast<RvqPartial*>(ws + o_part), plan, N,
                          D, K, st);
+}
+
+int ncm_rvq_encode_sharded(ncm_ctx_t* ctx, const uint16_t* x_local, const uint16_t* codebooks, const float* sqnorms,
+                           int32_t L, int32_t* codes_all, uint16_t* recon_all, int64_t n_local, int64_t D, int64_t K,
+                           ncm_stream_t stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (ctx->comm == nullptr) return ncm_fail(NCM_EINVAL, "rvq_encode_sharded: no communicator (ncm_ctx_comm_init)");
+  if ((rc = check_rvq_shape(n_local, D, K))) return rc;
+  if (L <= 0 || L > 64) return ncm_fail(NCM_EINVAL, "rvq_encode_sharded: L=%d must be in [1,64]", L);
+  if (!x_local || !codebooks || !codes_all) return ncm_fail(NCM_EINVAL, "rvq_encode_sharded: null buffer");
+  if (!aligned16(x_local) || !aligned16(codebooks) || !aligned16(codes_all) || (sqnorms && !aligned16(sqnorms)) ||
+      (recon_all && !aligned16(recon_all)))
+    return ncm_fail(NCM_EINVAL, "rvq_encode_sharded: buffers must be 16-byte aligned");
+  const int P = ctx->comm_size, me = ctx->comm_rank;
+  const int64_t N = n_local * P;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, n_local, K);
+  WsCarver cv;
+  const size_t o_sh = cv.take(2 * n_local * D);
+  const size_t o_res = cv.take(sizeof(float) * n_local * D);
+  const size_t o_part = cv.take(plan.partial_bytes);
+  const size_t o_sq = sqnorms ? 0 : cv.take(sizeof(float) * K * L);
+  const size_t o_codes = cv.take(sizeof(int32_t) * L * n_local);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "rvq_encode_sharded: workspace allocation failed");
+  if (sqnorms == nullptr) {
+    float* sq = reinterpret_cast<float*>(ws + o_sq);
+    {
+      Launch _launch(ctx, KID_SQNORM, st);
+      NCM_CUDA_TRY(launch_code_sqnorm(codebooks, sq, K * L, D, st));
+    }
+    sqnorms = sq;
+  }
+  int32_t* codes_local = reinterpret_cast<int32_t*>(ws + o_codes);
+  // this rank's reconstructions land in place, in its slice of recon_all
+  uint16_t* recon_mine = recon_all ? recon_all + static_cast<size_t>(me) * n_local * D : nullptr;
+  rc = rvq_encode_core(ctx, x_local, codebooks, sqnorms, L, codes_local, recon_mine,
+                       reinterpret_cast<float*>(ws + o_res), false, reinterpret_cast<uint16_t*>(ws + o_sh),
+                       reinterpret_cast<RvqPartial*>(ws + o_part), plan, n_local, D, K, st);
+  if (rc) return rc;
+  // codes [L, N]: one all-gather per level (rank r's rows sit at columns r*n..); recon [N, D] in place
+  AllGatherItem items[65];
+  int n = 0;
+  for (int l = 0; l < L; ++l)
+    items[n++] = AllGatherItem{codes_local + static_cast<size_t>(l) * n_local, codes_all + static_cast<size_t>(l) * N,
+                               static_cast<size_t>(n_local), 4};
+  if (recon_all) items[n++] = AllGatherItem{recon_mine, recon_all, static_cast<size_t>(n_local * D), 2};
+  return comm_all_gather(ctx, items, n, st);
 }
 
 int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* codebooks, const float* sqnorms,

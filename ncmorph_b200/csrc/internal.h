@@ -61,6 +61,10 @@ struct ncm_ctx {
   float* rope_sin = nullptr;
   int* rope_row_level = nullptr;
   int64_t rope_rows = 0;
+  // NCCL communicator bound by ncm_ctx_comm_init (row-sharded entry points)
+  void* comm = nullptr;
+  int comm_rank = 0;
+  int comm_size = 1;
 };
 
 namespace ncm {
@@ -200,6 +204,18 @@ int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16
 // bf16(y + bf16(x.w^T + bias)).
 int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y,
                    float* y_f32, int64_t M, int64_t K, int64_t N, cudaStream_t stream, int mode, int64_t F);
+
+// ---- NCCL (comm.cu, loaded on first use)
+// One all-gather of `count` elements of `bytes_per_elem` bytes from every
+// rank: recv[r * count ..] = rank r's send. Items run as one NCCL group.
+struct AllGatherItem {
+  const void* send;
+  void* recv;
+  size_t count;
+  int bytes_per_elem;
+};
+int comm_all_gather(ncm_ctx* ctx, const AllGatherItem* items, int n, cudaStream_t stream);
+void comm_release(ncm_ctx* ctx);
 
 // ---- codebook-tied head (head.cu, gemm.cu)
 // logits [T, K] f32 = (2 z.E^T - esq) / scal[0] * scal[1] + bias, z [T, d] and

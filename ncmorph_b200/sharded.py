@@ -88,3 +88,50 @@ def sharded_encode(x_local: torch.Tensor, codebooks: torch.Tensor, total_rows: i
     enc = ShardedEncoder(codebooks, total_rows, x_local.dtype, sqnorms, group, encode)
     codes, recon = enc(x_local)
     return codes.contiguous(), recon
+
+
+# ---------------------------------------------------------------- C ABI form
+# The same sharding through the library's own NCCL communicator
+# (ncm_ctx_comm_init / ncm_rvq_encode_sharded), for hosts without a
+# torch.distributed process group: the caller ships the 128-byte id.
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (call on one rank, send to all)."""
+    import ctypes
+
+    from . import _lib
+    buf = (ctypes.c_uint8 * 128)()
+    _lib.call("ncm_comm_unique_id", buf)
+    return bytes(buf)
+
+
+def comm_init(device, uid: bytes, rank: int, nranks: int) -> None:
+    """Binds a communicator of `nranks` ranks to this device's context (collective)."""
+    import ctypes
+
+    from . import _lib
+    from .device import context
+    if len(uid) != 128:
+        raise ValueError("the NCCL unique id has 128 bytes")
+    buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+    _lib.call("ncm_ctx_comm_init", context(device), buf, rank, nranks)
+
+
+def rvq_encode_sharded(x_local: torch.Tensor, codebooks: torch.Tensor, nranks: int,
+                       sqnorms: torch.Tensor | None = None, want_recon: bool = True):
+    """This rank's rows x_local [n, D] bf16 -> (codes [L, nranks*n] int32,
+    recon [nranks*n, D] bf16 or None) gathered from every rank."""
+    from . import _lib
+    from .device import context, need, ptr, stream_of
+    n, D = x_local.shape
+    L, K, D2 = codebooks.shape
+    if D2 != D:
+        raise ValueError("codebook width differs from x")
+    need(x_local, torch.bfloat16, "x_local")
+    need(codebooks, torch.bfloat16, "codebooks")
+    dev = x_local.device
+    codes = torch.empty((L, nranks * n), dtype=torch.int32, device=dev)
+    recon = torch.empty((nranks * n, D), dtype=torch.bfloat16, device=dev) if want_recon else None
+    _lib.call("ncm_rvq_encode_sharded", context(dev), ptr(x_local), ptr(codebooks), ptr(sqnorms), L, ptr(codes),
+              ptr(recon), n, D, K, stream_of(x_local))
+    return codes, recon

@@ -71,3 +71,20 @@ def test_ctx_create_without_gpu_fails_cleanly():
     assert rc in (_lib.NCM_ECUDA, _lib.NCM_EINVAL)
     assert ctx.value is None
     assert lib.ncm_last_error()
+
+
+def test_comm_unique_id_without_gpu():
+    """NCCL is loaded on demand; a unique id needs no GPU."""
+    from ncmorph_b200 import _lib, sharded
+    try:
+        uid = sharded.comm_unique_id()
+    except _lib.NcmError as e:
+        assert e.status == _lib.NCM_ENOTSUP  # no libnccl on this host
+        return
+    assert len(uid) == 128 and any(uid)
+
+
+def test_sharded_encode_without_communicator_is_rejected():
+    from ncmorph_b200 import _lib
+    lib = _lib.load()
+    assert lib.ncm_rvq_encode_sharded(None, None, None, None, 1, None, None, 1, 8, 1, None) == _lib.NCM_EINVAL
