@@ -249,6 +249,21 @@ NCM_API int ncm_multiscale_decode(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                                   const uint16_t* codebooks, const uint16_t* phi_weight, const float* phi_bias,
                                   uint16_t* recon, ncm_stream_t stream);
 
+/* ------------------------------------------------- checkpoint loading */
+
+/* safetensors element types the loader reads (packages/safetensors/root.zig:34-54) */
+enum { NCM_DTYPE_BF16 = 0, NCM_DTYPE_F16 = 1, NCM_DTYPE_F32 = 2 };
+
+/* One tensor of a safetensors file to device memory as bf16 (src/loader.zig:
+ * 286-345 read_tensor/decode_chunk, without widening to f32): nbytes at
+ * absolute file offset `offset` (= 8 + header_len + data_offsets[0], from the
+ * caller's parse_header) stream through pinned staging buffers to dst
+ * (nbytes / element size bf16 values). BF16 is copied bit for bit; F16 and F32
+ * round to bf16 on the device (nearest even, NaN -> 0x7FC0). Returns when the
+ * data is on the device. */
+NCM_API int ncm_load_tensor_bf16(ncm_ctx_t* ctx, const char* path, uint64_t offset, uint64_t nbytes, int32_t dtype,
+                                 uint16_t* dst, ncm_stream_t stream);
+
 /* ------------------------------------------- codebook-tied output head */
 
 /* _TiedCodebookHead (PROJECT.md:222, decision D18): per predicted level,

@@ -141,12 +141,13 @@ int ncm_tied_head_argmax(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* code
   if (!make_tmap_bf16_2d(&tmA, z, T, d, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, d, 256))
     return ncm_fail(NCM_EINVAL, "tied head: tensor map encoding failed (T=%lld d=%lld K=%lld)", (long long)T,
                     (long long)d, (long long)K);
+  int* counters = plan.splits > 1 ? rvq_counters(ctx, plan.row_blocks) : nullptr;
   {
     Launch _launch(ctx, KID_RVQ_ARGMIN, st);
     NCM_CUDA_TRY(launch_rvq_argmin(plan, tmA, tmB, c, codes, part, ctx->d_err, T, d, K, st, nullptr, nullptr,
-                                   scal + 2));
+                                   scal + 2, counters));
   }
-  if (plan.splits > 1) {
+  if (plan.splits > 1 && counters == nullptr) {
     Launch _launch(ctx, KID_RVQ_APPLY, st);
     NCM_CUDA_TRY(launch_rvq_apply(plan, part, codes, nullptr, nullptr, nullptr, codebook, ctx->d_err, T, d, K, false,
                                   st));

@@ -61,6 +61,13 @@ struct ncm_ctx {
   float* rope_sin = nullptr;
   int* rope_row_level = nullptr;
   int64_t rope_rows = 0;
+  // split-fixup arrival counters of the RVQ argmin kernel (kept zero between launches)
+  int* rvq_counters = nullptr;
+  int64_t rvq_counter_len = 0;
+  // pinned staging buffers and their events of the checkpoint loader (first use)
+  void* load_h[2] = {nullptr, nullptr};
+  cudaEvent_t load_ev[2] = {nullptr, nullptr};
+  size_t load_bytes = 0;
   // NCCL communicator bound by ncm_ctx_comm_init (row-sharded entry points)
   void* comm = nullptr;
   int comm_rank = 0;
@@ -162,12 +169,19 @@ struct RvqTop2 {
 
 // argmin_k (sqnorm[k] - 2 a_n . e_k) over bf16 rows `a` [N,D] (via tmA) and
 // (with mul_dev: argmin_k fmaf(*mul_dev, a_n . e_k, sqnorm[k]), the tied head's form)
+// With counters (and no top2) a split plan merges its splits inside the
+// kernel (the last CTA to finish a row block), writes the final codes and
+// applies `fu`; rvq_apply_kernel is then not needed.
 // codebook `e` [K,D] (via tmB). Writes codes (splits == 1) or partials, and
 // applies `fu` when given and the plan has one split.
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu = nullptr,
-                              const RvqTop2* top2 = nullptr, const float* mul_dev = nullptr);
+                              const RvqTop2* top2 = nullptr, const float* mul_dev = nullptr,
+                              int* counters = nullptr);
+// Per row block arrival counters of the split fixup (zeroed, kept in the
+// context, grown on demand); nullptr if the allocation fails.
+int* rvq_counters(ncm_ctx* ctx, int64_t row_blocks);
 
 // Final code per row (reducing partials when splits > 1), then
 // resid = (src_bf16 ? f32(src_bf16) : resid) - e[code]; shadow = bf16(resid).

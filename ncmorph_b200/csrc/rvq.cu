@@ -50,7 +50,11 @@ struct __align__(1024) ArgminSmem {
   uint64_t drain;
   uint64_t upd_full[2];   // epilogue -> update warps: a row block's codes are in codes_s
   uint64_t upd_empty[2];  // update warps -> epilogue: codes_s slot free again
+  uint64_t fix_arrive;    // split fixup: the 4 argmin warps published their partials
+  uint64_t fix_done;      // split fixup: the arrival was counted, fix_last is set
   int codes_s[2][BM];
+  int upd_rb[2];   // row block of each handoff; -1 ends the update warps' loop
+  int fix_last;    // split fixup: this CTA finished the row block's last split
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -72,6 +76,10 @@ struct ArgminArgs {
   const uint16_t* codebook;
   // dist = fmaf(mul, acc, csq[k]); mul = -2 (RVQ) or *mul_dev when given (tied head)
   const float* mul_dev;
+  // split fixup (splits > 1): per row block arrival counters (zero before the
+  // launch, zero again after it); the CTA that completes a row block's last
+  // split merges the partials, writes the codes and runs the fused update
+  int* counters;
   // top-2 gap (the GAP instantiation only)
   float* gap;        // [N] relative gap, splits == 1
   const float* a2;   // [N] ||bf16(r)||^2
@@ -114,6 +122,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&S.upd_empty[b], 4);
     }
     mbar_init(&S.drain, 1);
+    mbar_init(&S.fix_arrive, 4);
+    mbar_init(&S.fix_done, 1);
     S.abort_flag = 0;
     fence_mbar_init();
   }
@@ -227,7 +237,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* csq_s = S.csq[warp - 2];
     const float mul = args.mul_dev != nullptr ? __ldg(args.mul_dev) : -2.f;
     uint32_t acc_it = 0;
-    uint32_t uit = 0;  // units handed to the update warps
+    uint32_t uit = 0;     // units handed to the update warps
+    uint32_t fix_ph = 0;  // phase of the split-fixup handshake barriers
     bool ok = true;
     for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
       const int rb = unit / args.splits;
@@ -307,6 +318,56 @@ __global__ void __launch_bounds__(THREADS, 1)
           if constexpr (GAP) args.part_d2[static_cast<size_t>(sp) * args.N + row] = s2;
         }
       }
+      if (args.splits > 1) {
+        if (args.counters == nullptr) continue;  // rvq_apply_kernel merges the splits
+        // Split fixup: publish this split's partials, count the arrival; the
+        // CTA completing the row block merges all splits (lowest distance,
+        // then lowest index) and carries on as if it had owned every code.
+        // (bounded mbarrier handshakes among the 4 argmin warps, so an abort cannot strand a warp)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.fix_arrive);
+        if (warp == 2) {
+          int fine = 1;
+          if (lane == 0) {
+            fine = mbar_wait(&S.fix_arrive, fix_ph, abort_flag) ? 1 : 0;
+            if (fine) {
+              const int prev = atomicAdd(args.counters + rb, 1);
+              const int last = prev == args.splits - 1;
+              if (last) atomicExch(args.counters + rb, 0);  // ready for the next launch
+              *reinterpret_cast<volatile int*>(&S.fix_last) = last;
+              mbar_arrive(&S.fix_done);
+            }
+          }
+          if (!__shfl_sync(0xffffffffu, fine, 0)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!mbar_wait(&S.fix_done, fix_ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        fix_ph ^= 1u;
+        if (!*reinterpret_cast<volatile int*>(&S.fix_last)) continue;
+        __threadfence();
+        if (row < args.N) {
+          float bd = INFINITY;
+          int bi = INT_MAX;
+          for (int s2i = 0; s2i < args.splits; ++s2i) {
+            // L2 reads: the other splits were written by other SMs
+            const int2 pv = __ldcg(reinterpret_cast<const int2*>(args.part + static_cast<size_t>(s2i) * args.N + row));
+            const float d = __int_as_float(pv.x);
+            if (d < bd || (d == bd && pv.y < bi)) {
+              bd = d;
+              bi = pv.y;
+            }
+          }
+          if (bi == INT_MAX) bi = __ldcg(reinterpret_cast<const int2*>(args.part + row)).y;  // all NaN/inf
+          bidx = bi;
+          args.codes[row] = bidx;
+        }
+      }
       if (args.fuse) {
         const uint32_t ub = uit & 1u, up = (uit >> 1) & 1u;
         if (!mbar_wait(&S.upd_empty[ub], up ^ 1u, abort_flag)) {
@@ -314,9 +375,21 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         S.codes_s[ub][q * 32 + lane] = row < args.N ? bidx : -1;
+        if (lane == 0) S.upd_rb[ub] = rb;
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.upd_full[ub]);
         ++uit;
+      }
+    }
+    if (ok && args.fuse) {
+      // end of work: tell the update warps
+      const uint32_t ub = uit & 1u, up = (uit >> 1) & 1u;
+      if (mbar_wait(&S.upd_empty[ub], up ^ 1u, abort_flag)) {
+        if (lane == 0) S.upd_rb[ub] = -1;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.upd_full[ub]);
+      } else {
+        ok = false;
       }
     }
     if (!ok) raise_abort(abort_flag, args.err);
@@ -327,13 +400,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int uw = warp - 6;
     uint32_t uit = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < args.n_units; unit += gridDim.x) {
+    for (;;) {
       const uint32_t ub = uit & 1u, up = (uit >> 1) & 1u;
       if (!mbar_wait(&S.upd_full[ub], up, abort_flag)) {
         ok = false;
         break;
       }
-      const int rb = unit;  // splits == 1: one unit per row block
+      const int rb = *reinterpret_cast<volatile int*>(&S.upd_rb[ub]);
+      if (rb < 0) break;  // the epilogue has no more row blocks
       for (int r = 0; r < 32; ++r) {
         const int code = S.codes_s[ub][uw * 32 + r];
         if (code < 0) continue;
@@ -343,24 +417,40 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         const size_t ro = static_cast<size_t>(rb * BM + uw * 32 + r) * args.D;
         const uint16_t* e = args.codebook + static_cast<size_t>(code) * args.D;
-#pragma unroll 4
-        for (int d = lane * 4; d < args.D; d += 128) {
-          float4 x;
-          if (args.src_bf16 != nullptr) {
-            const uint2 sv = *reinterpret_cast<const uint2*>(args.src_bf16 + ro + d);
-            x = make_float4(bf16lo(sv.x), bf16hi(sv.x), bf16lo(sv.y), bf16hi(sv.y));
-          } else {
-            x = *reinterpret_cast<const float4*>(args.resid + ro + d);
+        // 1024 columns per batch: every load of the batch is issued before the
+        // first store (the stores may alias later loads as far as the compiler
+        // knows, so an interleaved loop keeps one load in flight per lane)
+        for (int d0 = 0; d0 < args.D; d0 += 1024) {
+          float4 x[8];
+          uint2 ev[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int d = d0 + lane * 4 + j * 128;
+            if (d < args.D) {
+              if (args.src_bf16 != nullptr) {
+                const uint2 sv = *reinterpret_cast<const uint2*>(args.src_bf16 + ro + d);
+                x[j] = make_float4(bf16lo(sv.x), bf16hi(sv.x), bf16lo(sv.y), bf16hi(sv.y));
+              } else {
+                x[j] = *reinterpret_cast<const float4*>(args.resid + ro + d);
+              }
+              ev[j] = __ldg(reinterpret_cast<const uint2*>(e + d));
+            }
           }
-          const uint2 ev = __ldg(reinterpret_cast<const uint2*>(e + d));
-          x.x -= bf16lo(ev.x);
-          x.y -= bf16hi(ev.x);
-          x.z -= bf16lo(ev.y);
-          x.w -= bf16hi(ev.y);
-          *reinterpret_cast<float4*>(args.resid + ro + d) = x;
-          if (args.shadow != nullptr)
-            *reinterpret_cast<uint2*>(args.shadow + ro + d) =
-                make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int d = d0 + lane * 4 + j * 128;
+            if (d < args.D) {
+              float4 v = x[j];
+              v.x -= bf16lo(ev[j].x);
+              v.y -= bf16hi(ev[j].x);
+              v.z -= bf16lo(ev[j].y);
+              v.w -= bf16hi(ev[j].y);
+              *reinterpret_cast<float4*>(args.resid + ro + d) = v;
+              if (args.shadow != nullptr)
+                *reinterpret_cast<uint2*>(args.shadow + ro + d) =
+                    make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+            }
+          }
         }
       }
       __syncwarp();
@@ -720,7 +810,7 @@ RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
 cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const CUtensorMap& tmB,
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu,
-                              const RvqTop2* top2, const float* mul_dev) {
+                              const RvqTop2* top2, const float* mul_dev, int* counters) {
   // the shared-memory opt-in is per device and per instantiation: remember which devices have it
   static unsigned long long attr_set[2] = {0, 0};
   const int gi = top2 != nullptr ? 1 : 0;
@@ -747,7 +837,9 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.tiles_per_split = plan.tiles_per_split;
   a.code_tiles = plan.code_tiles;
   a.n_units = plan.n_units;
-  a.fuse = (fu != nullptr && plan.splits == 1) ? 1 : 0;
+  // the split fixup needs counters and does not carry the top-2 gap
+  a.counters = (plan.splits > 1 && top2 == nullptr) ? counters : nullptr;
+  a.fuse = (fu != nullptr && (plan.splits == 1 || a.counters != nullptr)) ? 1 : 0;
   a.resid = fu ? fu->resid : nullptr;
   a.src_bf16 = fu ? fu->src_bf16 : nullptr;
   a.shadow = fu ? fu->shadow : nullptr;
