@@ -9,11 +9,11 @@
 // MMA and the argmin epilogue, and two 256-column TMEM accumulators let the
 // epilogue of code tile t run while the MMA of tile t+1 proceeds.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over work units):
+// Warp roles (448 threads, one CTA per SM, persistent over work units):
 //   warp 0     TMA producer (one elected lane)
 //   warp 1     TMEM allocator + MMA issuer (one elected lane)
 //   warps 2-5  argmin epilogue, one thread per accumulator row (TMEM lane)
-//   warps 6-9  residual update: when a row block's codes are final they
+//   warps 6-13 residual update: when a row block's codes are final they
 //              apply r -= e[code] (f32) and write bf16(r) for the next level,
 //              while the tensor cores already work on the next row block
 //
@@ -34,7 +34,9 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int STAGES = 4;
-constexpr int THREADS = 320;
+constexpr int UPD_WARPS = 8;  // residual-update warps (rows split evenly among them)
+constexpr int UPD_ROWS = BM / UPD_WARPS;
+constexpr int THREADS = 64 + 128 + 32 * UPD_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&S.tfull[b], 1);
       mbar_init(&S.tempty[b], 4);
       mbar_init(&S.upd_full[b], 4);
-      mbar_init(&S.upd_empty[b], 4);
+      mbar_init(&S.upd_empty[b], UPD_WARPS);
     }
     mbar_init(&S.drain, 1);
     mbar_init(&S.fix_arrive, 4);
@@ -395,7 +397,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!ok) raise_abort(abort_flag, args.err);
   } else if (args.fuse) {
     // ------------------------------------------------- residual update
-    // Warp uw updates rows uw*32.. of each finished row block: one row at a
+    // Warp uw updates rows uw*16.. of each finished row block: one row at a
     // time, lanes striding the row in 16-byte (f32) / 8-byte (bf16) pieces.
     const int uw = warp - 6;
     uint32_t uit = 0;
@@ -408,14 +410,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int rb = *reinterpret_cast<volatile int*>(&S.upd_rb[ub]);
       if (rb < 0) break;  // the epilogue has no more row blocks
-      for (int r = 0; r < 32; ++r) {
-        const int code = S.codes_s[ub][uw * 32 + r];
+      for (int r = 0; r < UPD_ROWS; ++r) {
+        const int code = S.codes_s[ub][uw * UPD_ROWS + r];
         if (code < 0) continue;
         if (code >= args.K) {
           if (lane == 0) atomicOr(args.err, kErrBadIndex);
           continue;
         }
-        const size_t ro = static_cast<size_t>(rb * BM + uw * 32 + r) * args.D;
+        const size_t ro = static_cast<size_t>(rb * BM + uw * UPD_ROWS + r) * args.D;
         const uint16_t* e = args.codebook + static_cast<size_t>(code) * args.D;
         // 1024 columns per batch: every load of the batch is issued before the
         // first store (the stores may alias later loads as far as the compiler
