@@ -328,6 +328,17 @@ NCM_API int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride
                                const float* sin_t, uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads,
                                const ncm_mask_t* mask, ncm_stream_t stream);
 
+/* Fused QKV projection of one decoder layer (src/decoder.zig:171-190 and
+ * rotate_head, packages/kernels/root.zig:615-633): qkv [T, (heads + 2 kv_heads) * 64]
+ * = bf16(x . w^T + bias) with RoPE (bf16 mode, tables cos_t/sin_t [T, 64] f32
+ * device) applied to the Q and K heads in the GEMM epilogue, and vt
+ * [kv_heads * 64, T] receiving the V heads transposed (the attention's P.V
+ * operand). Bit-identical to ncm_linear_bf16 followed by the RoPE that
+ * ncm_attention_bf16 applies. head_dim 64; T > 64. */
+NCM_API int ncm_qkv_projection_rope(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                                    const float* cos_t, const float* sin_t, uint16_t* qkv, uint16_t* vt, int64_t T,
+                                    int64_t hidden, int32_t heads, int32_t kv_heads, ncm_stream_t stream);
+
 /* NCM body forward (src/ncm_model.zig:89-250) with the bf16 layer of
  * src/decoder.zig:168-216: input projection (+bias), level embeddings,
  * per-level restarting RoPE positions, the configured mask, num_layers x

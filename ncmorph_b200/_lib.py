@@ -132,6 +132,7 @@ SIGNATURES: dict[str, list] = {
     "ncm_ctx_comm_init": [c_vp, c_vp, c_i32, c_i32],
     "ncm_rvq_encode_sharded": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_load_tensor_bf16": [c_vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64, c_i32, c_vp, c_vp],
+    "ncm_qkv_projection_rope": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_i32, c_vp],
     "ncm_upsample": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_conv1d_k3": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, ctypes.c_float, ctypes.c_float,
                       c_vp],

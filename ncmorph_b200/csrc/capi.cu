@@ -263,6 +263,8 @@ int ncm_ctx_destroy(ncm_ctx_t* ctx) {
   if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
   if (ctx->rope_cos) cudaFree(ctx->rope_cos);
   if (ctx->rope_sin) cudaFree(ctx->rope_sin);
+  if (ctx->rope_cos_bf) cudaFree(ctx->rope_cos_bf);
+  if (ctx->rope_sin_bf) cudaFree(ctx->rope_sin_bf);
   if (ctx->rope_row_level) cudaFree(ctx->rope_row_level);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
   if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);

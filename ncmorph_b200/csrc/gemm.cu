@@ -68,6 +68,13 @@ struct LinearArgs {
   const float* head_esq;
   const float* head_bias;
   const float* head_scal;
+  // mode 5 (fused QKV projection): RoPE on the Q and K columns (n < voff) with
+  // per-token tables cos/sin [M, 64]; V columns also written transposed to
+  // vt [(n - voff), M]
+  const uint16_t* rope_cos;  // bf16(cos), bf16(sin) tables [M, 64]
+  const uint16_t* rope_sin;
+  uint16_t* vt;
+  int voff;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& ta, int& tb) {
@@ -255,6 +262,86 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint16_t* dst = args.y + static_cast<size_t>(m) * args.F + n0 + c;
             *reinterpret_cast<uint4*>(dst) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
             *reinterpret_cast<uint4*>(dst + 8) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          }
+        }
+      } else if (!SWAP && args.mode == 5) {
+        // QKV epilogue: y = bf16(acc + bias); per 64-column head, rotate_head in
+        // bf16 mode (packages/kernels/root.zig:615-633) on the pair (d, d + 32)
+        // for Q and K heads, and V heads also stored transposed for the
+        // attention's P.V operand. This warp takes the pairs whose first
+        // column is at c0 + 64 j (c0 = 0 or 16): both halves are its own, and
+        // every head of the tile uses the same 16 pair indices c0...
+        const int m = arow;
+        const uint4* crow = reinterpret_cast<const uint4*>(args.rope_cos + static_cast<size_t>(m) * 64 + c0);
+        const uint4* srow = reinterpret_cast<const uint4*>(args.rope_sin + static_cast<size_t>(m) * 64 + c0);
+#pragma unroll 1
+        for (int c = c0; c < BN; c += 64) {
+          uint32_t va[16], vb[16];
+          tmem_ld_x16(tbase + c, va);
+          tmem_ld_x16(tbase + c + 32, vb);
+          tmem_wait_ld();
+          if (m >= args.M) continue;
+          const int n0 = tb * BN + c;  // columns n0.. and n0 + 32..
+          const int seg = n0 & ~63;
+          uint32_t pa[8], pb[8];  // bf16(acc + bias), packed pairs
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            float a0 = __uint_as_float(va[j]), a1 = __uint_as_float(va[j + 1]);
+            float b0 = __uint_as_float(vb[j]), b1 = __uint_as_float(vb[j + 1]);
+            if (args.bias != nullptr) {
+              a0 += bf16_to_f32(__ldg(args.bias + n0 + j));
+              a1 += bf16_to_f32(__ldg(args.bias + n0 + j + 1));
+              b0 += bf16_to_f32(__ldg(args.bias + n0 + 32 + j));
+              b1 += bf16_to_f32(__ldg(args.bias + n0 + 33 + j));
+            }
+            pa[j / 2] = cvt_bf16x2(a0, a1);
+            pb[j / 2] = cvt_bf16x2(b0, b1);
+          }
+          uint16_t* ya = args.y + static_cast<size_t>(m) * args.N + n0;
+          if (seg < args.voff) {
+            // this token's bf16 cos/sin at indices c0.. and c0 + 32.. (16-byte loads, L1-resident)
+            uint32_t tc[16], ts[16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const uint4 cv = __ldg(crow + (q4 & 1) + (q4 >> 1) * 4);
+              const uint4 sv = __ldg(srow + (q4 & 1) + (q4 >> 1) * 4);
+              tc[4 * q4 + 0] = cv.x, tc[4 * q4 + 1] = cv.y, tc[4 * q4 + 2] = cv.z, tc[4 * q4 + 3] = cv.w;
+              ts[4 * q4 + 0] = sv.x, ts[4 * q4 + 1] = sv.y, ts[4 * q4 + 2] = sv.z, ts[4 * q4 + 3] = sv.w;
+            }
+            uint32_t oa[8], ob[8];
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+              // pair p holds indices i = c0 + 2p, c0 + 2p + 1; each product and
+              // the sums rounded to bf16 as rotate_head does
+              const float f0 = bf16lo(pa[p]), f1 = bf16hi(pa[p]);  // first
+              const float s0 = bf16lo(pb[p]), s1 = bf16hi(pb[p]);  // second
+              const float cf0 = bf16lo(tc[p]), cf1 = bf16hi(tc[p]), cs0 = bf16lo(tc[8 + p]), cs1 = bf16hi(tc[8 + p]);
+              const float sf0 = bf16lo(ts[p]), sf1 = bf16hi(ts[p]), ss0 = bf16lo(ts[8 + p]), ss1 = bf16hi(ts[8 + p]);
+              const uint32_t left = cvt_bf16x2(f0 * cf0, f1 * cf1);
+              const uint32_t right = cvt_bf16x2(-s0 * sf0, -s1 * sf1);
+              const uint32_t right2 = cvt_bf16x2(f0 * ss0, f1 * ss1);
+              const uint32_t left2 = cvt_bf16x2(s0 * cs0, s1 * cs1);
+              oa[p] = cvt_bf16x2(bf16lo(left) + bf16lo(right), bf16hi(left) + bf16hi(right));
+              ob[p] = cvt_bf16x2(bf16lo(left2) + bf16lo(right2), bf16hi(left2) + bf16hi(right2));
+            }
+            *reinterpret_cast<uint4*>(ya) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+            *reinterpret_cast<uint4*>(ya + 8) = make_uint4(oa[4], oa[5], oa[6], oa[7]);
+            *reinterpret_cast<uint4*>(ya + 32) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+            *reinterpret_cast<uint4*>(ya + 40) = make_uint4(ob[4], ob[5], ob[6], ob[7]);
+          } else {
+            *reinterpret_cast<uint4*>(ya) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+            *reinterpret_cast<uint4*>(ya + 8) = make_uint4(pa[4], pa[5], pa[6], pa[7]);
+            *reinterpret_cast<uint4*>(ya + 32) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+            *reinterpret_cast<uint4*>(ya + 40) = make_uint4(pb[4], pb[5], pb[6], pb[7]);
+            // transposed copy: lanes hold consecutive tokens, so each column's store is contiguous
+            uint16_t* vta = args.vt + static_cast<size_t>(n0 - args.voff) * args.M + m;
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              vta[static_cast<size_t>(j) * args.M] = static_cast<uint16_t>(pa[j / 2] & 0xFFFFu);
+              vta[static_cast<size_t>(j + 1) * args.M] = static_cast<uint16_t>(pa[j / 2] >> 16);
+              vta[static_cast<size_t>(j + 32) * args.M] = static_cast<uint16_t>(pb[j / 2] & 0xFFFFu);
+              vta[static_cast<size_t>(j + 33) * args.M] = static_cast<uint16_t>(pb[j / 2] >> 16);
+            }
           }
         }
       } else if (!SWAP && args.mode == 4) {
@@ -588,6 +675,45 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
       case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
       default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
     }
+  }
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  return NCM_OK;
+}
+
+int linear_qkv_rope(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* qkv,
+                    uint16_t* vt, const uint16_t* cos_bf, const uint16_t* sin_bf, int64_t M, int64_t K, int64_t N,
+                    int64_t voff, cudaStream_t stream) {
+  if (M <= 64 || N % 64 != 0 || voff % 64 != 0 || voff > N)
+    return ncm_fail(NCM_EINVAL, "qkv projection: fused RoPE needs M > 64 and head-aligned widths");
+  LinearArgs a{};
+  a.mode = 5;
+  a.taps = 1;
+  a.bias = bias;
+  a.y = qkv;
+  a.err = ctx->d_err;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.rope_cos = cos_bf;
+  a.rope_sin = sin_bf;
+  a.vt = vt;
+  a.voff = static_cast<int>(voff);
+  const long long mt = ceil_div(M, BM);
+  const int bn = (mt * ceil_div(N, 256) >= ctx->num_sms) ? 256 : (mt * ceil_div(N, 128) >= ctx->num_sms ? 128 : 64);
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, bn))
+    return ncm_fail(NCM_EINVAL, "qkv projection: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
+                    (long long)K, (long long)N);
+  a.tiles_a = static_cast<int>(mt);
+  a.tiles_b = ceil_div(N, bn);
+  a.a_fast = double(M) <= double(N) ? 1 : 0;
+  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
+  cudaError_t e;
+  Launch _launch(ctx, KID_LINEAR, stream);
+  switch (bn) {
+    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
+    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
+    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
   }
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
   return NCM_OK;

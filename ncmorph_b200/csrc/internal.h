@@ -59,6 +59,8 @@ struct ncm_ctx {
   uint64_t rope_key = 0;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
+  uint16_t* rope_cos_bf = nullptr;  // the same tables rounded to bf16 (fused QKV epilogue)
+  uint16_t* rope_sin_bf = nullptr;
   int* rope_row_level = nullptr;
   int64_t rope_rows = 0;
   // split-fixup arrival counters of the RVQ argmin kernel (kept zero between launches)
@@ -230,6 +232,15 @@ struct AllGatherItem {
 };
 int comm_all_gather(ncm_ctx* ctx, const AllGatherItem* items, int n, cudaStream_t stream);
 void comm_release(ncm_ctx* ctx);
+
+// Fused QKV projection for M > 64: qkv [M, N] = bf16(x . w^T + bias) with
+// rotate_head (bf16 mode) applied to every 64-column head below voff using
+// the per-token bf16-rounded tables cos_bf/sin_bf [M, 64] (16-byte aligned),
+// and the V columns (n >= voff) also written transposed to vt [(N - voff), M].
+// N and voff multiples of 64.
+int linear_qkv_rope(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* qkv,
+                    uint16_t* vt, const uint16_t* cos_bf, const uint16_t* sin_bf, int64_t M, int64_t K, int64_t N,
+                    int64_t voff, cudaStream_t stream);
 
 // ---- codebook-tied head (head.cu, gemm.cu)
 // logits [T, K] f32 = (2 z.E^T - esq) / scal[0] * scal[1] + bias, z [T, d] and

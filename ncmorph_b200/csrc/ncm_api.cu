@@ -112,6 +112,35 @@ int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const 
                         mask->prefix_length, mask->prefix_pad_mask, mask->level_lengths, mask->num_levels, st);
 }
 
+int ncm_qkv_projection_rope(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                            const float* cos_t, const float* sin_t, uint16_t* qkv, uint16_t* vt, int64_t T,
+                            int64_t hidden, int32_t heads, int32_t kv_heads, ncm_stream_t stream) {
+  int rc = ctx_ok(ctx);
+  if (rc) return rc;
+  if (T <= 64 || T > INT32_MAX || hidden <= 0 || hidden % 8 != 0 || heads <= 0 || kv_heads <= 0)
+    return ncm_fail(NCM_EINVAL, "qkv_projection_rope: bad shape (T=%lld must exceed 64, hidden %lld)", (long long)T,
+                    (long long)hidden);
+  if (!x || !w || !cos_t || !sin_t || !qkv || !vt) return ncm_fail(NCM_EINVAL, "qkv_projection_rope: null buffer");
+  if (!a16(x) || !a16(w) || !a16(qkv) || (bias && !a16(bias)))
+    return ncm_fail(NCM_EINVAL, "qkv_projection_rope: buffers must be 16-byte aligned");
+  if (!a16(cos_t) || !a16(sin_t)) return ncm_fail(NCM_EINVAL, "qkv_projection_rope: tables must be 16-byte aligned");
+  const int64_t N = static_cast<int64_t>(heads + 2 * kv_heads) * 64;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  WsCarver cv;
+  const size_t o_c = cv.take(2 * T * 64), o_s = cv.take(2 * T * 64);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "qkv_projection_rope: workspace allocation failed");
+  uint16_t* cb = reinterpret_cast<uint16_t*>(ws + o_c);
+  uint16_t* sb = reinterpret_cast<uint16_t*>(ws + o_s);
+  {
+    Launch _l(ctx, KID_CAST, st);
+    NCM_CUDA_TRY(launch_f32_to_bf16(cos_t, cb, T * 64, st));
+    NCM_CUDA_TRY(launch_f32_to_bf16(sin_t, sb, T * 64, st));
+  }
+  return linear_qkv_rope(ctx, x, w, bias, qkv, vt, cb, sb, T, hidden, N, static_cast<int64_t>(heads + kv_heads) * 64,
+                         st);
+}
+
 int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_decoder_weights_t* W,
                     const uint16_t* inputs, uint16_t* out, ncm_stream_t stream) {
   int rc = ctx_ok(ctx);
@@ -190,17 +219,29 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
     if (T > ctx->rope_rows) {
       cudaFree(ctx->rope_cos);
       cudaFree(ctx->rope_sin);
+      cudaFree(ctx->rope_cos_bf);
+      cudaFree(ctx->rope_sin_bf);
       cudaFree(ctx->rope_row_level);
       ctx->rope_cos = ctx->rope_sin = nullptr;
+      ctx->rope_cos_bf = ctx->rope_sin_bf = nullptr;
       ctx->rope_row_level = nullptr;
       ctx->rope_rows = 0;
       NCM_CUDA_TRY(cudaMalloc(&ctx->rope_cos, 4 * T * 64));
       NCM_CUDA_TRY(cudaMalloc(&ctx->rope_sin, 4 * T * 64));
+      NCM_CUDA_TRY(cudaMalloc(&ctx->rope_cos_bf, 2 * T * 64));
+      NCM_CUDA_TRY(cudaMalloc(&ctx->rope_sin_bf, 2 * T * 64));
       NCM_CUDA_TRY(cudaMalloc(&ctx->rope_row_level, 4 * T));
       ctx->rope_rows = T;
     }
     NCM_CUDA_TRY(cudaMemcpy(ctx->rope_cos, ch.data(), 4 * T * 64, cudaMemcpyHostToDevice));
     NCM_CUDA_TRY(cudaMemcpy(ctx->rope_sin, sh.data(), 4 * T * 64, cudaMemcpyHostToDevice));
+    {
+      // bf16-rounded copies for the fused QKV epilogue (rotate_head rounds each table value)
+      std::vector<uint16_t> cb(T * 64), sb(T * 64);
+      for (int64_t i = 0; i < T * 64; ++i) cb[i] = f32_to_bf16(ch[i]), sb[i] = f32_to_bf16(sh[i]);
+      NCM_CUDA_TRY(cudaMemcpy(ctx->rope_cos_bf, cb.data(), 2 * T * 64, cudaMemcpyHostToDevice));
+      NCM_CUDA_TRY(cudaMemcpy(ctx->rope_sin_bf, sb.data(), 2 * T * 64, cudaMemcpyHostToDevice));
+    }
     NCM_CUDA_TRY(cudaMemcpy(ctx->rope_row_level, lev.data(), 4 * T, cudaMemcpyHostToDevice));
     ctx->rope_key = key;
   }
@@ -251,8 +292,13 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
       Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
       NCM_CUDA_TRY(launch_rms_norm_bf16(h, L.ln_1, nullptr, nrm, Ti, static_cast<int>(Hd), eps, st));
     }
-    if ((rc = linear_bf16(ctx, nrm, L.qkv, L.qkv_bias, qkv, nullptr, T, Hd, QKV, st))) return rc;
-    {
+    if (T > 64) {
+      // RoPE and the V transpose in the projection's epilogue
+      if ((rc = linear_qkv_rope(ctx, nrm, L.qkv, L.qkv_bias, qkv, vt, ctx->rope_cos_bf, ctx->rope_sin_bf, T, Hd, QKV,
+                                static_cast<int64_t>(H + Hkv) * 64, st)))
+        return rc;
+    } else {
+      if ((rc = linear_bf16(ctx, nrm, L.qkv, L.qkv_bias, qkv, nullptr, T, Hd, QKV, st))) return rc;
       Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
       NCM_CUDA_TRY(launch_rope_bf16(qkv, QKV, Ti, H + Hkv, cosd, sind, st));
       NCM_CUDA_TRY(launch_v_transpose(qkv, QKV, static_cast<int64_t>(H + Hkv) * 64, Ti, Hkv * 64, vt, st));

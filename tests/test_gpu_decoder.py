@@ -275,3 +275,27 @@ def test_config4_forward_runs_and_is_normalised(cuda_dev):
     assert torch.isfinite(o).all()
     rms = o.pow(2).mean(dim=1).sqrt()
     assert torch.allclose(rms, torch.ones_like(rms), atol=2e-2)
+
+
+def test_qkv_projection_rope_equals_linear_then_rope(orc, cuda_dev):
+    """The fused QKV epilogue (RoPE + V transpose) is bit-identical to the
+    separate projection and the RoPE that ncm_attention_bf16 applies."""
+    import ctypes
+    from ncmorph_b200 import _lib, device, kernels, ncm_model
+    T, hidden, H, Hkv = 320, 256, 4, 2
+    g = torch.Generator(device=cuda_dev).manual_seed(12)
+    x = torch.randn((T, hidden), generator=g, device=cuda_dev).to(torch.bfloat16)
+    w = (torch.randn(((H + 2 * Hkv) * 64, hidden), generator=g, device=cuda_dev) * 0.05).to(torch.bfloat16)
+    pos = ncm_model.level_positions(0, (64, 64, 64, 128))
+    c, s = ncm_model.rope_tables(64, 500000.0, pos)
+    cd, sd = torch.from_numpy(c).to(cuda_dev), torch.from_numpy(s).to(cuda_dev)
+    qkv = torch.empty((T, (H + 2 * Hkv) * 64), dtype=torch.bfloat16, device=cuda_dev)
+    vt = torch.empty((Hkv * 64, T), dtype=torch.bfloat16, device=cuda_dev)
+    _lib.call("ncm_qkv_projection_rope", device.context(cuda_dev), x.data_ptr(), w.data_ptr(), None, cd.data_ptr(),
+              sd.data_ptr(), qkv.data_ptr(), vt.data_ptr(), T, hidden, H, Hkv, device.stream_of(x))
+    ref = kernels.linear_bf16(x, w)
+    mask = ncm_model.make_mask("causal")
+    ncm_model.attention_bf16(ref, H, Hkv, mask, cos=cd, sin=sd)   # applies RoPE to ref in place
+    torch.cuda.synchronize()
+    assert torch.equal(qkv.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(vt.view(torch.int16), ref[:, (H + Hkv) * 64:].t().contiguous().view(torch.int16))
