@@ -150,7 +150,8 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
                           RvqPartial* part, const RvqPlan& plan, int64_t N, int64_t D, int64_t K, bool update,
                           cudaStream_t stream, const RvqTop2* top2 = nullptr) {
   CUtensorMap tmA, tmB;
-  if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) || !make_tmap_bf16_2d(&tmB, codebook, K, D, 256))
+  if (!make_tmap_bf16_2d(&tmA, a_bf16, N, D, 128) ||
+      !make_tmap_bf16_2d(&tmB, codebook, K, D, rvq_codebook_box_rows(plan)))
     return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
                     (long long)D, (long long)K);
   // Code splits merge inside the distance kernel (split fixup) only when no
@@ -445,7 +446,7 @@ int ncm_rvq_level(ncm_ctx_t* ctx, float* residual, const uint16_t* codebook, con
   if (!aligned16(residual) || !aligned16(codebook) || !aligned16(codes) || (sqnorm && !aligned16(sqnorm)))
     return ncm_fail(NCM_EINVAL, "rvq_level: buffers must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K, true);
   WsCarver cv;
   const size_t o_sh = cv.take(2 * N * D);
   const size_t o_part = cv.take(plan.partial_bytes);
@@ -524,7 +525,7 @@ int ncm_rvq_encode(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* codebooks,
       (recon && !aligned16(recon)) || (residual_out && !aligned16(residual_out)))
     return ncm_fail(NCM_EINVAL, "rvq_encode: buffers must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, N, K, true);
   WsCarver cv;
   const size_t o_sh = cv.take(2 * N * D);
   const size_t o_res = residual_out ? 0 : cv.take(sizeof(float) * N * D);
@@ -561,7 +562,7 @@ int ncm_rvq_encode_sharded(ncm_ctx_t* ctx, const uint16_t* x_local, const uint16
   const int P = ctx->comm_size, me = ctx->comm_rank;
   const int64_t N = n_local * P;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const RvqPlan plan = rvq_plan(ctx->num_sms, n_local, K);
+  const RvqPlan plan = rvq_plan(ctx->num_sms, n_local, K, true);
   WsCarver cv;
   const size_t o_sh = cv.take(2 * n_local * D);
   const size_t o_res = cv.take(sizeof(float) * n_local * D);
@@ -611,10 +612,10 @@ int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* 
   const int64_t wave_rows = static_cast<int64_t>(ctx->num_sms) * 128 * 7;
   const int64_t nchunks = std::max<int64_t>(1, std::min<int64_t>(16, (N + wave_rows - 1) / wave_rows));
   const int64_t C = ((N + nchunks - 1) / nchunks + 127) / 128 * 128;
-  const RvqPlan plan_c = rvq_plan(ctx->num_sms, C, K);
+  const RvqPlan plan_c = rvq_plan(ctx->num_sms, C, K, true);
   size_t part_bytes = plan_c.partial_bytes;
   const int64_t last_rows = N - (nchunks - 1) * C;
-  if (last_rows > 0) part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, last_rows, K).partial_bytes);
+  if (last_rows > 0) part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, last_rows, K, true).partial_bytes);
   WsCarver cv;
   size_t o_x[2], o_codes[2], o_rec[2];
   for (int i = 0; i < 2; ++i) {
@@ -661,7 +662,7 @@ int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* 
     // compute: rows landed, and the slot's previous results are copied out
     NCM_CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[slot], 0));
     if (c >= 2) NCM_CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_out[slot], 0));
-    const RvqPlan plan = rvq_plan(ctx->num_sms, n, K);
+    const RvqPlan plan = rvq_plan(ctx->num_sms, n, K, true);
     if ((rc = rvq_encode_core(ctx, xd, codebooks, sqnorms, L, cd, rd, resid, false, shadow, part, plan, n, D, K, st)))
       return rc;
     NCM_CUDA_TRY(cudaEventRecord(ctx->ev_done[slot], st));
@@ -849,7 +850,7 @@ int ncm_tokenizer_forward_ex(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, 
   for (int s = 0; s < S; ++s) max_rows = std::max<int64_t>(max_rows, N / cfg->pool_factors[s]);
   size_t part_bytes = 0;
   for (int s = 0; s < S; ++s)
-    part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, N / cfg->pool_factors[s], K).partial_bytes);
+    part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, N / cfg->pool_factors[s], K, true).partial_bytes);
   WsCarver cv;
   const size_t o_h = cv.take(2 * N * D);
   const size_t o_r = cv.take(sizeof(float) * N * D);
@@ -896,7 +897,7 @@ int ncm_tokenizer_forward_ex(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* cfg, 
   for (int s = 0; s < S; ++s) {
     const int f = cfg->pool_factors[s];
     const int64_t rows = N / f;
-    const RvqPlan plan = rvq_plan(ctx->num_sms, rows, K);
+    const RvqPlan plan = rvq_plan(ctx->num_sms, rows, K, true);
     for (int l = 0; l < L; ++l) {
       const size_t cb_off = (static_cast<size_t>(s) * L + l) * K;
       rc = rvq_level_core(ctx, ub, nullptr, u, l == L - 1 ? nullptr : ub, codebooks + cb_off * D, sqnorms + cb_off,

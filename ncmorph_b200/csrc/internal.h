@@ -144,11 +144,15 @@ struct RvqPartial {
 
 // Plans how many code splits one level uses; returns workspace bytes needed
 // for the partial results (0 when no split).
+// pair = 1: CTA pairs share each MMA (units of 256 rows, splits = 1); the
+// codebook tensor map then needs a 128-row box (rvq_codebook_box_rows).
 struct RvqPlan {
   int row_blocks, code_tiles, splits, tiles_per_split, n_units, grid;
   size_t partial_bytes;
+  int pair;
 };
-RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K);
+RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K, bool allow_pair = false);
+inline uint32_t rvq_codebook_box_rows(const RvqPlan& p) { return p.pair ? 128u : 256u; }
 
 // Residual update done inside the distance kernel (only when the plan has
 // one code split): resid = (src_bf16 ? f32(src_bf16) : resid) - e[code],

@@ -20,6 +20,7 @@
 // A work unit is (row block of 128 residuals, range of code tiles). When the
 // rows alone cannot fill the GPU the code range is split, each split writes a
 // (distance, index) partial per row, and rvq_apply_kernel reduces them.
+#include <algorithm>
 #include <cfloat>
 #include <climits>
 #include <cmath>
@@ -41,9 +42,22 @@ constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
+// Stage layout of one CTA. PAIR: the CTA holds half of each 256-code tile
+// (its partner the other half), so a stage is half as large and six fit.
+template <bool PAIR>
+struct ArgminCfg {
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_TILE = B_ROWS * BK * 2;
+  // bytes the leader's full barrier counts per stage (both CTAs' copies in a pair)
+  static constexpr uint32_t STAGE_TX = PAIR ? 2u * (A_BYTES + B_TILE) : A_BYTES + B_TILE;
+};
+
+template <bool PAIR>
 struct __align__(1024) ArgminSmem {
+  static constexpr int STAGES = ArgminCfg<PAIR>::STAGES;
   uint8_t a[STAGES][A_BYTES];
-  uint8_t b[STAGES][B_BYTES];
+  uint8_t b[STAGES][ArgminCfg<PAIR>::B_TILE];
   float csq[4][BN];  // per epilogue warp: ||e||^2 of the current code tile
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -60,8 +74,11 @@ struct __align__(1024) ArgminSmem {
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t ARGMIN_SMEM = sizeof(ArgminSmem) + 1024;
-static_assert(ARGMIN_SMEM <= 232448, "shared memory budget");
+template <bool PAIR>
+constexpr size_t argmin_smem_bytes() {
+  return sizeof(ArgminSmem<PAIR>) + 1024;
+}
+static_assert(argmin_smem_bytes<false>() <= 232448 && argmin_smem_bytes<true>() <= 232448, "shared memory budget");
 
 struct ArgminArgs {
   const float* csq;
@@ -100,17 +117,29 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err) 
 }
 
 // GAP: also track the second-smallest distance per row for the top-2 gap.
-template <bool GAP>
+// PAIR: launched as clusters of 2 CTAs sharing each MMA (cta_group::2): a
+// unit is then 256 rows (128 per CTA) and the even CTA issues the MMAs.
+template <bool GAP, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     rvq_argmin_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const ArgminArgs args) {
+  constexpr int STAGES = ArgminCfg<PAIR>::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  ArgminSmem& S = *reinterpret_cast<ArgminSmem*>(smem_raw + pad);
+  ArgminSmem<PAIR>& S = *reinterpret_cast<ArgminSmem<PAIR>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nk = (args.D + BK - 1) / BK;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 = leader (issues the pair's MMAs)
+  const int cid = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ncl = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // unit -> first row this CTA owns, and the index of its 128-row block
+  auto unit_rows = [&](int unit, int& rbase, int& rblock) {
+    const int rb = unit / args.splits;
+    rbase = PAIR ? rb * 2 * BM + static_cast<int>(rank) * BM : rb * BM;
+    rblock = rbase / BM;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -119,7 +148,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S.tfull[b], 1);
-      mbar_init(&S.tempty[b], 4);
+      mbar_init(&S.tempty[b], PAIR ? 8 : 4);  // a pair's leader hears both CTAs' epilogues
       mbar_init(&S.upd_full[b], 4);
       mbar_init(&S.upd_empty[b], UPD_WARPS);
     }
@@ -130,14 +159,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&S.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&S.tmem_base, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&S.tmem_base, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair's barriers must be initialised in both CTAs before either signals the other
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort_flag = &S.abort_flag;
+  auto abort_all = [&]() {
+    raise_abort(abort_flag, args.err);
+    if constexpr (PAIR) st_shared_cluster_u32(mapa_shared(smem_u32(&S.abort_flag), rank ^ 1u), 1u);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -150,9 +190,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
-        const int rb = unit / args.splits;
-        const int sp = unit - rb * args.splits;
+      for (int unit = cid; ok && unit < args.n_units; unit += ncl) {
+        int rbase, rblock;
+        unit_rows(unit, rbase, rblock);
+        const int sp = unit - (unit / args.splits) * args.splits;
         const int t0 = sp * args.tiles_per_split;
         const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
         for (int t = t0; ok && t < t1; ++t) {
@@ -161,9 +202,18 @@ __global__ void __launch_bounds__(THREADS, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&S.full[stage], A_BYTES + B_BYTES);
-            tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, rb * BM);
-            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, t * BN);
+            if constexpr (PAIR) {
+              // both CTAs' copies complete on the leader's full barrier; the
+              // leader posts the expected bytes of both
+              if (rank == 0) mbar_arrive_expect_tx(&S.full[stage], ArgminCfg<PAIR>::STAGE_TX);
+              const uint32_t fb = mapa_shared(smem_u32(&S.full[stage]), 0);
+              tma_load_2d_pair(&tmA, fb, S.a[stage], kc * BK, rbase);
+              tma_load_2d_pair(&tmB, fb, S.b[stage], kc * BK, t * BN + static_cast<int>(rank) * (BN / 2));
+            } else {
+              mbar_arrive_expect_tx(&S.full[stage], ArgminCfg<PAIR>::STAGE_TX);
+              tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, rbase);
+              tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, t * BN);
+            }
             issued[stage] = true;
             issued_parity[stage] = phase;
             if (++stage == STAGES) {
@@ -174,26 +224,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) {
-        raise_abort(abort_flag, args.err);
-        // let every copy this thread issued land before the CTA exits
-        for (int s = 0; s < STAGES; ++s)
-          if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+        abort_all();
+        // let every copy this thread issued land before the CTA exits (a
+        // pair's follower cannot observe the leader's barrier: it waits a
+        // fixed 20 us, far longer than any copy takes)
+        if (!PAIR || rank == 0) {
+          for (int s = 0; s < STAGES; ++s)
+            if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+        } else {
+          __nanosleep(20000);
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || rank == 0)) {
       // ------------------------------------------------ MMA issuer
-      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
-        const int rb = unit / args.splits;
-        const int sp = unit - rb * args.splits;
+      for (int unit = cid; ok && unit < args.n_units; unit += ncl) {
+        const int sp = unit - (unit / args.splits) * args.splits;
         const int t0 = sp * args.tiles_per_split;
         const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
-        (void)rb;
         for (int t = t0; ok && t < t1; ++t) {
           const uint32_t b = acc_it & 1u;
           const uint32_t ap = (acc_it >> 1) & 1u;
@@ -213,23 +267,38 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t b0 = smem_u32(S.b[stage]);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
-              tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
-                         (kc | k) != 0 ? 1u : 0u);
+              if constexpr (PAIR)
+                tc_mma_f16_pair(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                                (kc | k) != 0 ? 1u : 0u);
+              else
+                tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                           (kc | k) != 0 ? 1u : 0u);
             }
-            tc_commit(&S.empty[stage]);
+            // the stage is free again in both CTAs of a pair
+            if constexpr (PAIR)
+              tc_commit_pair(&S.empty[stage], 0x3);
+            else
+              tc_commit(&S.empty[stage]);
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (!ok) break;
-          tc_commit(&S.tfull[b]);
+          if constexpr (PAIR)
+            tc_commit_pair(&S.tfull[b], 0x3);
+          else
+            tc_commit(&S.tfull[b]);
           ++acc_it;
         }
       }
       if (!ok) {
-        raise_abort(abort_flag, args.err);
-        tc_commit(&S.drain);  // wait for every MMA issued so far before TMEM is freed
+        abort_all();
+        // wait for every MMA issued so far before TMEM is freed
+        if constexpr (PAIR)
+          tc_commit_pair(&S.drain, 0x1);
+        else
+          tc_commit(&S.drain);
         mbar_wait(&S.drain, 0, nullptr);
       }
     }
@@ -242,12 +311,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t uit = 0;     // units handed to the update warps
     uint32_t fix_ph = 0;  // phase of the split-fixup handshake barriers
     bool ok = true;
-    for (int unit = blockIdx.x; ok && unit < args.n_units; unit += gridDim.x) {
-      const int rb = unit / args.splits;
-      const int sp = unit - rb * args.splits;
+    for (int unit = cid; ok && unit < args.n_units; unit += ncl) {
+      int rbase, rb;
+      unit_rows(unit, rbase, rb);
+      const int sp = unit - (unit / args.splits) * args.splits;
       const int t0 = sp * args.tiles_per_split;
       const int t1 = min(t0 + args.tiles_per_split, args.code_tiles);
-      const int row = rb * BM + q * 32 + lane;
+      const int row = rbase + q * 32 + lane;
       float best = INFINITY;
       int bidx = t0 * BN;
       float s1 = INFINITY, s2 = INFINITY;  // GAP: smallest and second-smallest distance
@@ -307,7 +377,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.tempty[b]);
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(smem_u32(&S.tempty[b]), 0));  // the leader's barrier
+          else
+            mbar_arrive(&S.tempty[b]);
+        }
         ++acc_it;
       }
       if (!ok) break;
@@ -394,7 +469,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = false;
       }
     }
-    if (!ok) raise_abort(abort_flag, args.err);
+    if (!ok) abort_all();
   } else if (args.fuse) {
     // ------------------------------------------------- residual update
     // Warp uw updates rows uw*16.. of each finished row block: one row at a
@@ -459,15 +534,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&S.upd_empty[ub]);
       ++uit;
     }
-    if (!ok) raise_abort(abort_flag, args.err);
+    if (!ok) abort_all();
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  // a pair's partner may still read this CTA's shared memory (the leader's
+  // MMAs) or arrive on its barriers until both are done
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, TMEM_COLS);
+    else
+      tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -771,10 +852,56 @@ __global__ void __launch_bounds__(256) bf16_to_f32_kernel(const uint16_t* __rest
 
 // ================================================================== host
 
-RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K) {
+namespace {
+// How many 2-CTA clusters of the pair kernel fit on this device at once
+// (cluster placement can leave SMs idle); cached per device.
+int max_active_pairs(int num_sms) {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms / 2;
+  if (cached[dev] > 0) return cached[dev];
+  int n = 0;
+  const size_t smem = argmin_smem_bytes<true>();
+  if (cudaFuncSetAttribute(rvq_argmin_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (num_sms / 2));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, rvq_argmin_kernel<false, true>, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cached[dev] = n > 0 ? std::min(n, num_sms / 2) : -1;
+  return cached[dev];
+}
+}  // namespace
+
+RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K, bool allow_pair) {
   RvqPlan p{};
   p.row_blocks = ceil_div(N, BM);
   p.code_tiles = ceil_div(K, BN);
+  if (allow_pair) {
+    // CTA pairs (one MMA over 256 rows, each CTA loading half of every code
+    // tile) when the 256-row units alone fill every pair: no code split
+    const int pairs = max_active_pairs(num_sms);
+    const int units = ceil_div(N, 2 * BM);
+    if (pairs > 0 && units >= pairs) {
+      p.pair = 1;
+      p.splits = 1;
+      p.tiles_per_split = p.code_tiles;
+      p.n_units = units;
+      p.grid = 2 * pairs;
+      p.partial_bytes = 0;
+      return p;
+    }
+  }
   if (p.row_blocks >= num_sms) {
     // enough row blocks for every SM: no code split, so the residual update
     // can run inside the distance kernel
@@ -813,17 +940,23 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu,
                               const RvqTop2* top2, const float* mul_dev, int* counters) {
+  if (plan.pair && (top2 != nullptr || plan.splits != 1)) return cudaErrorInvalidValue;
   // the shared-memory opt-in is per device and per instantiation: remember which devices have it
-  static unsigned long long attr_set[2] = {0, 0};
-  const int gi = top2 != nullptr ? 1 : 0;
+  static unsigned long long attr_set[3] = {0, 0, 0};
+  const int gi = plan.pair ? 2 : (top2 != nullptr ? 1 : 0);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !(attr_set[gi] & (1ull << dev))) {
-    e = gi ? cudaFuncSetAttribute(rvq_argmin_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)ARGMIN_SMEM)
-           : cudaFuncSetAttribute(rvq_argmin_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)ARGMIN_SMEM);
+    if (gi == 2)
+      e = cudaFuncSetAttribute(rvq_argmin_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(argmin_smem_bytes<true>()));
+    else if (gi == 1)
+      e = cudaFuncSetAttribute(rvq_argmin_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(argmin_smem_bytes<false>()));
+    else
+      e = cudaFuncSetAttribute(rvq_argmin_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(argmin_smem_bytes<false>()));
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set[gi] |= 1ull << dev;
   }
@@ -847,13 +980,28 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.shadow = fu ? fu->shadow : nullptr;
   a.codebook = fu ? fu->codebook : nullptr;
   a.mul_dev = mul_dev;
-  if (top2 != nullptr) {
+  if (plan.pair) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = argmin_smem_bytes<true>();
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, rvq_argmin_kernel<false, true>, tmA, tmB, a);
+    if (e != cudaSuccess) return e;
+  } else if (top2 != nullptr) {
     a.gap = top2->gap;
     a.a2 = top2->a2;
     a.part_d2 = top2->part_d2;
-    rvq_argmin_kernel<true><<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+    rvq_argmin_kernel<true, false><<<plan.grid, THREADS, argmin_smem_bytes<false>(), stream>>>(tmA, tmB, a);
   } else {
-    rvq_argmin_kernel<false><<<plan.grid, THREADS, ARGMIN_SMEM, stream>>>(tmA, tmB, a);
+    rvq_argmin_kernel<false, false><<<plan.grid, THREADS, argmin_smem_bytes<false>(), stream>>>(tmA, tmB, a);
   }
   return cudaGetLastError();
 }
