@@ -134,7 +134,7 @@ def ncu_traffic(rows_per_launch: int):
     """DRAM bytes per rvq_argmin launch from the committed ncu summary, scaled
     from the captured case to this launch by rows (traffic ~ rows * D * 2
     plus one codebook read)."""
-    p = ROOT / "profiles" / "rvq_argmin_kernel_n131072.md"
+    p = ROOT / "profiles" / "rvq_argmin_pair_kernel_n131072.md"
     if not p.exists():
         return None
     d = {}
