@@ -1,22 +1,29 @@
 // Fused masked GQA attention on tcgen05 (L3), for the NCM decoder forward.
 //
-// One CTA per (128-query tile, query head). Per key tile of 128:
-//   S = Q . K^T           tcgen05.mma M=128 N=128 K=64, f32 in TMEM (2 buffers)
-//   online softmax        4 epilogue warps, one query row per thread, in registers
-//   P (bf16) -> smem      128-byte-swizzled, the A operand of the next MMA
-//   O_tile = P . V        tcgen05.mma M=128 N=64 K=128, f32 in TMEM (2 buffers)
-//   o = o*alpha + O_tile  accumulated in registers with the running-max correction
-// The MMA of S for tile j+1 and of P.V for tile j overlap the softmax of the
-// neighbouring tiles. Key tiles that the mask removes entirely are never
-// loaded. K tiles come straight from the fused QKV projection output by TMA;
-// V is read transposed ([kv_head*64 + d][t], written by the RoPE kernel) so
-// both MMAs take K-major operands.
+// One CTA per (256 queries = two 128-query tiles Q0 and Q1, query head), both
+// tiles sharing every K/V stage. Per key tile of 128:
+//   S_i = Q_i . K^T       tcgen05.mma M=128 N=128 K=64, f32 in TMEM
+//   softmax               one thread per query row (warps 2-5: Q0, 6-9: Q1),
+//                         reading its whole S row from TMEM; P (bf16) into a
+//                         128-byte-swizzled smem tile, the A operand of P.V
+//   O_i += P_i . V        tcgen05.mma M=128 N=64 K=128, accumulated in TMEM
+// The MMA warp interleaves the two tiles (P.V and the next S of one run while
+// the other group computes its softmax). Key tiles that the mask removes
+// entirely are never loaded, and CTAs launch heaviest first (late query
+// tiles see the most keys). K tiles come straight from the fused QKV rows by
+// TMA; V is read transposed ([kv_head*64 + d][t]) so both MMAs take K-major
+// operands.
+//
+// Softmax in the log2 domain with a lagging reference maximum: after a row's
+// first tile, a tile runs in one pass against the running reference (p may
+// exceed 1; f32 sums and bf16 P carry it exactly up to 2^64); only a row
+// without a reference, or whose maximum jumped by more than 2^64, makes its
+// warp redo the tile in two passes (maximum first) and rescale O_i in TMEM.
 //
 // Score rounding follows ncmorph's bf16 attention (packages/kernels/root.zig:
-// 546-548): s = bf16(bf16(q.k) * scale). The softmax is computed online
-// (running max), probabilities enter the P.V product as bf16, and the
-// context is rounded once to bf16 — within the bf16 bar of the reference's
-// materialised softmax, not bit-equal to it.
+// 546-548): the raw score q.k is rounded to bf16 before scaling. Probabilities
+// enter P.V as bf16 and the context is rounded once to bf16 — within the bf16
+// bar of the reference's materialised softmax, not bit-equal to it.
 #include <cfloat>
 #include <cmath>
 
@@ -26,38 +33,12 @@
 namespace ncm {
 namespace {
 
-constexpr int AT_Q = 128;       // queries per CTA
+constexpr int AT_Q = 128;       // queries per tile (two tiles per CTA)
 constexpr int AT_K = 128;       // keys per tile
 constexpr int AT_D = 64;        // head dim (fixed)
-constexpr int AT_STAGES = 3;
-constexpr int AT_THREADS = 320;  // w0 TMA, w1 MMA, w2-9 softmax
-constexpr uint32_t AT_TMEM_COLS = 512;  // S: 2 x 128 cols, O: 2 x 64 cols
+constexpr int AT_THREADS = 320;  // w0 TMA, w1 MMA, w2-5 softmax of Q0, w6-9 softmax of Q1
+constexpr uint32_t AT_TMEM_COLS = 512;  // S_0, S_1: 128 cols each; O_0, O_1: 64 cols each
 constexpr int kMaxLevels = 32;
-
-struct __align__(1024) AttnSmem {
-  uint8_t q[AT_Q * AT_D * 2];                 // 16 KB
-  uint8_t k[AT_STAGES][AT_K * AT_D * 2];      // 16 KB each
-  uint8_t vt[AT_STAGES][2][AT_D * 64 * 2];    // 2 x 8 KB each: [64 d rows x 64 keys] per half
-  uint8_t p[2][2][AT_Q * 64 * 2];             // 2 buffers x 2 key halves x 16 KB
-  uint64_t q_full;
-  uint64_t kv_full[AT_STAGES];
-  uint64_t kv_empty[AT_STAGES];
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full[2];
-  uint64_t p_empty[2];
-  uint64_t o_full[2];
-  uint64_t o_empty[2];
-  uint64_t mx_ready[2];
-  uint64_t l_ready;
-  uint64_t drain;
-  float mx[2][2][AT_Q];   // [tile parity][key half][row] partial row maxima
-  float lsum[2][AT_Q];    // [key half][row] final partial row sums
-  uint32_t tmem_base;
-  int abort_flag;
-};
-constexpr size_t ATTN_SMEM = sizeof(AttnSmem) + 1024;
-static_assert(ATTN_SMEM <= 232448, "attention smem budget");
 
 struct AttnArgs {
   uint16_t* out;  // [T, H*64] bf16
@@ -114,36 +95,116 @@ __device__ __forceinline__ void raise_abort_attn(volatile int* abort_flag, int* 
   atomicOr(err, kErrWaitTimeout);
 }
 
+constexpr int A2_STAGES = 3;
+constexpr float kRescaleLog2 = 8.0f;
+
+struct __align__(1024) Attn2Smem {
+  uint8_t q[2][AT_Q * AT_D * 2];              // 2 x 16 KB
+  uint8_t k[A2_STAGES][AT_K * AT_D * 2];      // 16 KB each
+  uint8_t vt[A2_STAGES][2][AT_D * 64 * 2];    // 2 x 8 KB each: [64 d rows x 64 keys] per key half
+  uint8_t p[2][2][AT_Q * 64 * 2];             // [query tile][key half] 16 KB, 128-byte swizzle
+  uint64_t q_full;
+  uint64_t kv_full[A2_STAGES];
+  uint64_t kv_empty[A2_STAGES];
+  uint64_t s_full[2];   // S_i computed
+  uint64_t p_full[2];   // P_i written (and O_i rescaled): the 4 warps of group i
+  uint64_t p_empty[2];  // P_i . V done: P_i and O_i free again
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t ATTN2_SMEM = sizeof(Attn2Smem) + 1024;
+static_assert(ATTN2_SMEM <= 232448, "attention smem budget");
+
+// One pass over a 128-key S row in tensor memory: p = 2^(bf16(s) * c_scale -
+// m_use) for allowed keys (0 for masked ones) stored as bf16 into the row of
+// the 128-byte-swizzled P tile (two 64-key halves), their sum added to rs.
+// Returns the row's maximum bf16-rounded score times c_scale (log2 domain).
+__device__ __forceinline__ float softmax_tile_pass(uint8_t (*p_half)[AT_Q * 64 * 2], uint32_t sbase, int row,
+                                                   int k0, bool unmasked, int Pq, int lo, int hi,
+                                                   unsigned long long pad_mask, float c_scale, float m_use,
+                                                   float& rs) {
+  const unsigned long long cs2 = f2_pack(c_scale, c_scale), nm2 = f2_pack(-m_use, -m_use);
+  unsigned long long rs2 = f2_pack(0.f, 0.f);
+  uint32_t mx2 = 0xFF80FF80u;  // bf16x2 -inf
+#pragma unroll 1
+  for (int c = 0; c < AT_K; c += 32) {
+    uint32_t v[32];
+    tmem_ld_x32(sbase + c, v);
+    tmem_wait_ld();
+    if (!unmasked) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (!key_allowed(k0 + c + e, Pq, lo, hi, pad_mask)) v[e] = __float_as_uint(-INFINITY);
+    }
+    uint8_t* prow = p_half[c >> 6] + row * 128;
+    const int ch0 = (c & 63) >> 3;
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {  // four 16-byte chunks of 8 keys
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ii = q4 * 8 + e * 2;
+        const uint32_t pr = cvt_bf16x2(__uint_as_float(v[ii]), __uint_as_float(v[ii + 1]));
+        mx2 = bf16x2_max(mx2, pr);
+        const unsigned long long t2 = f2_fma(f2_pack(bf16lo(pr), bf16hi(pr)), cs2, nm2);
+        float t0, t1;
+        f2_unpack(t2, t0, t1);
+        const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+        w4[e] = cvt_bf16x2(p0, p1);
+        rs2 = f2_add(rs2, f2_pack(p0, p1));
+      }
+      const int sw = (ch0 + q4) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
+      *reinterpret_cast<uint4*>(prow + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  }
+  float r0, r1;
+  f2_unpack(rs2, r0, r1);
+  rs += r0 + r1;
+  return fmaxf(bf16lo(mx2), bf16hi(mx2)) * c_scale;
+}
+
+struct TileSpan {
+  int P, A, B;
+  bool has;
+  __device__ __forceinline__ bool need(int t) const { return has && tile_needed(t, P, A, B); }
+};
+
 __global__ void __launch_bounds__(AT_THREADS, 1)
-    attention_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmVt, const AttnArgs args) {
+    attention2_bf16_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmVt, const AttnArgs args) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw + pad);
+  Attn2Smem& S = *reinterpret_cast<Attn2Smem*>(smem_raw + pad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * AT_Q;
-  const int h = blockIdx.y;
+  // CTAs are ordered heaviest first: causal masks give late query tiles the
+  // most keys, so the last query-tile pair of every head launches first and
+  // the light early tiles fill the tail of the grid
+  const int n_qp = (args.T + 2 * AT_Q - 1) / (2 * AT_Q);
+  const int qp = n_qp - 1 - static_cast<int>(blockIdx.x) / args.H;
+  const int h = static_cast<int>(blockIdx.x) % args.H;
+  const int q0 = qp * 2 * AT_Q;
   const int kvh = h / (args.H / args.Hkv);
-  int P, A, B;
-  cta_key_span(args, q0, P, A, B);
-  const int n_tiles_all = (max(B, P) + AT_K - 1) / AT_K;
+  TileSpan span[2];
+  int n_tiles_all = 0;
+  for (int i = 0; i < 2; ++i) {
+    span[i].has = q0 + i * AT_Q < args.T;
+    cta_key_span(args, q0 + i * AT_Q, span[i].P, span[i].A, span[i].B);
+    if (span[i].has) n_tiles_all = max(n_tiles_all, (max(span[i].B, span[i].P) + AT_K - 1) / AT_K);
+  }
+  auto need_any = [&](int t) { return span[0].need(t) || span[1].need(t); };
 
   if (threadIdx.x == 0) {
     mbar_init(&S.q_full, 1);
-    for (int s = 0; s < AT_STAGES; ++s) {
+    for (int s = 0; s < A2_STAGES; ++s) {
       mbar_init(&S.kv_full[s], 1);
       mbar_init(&S.kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&S.s_full[b], 1);
-      mbar_init(&S.s_empty[b], 8);
-      mbar_init(&S.p_full[b], 8);
-      mbar_init(&S.p_empty[b], 1);
-      mbar_init(&S.o_full[b], 1);
-      mbar_init(&S.o_empty[b], 8);
-      mbar_init(&S.mx_ready[b], 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.s_full[i], 1);
+      mbar_init(&S.p_full[i], 4);
+      mbar_init(&S.p_empty[i], 1);
     }
-    mbar_init(&S.l_ready, 8);
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_mbar_init();
@@ -155,7 +216,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = S.tmem_base;
+  const uint32_t tmem = S.tmem_base;  // S_i at columns 128 i, O_i at 256 + 64 i
   volatile int* abort_flag = &S.abort_flag;
 
   if (warp == 0) {
@@ -164,16 +225,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmVt);
-      mbar_arrive_expect_tx(&S.q_full, AT_Q * AT_D * 2);
-      tma_load_2d(&tmQ, &S.q_full, S.q, h * AT_D, q0);
+      mbar_arrive_expect_tx(&S.q_full, (span[1].has ? 2 : 1) * AT_Q * AT_D * 2);
+      tma_load_2d(&tmQ, &S.q_full, S.q[0], h * AT_D, q0);
+      if (span[1].has) tma_load_2d(&tmQ, &S.q_full, S.q[1], h * AT_D, q0 + AT_Q);
       int stage = 0;
       uint32_t phase = 0;
-      bool issued[AT_STAGES];
-      uint32_t iss_par[AT_STAGES];
-      for (int s = 0; s < AT_STAGES; ++s) issued[s] = false, iss_par[s] = 0;
+      bool issued[A2_STAGES];
+      uint32_t iss_par[A2_STAGES];
+      for (int s = 0; s < A2_STAGES; ++s) issued[s] = false, iss_par[s] = 0;
       bool ok = true;
       for (int t = 0; t < n_tiles_all && ok; ++t) {
-        if (!tile_needed(t, P, A, B)) continue;
+        if (!need_any(t)) continue;
         if (!mbar_wait(&S.kv_empty[stage], phase ^ 1u, abort_flag)) {
           ok = false;
           break;
@@ -184,7 +246,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tma_load_2d(&tmVt, &S.kv_full[stage], S.vt[stage][1], t * AT_K + 64, kvh * AT_D);
         issued[stage] = true;
         iss_par[stage] = phase;
-        if (++stage == AT_STAGES) {
+        if (++stage == A2_STAGES) {
           stage = 0;
           phase ^= 1u;
         }
@@ -192,7 +254,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       if (!ok) {
         raise_abort_attn(abort_flag, args.err);
         mbar_wait(&S.q_full, 0, nullptr);
-        for (int s = 0; s < AT_STAGES; ++s)
+        for (int s = 0; s < A2_STAGES; ++s)
           if (issued[s]) mbar_wait(&S.kv_full[s], iss_par[s], nullptr);
       }
     }
@@ -203,58 +265,71 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const uint32_t idesc_o = idesc_bf16_f32(AT_Q, AT_D);
       bool ok = mbar_wait(&S.q_full, 0, abort_flag);
       tc_fence_after();
-      const uint32_t qa = smem_u32(S.q);
-      int stage = 0, prev_stage = 0;
+      auto next_needed = [&](int t) {
+        for (int u = t + 1; u < n_tiles_all; ++u)
+          if (need_any(u)) return u;
+        return -1;
+      };
+      auto issue_s = [&](int i, int st) {
+        const uint32_t qa = smem_u32(S.q[i]), ka = smem_u32(S.k[st]);
+#pragma unroll
+        for (int k = 0; k < AT_D / 16; ++k)
+          tc_mma_f16(tmem + i * AT_K, smem_desc_k_sw128(qa + k * 32), smem_desc_k_sw128(ka + k * 32), idesc_s,
+                     k != 0 ? 1u : 0u);
+        tc_commit(&S.s_full[i]);
+      };
+      int cur = next_needed(-1);
+      int stage = 0;
       uint32_t phase = 0;
-      int j = 0;  // index among needed tiles
-      for (int t = 0; t <= n_tiles_all && ok; ++t) {
-        const bool have = t < n_tiles_all && tile_needed(t, P, A, B);
-        if (t < n_tiles_all && !have) continue;
-        if (have) {
-          // S_j = Q . K^T
-          const uint32_t b = j & 1, bp = (j >> 1) & 1;
-          if (!mbar_wait(&S.kv_full[stage], phase, abort_flag) || !mbar_wait(&S.s_empty[b], bp ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ka = smem_u32(S.k[stage]);
+      uint32_t npv[2] = {0u, 0u};  // P.V products issued per query tile
+      if (ok && cur >= 0) {
+        if (!mbar_wait(&S.kv_full[0], 0, abort_flag)) ok = false;
+        tc_fence_after();
+        for (int i = 0; ok && i < 2; ++i)
+          if (span[i].need(cur)) issue_s(i, 0);
+      }
+      while (ok && cur >= 0) {
+        const int nxt = next_needed(cur);
+        int nstage = stage + 1;
+        uint32_t nphase = phase;
+        if (nstage == A2_STAGES) nstage = 0, nphase ^= 1u;
+        bool kv_ready = false;
+        for (int i = 0; i < 2; ++i) {
+          if (span[i].need(cur)) {
+            // O_i (+)= P_i . V_cur once the softmax of group i released the tile
+            if (!mbar_wait(&S.p_full[i], npv[i] & 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < AT_D / 16; ++k)
-            tc_mma_f16(tmem + b * AT_K, smem_desc_k_sw128(qa + k * 32), smem_desc_k_sw128(ka + k * 32), idesc_s,
-                       k != 0 ? 1u : 0u);
-          tc_commit(&S.s_full[b]);
-        }
-        if (j > 0) {
-          // O_{j-1} = P_{j-1} . V_{j-1}
-          const int jp = j - 1;
-          const uint32_t b = jp & 1, bp = (jp >> 1) & 1;
-          if (!mbar_wait(&S.p_full[b], bp, abort_flag) || !mbar_wait(&S.o_empty[b], bp ^ 1u, abort_flag)) {
-            ok = false;
-            break;
+            for (int kk = 0; kk < AT_K / 16; ++kk) {
+              const uint32_t pa = smem_u32(S.p[i][kk >> 2]) + (kk & 3) * 32;
+              const uint32_t va = smem_u32(S.vt[stage][kk >> 2]) + (kk & 3) * 32;
+              tc_mma_f16(tmem + 2 * AT_K + i * AT_D, smem_desc_k_sw128(pa), smem_desc_k_sw128(va), idesc_o,
+                         (npv[i] > 0 || kk != 0) ? 1u : 0u);
+            }
+            tc_commit(&S.p_empty[i]);
+            ++npv[i];
           }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < AT_K / 16; ++kk) {
-            const uint32_t pa = smem_u32(S.p[b][kk >> 2]) + (kk & 3) * 32;
-            const uint32_t va = smem_u32(S.vt[prev_stage][kk >> 2]) + (kk & 3) * 32;
-            tc_mma_f16(tmem + 2 * AT_K + b * AT_D, smem_desc_k_sw128(pa), smem_desc_k_sw128(va), idesc_o,
-                       kk != 0 ? 1u : 0u);
+          if (nxt >= 0 && span[i].need(nxt)) {
+            // the S_i buffer is free: its softmax finished reading (p_full waited above, or long ago)
+            if (!kv_ready) {
+              if (!mbar_wait(&S.kv_full[nstage], nphase, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              kv_ready = true;
+            }
+            issue_s(i, nstage);
           }
-          tc_commit(&S.o_full[b]);
-          tc_commit(&S.p_empty[b]);
-          tc_commit(&S.kv_empty[prev_stage]);
         }
-        if (have) {
-          prev_stage = stage;
-          if (++stage == AT_STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-          ++j;
-        } else {
-          break;
-        }
+        if (!ok) break;
+        tc_commit(&S.kv_empty[stage]);
+        cur = nxt;
+        stage = nstage;
+        phase = nphase;
       }
       if (!ok) {
         raise_abort_attn(abort_flag, args.err);
@@ -263,17 +338,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------- softmax / epilogue
-    // Eight warps: warp w reads TMEM lanes 32*(w%4).. (its 32 query rows) and
-    // owns key columns [64*hf, 64*hf + 64) of each S tile and output dims
-    // [32*hf, 32*hf + 32) of O, hf = (w - 2) / 4. The two warps of a row group
-    // swap their partial row maxima through shared memory each tile.
-    // Scores live in the log2 domain: t = bf16(q.k) * scale * log2(e), so
-    // p = 2^(t - max t) and alpha = 2^(old max - new max).
+    // ------------------------------------------------------------ softmax
+    const int gi = (warp - 2) >> 2;  // query tile of this warp group
     const int qw = warp & 3;
-    const int hf = (warp - 2) >> 2;
     const int row = qw * 32 + lane;
-    const int q = q0 + row;
+    const int q = q0 + gi * AT_Q + row;
+    const TileSpan sp = span[gi];
     int lo = 0, hi = 0;
     if (args.mode == 0) {
       lo = 0;
@@ -285,165 +355,123 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     const int Pq = args.mode == 0 ? 0 : args.prefix;
     const float c_scale = args.scale * 1.4426950408889634f;
-    constexpr int HK = AT_K / 2, HD = AT_D / 2;
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    const uint32_t lane_base = static_cast<uint32_t>(qw * 32) << 16;
+    const uint32_t sbase = tmem + lane_base + gi * AT_K;
+    const uint32_t obase = tmem + lane_base + 2 * AT_K + gi * AT_D;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    int j = 0;
+    uint32_t j = 0;
     for (int t = 0; t < n_tiles_all; ++t) {
-      if (!tile_needed(t, P, A, B)) continue;
-      const uint32_t b = j & 1, bp = (j >> 1) & 1;
-      if (!mbar_wait(&S.s_full[b], bp, abort_flag)) {
+      if (!sp.need(t)) continue;
+      // every outcome that guards a warp-wide (.sync.aligned) TMEM access is made
+      // uniform across the warp, so no lane can take a branch its neighbours skip
+      if (!__all_sync(0xffffffffu, mbar_wait(&S.s_full[gi], j & 1u, abort_flag))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sbase = tmem + (static_cast<uint32_t>(qw * 32) << 16) + b * AT_K + hf * HK;
-      const int k0 = t * AT_K + hf * HK;
-      const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + HK <= hi);
-      // pass 1: max of this warp's 64 raw scores per row (rounding to bf16 is
-      // monotonic, so the max of the rounded scores is the rounded max); in a
-      // tile the mask touches, disallowed scores become -inf in TMEM first
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < HK; c += 32) {
-        uint32_t v[32];
-        tmem_ld_x32(sbase + c, v);
-        tmem_wait_ld();
-        if (!unmasked) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (!key_allowed(k0 + c + i, Pq, lo, hi, args.pad_mask)) v[i] = __float_as_uint(-INFINITY);
-          tmem_st_x32(sbase + c, v);
-        }
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          mx0 = fmaxf(mx0, __uint_as_float(v[i]));
-          mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
-        }
-      }
-      if (!unmasked) tmem_wait_st();
-      // swap partial maxima with the partner warp (same rows, other key half)
-      S.mx[b][hf][row] = fmaxf(mx0, mx1);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.mx_ready[b]);
-      if (!mbar_wait(&S.mx_ready[b], bp, abort_flag)) {
+      const int k0 = t * AT_K;
+      const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + AT_K <= hi);
+      // P_i and O_i are free once P.V of this group's previous tile completed
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&S.p_empty[gi], (j - 1) & 1u, abort_flag))) {
         ok = false;
         break;
       }
-      const float raw_max = fmaxf(S.mx[b][0][row], S.mx[b][1][row]);
-      const float mt = bf16lo(cvt_bf16x2(raw_max, 0.f)) * c_scale;
-      const float m_new = fmaxf(m, mt);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2_approx(m - m_use);  // m = -inf -> 0
-      // P_j (bf16): this warp's key half goes to P block hf; wait until P.V_{j-2} released it
-      if (!mbar_wait(&S.p_empty[b], bp ^ 1u, abort_flag)) {
-        ok = false;
-        break;
+      // One pass against the running reference m_used when every row of the
+      // warp has one: probabilities may then exceed 1 (the reference lags the
+      // true maximum), which f32 sums and bf16 P carry exactly up to 2^64. A
+      // row without a reference yet, or whose maximum jumped past m_used + 64,
+      // makes the warp redo the tile in two passes with a rescale.
+      bool two_pass = __any_sync(0xffffffffu, m_used == -INFINITY);
+      if (!two_pass) {
+        float rs = 0.f;
+        const float mt = softmax_tile_pass(S.p[gi], sbase, row, k0, unmasked, Pq, lo, hi, args.pad_mask, c_scale,
+                                           m_used, rs);
+        if (__any_sync(0xffffffffu, mt > m_used + 64.f)) {
+          two_pass = true;
+        } else {
+          l += rs;
+        }
       }
-      // pass 2: t = bf16(s) * scale*log2e - m, p = 2^t, packed f32x2 arithmetic
-      const unsigned long long cs2 = f2_pack(c_scale, c_scale), nm2 = f2_pack(-m_use, -m_use);
-      unsigned long long rs2 = f2_pack(0.f, 0.f);
-      uint8_t* prow = S.p[b][hf] + row * 128;
+      if (two_pass) {
+        // pass 1: row maximum of the raw scores (rounding to bf16 is monotonic)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < HK; c += 32) {
-        uint32_t v[32];
-        tmem_ld_x32(sbase + c, v);
-        tmem_wait_ld();
-        const int ch0 = c >> 3;
+        for (int c = 0; c < AT_K; c += 32) {
+          uint32_t v[32];
+          tmem_ld_x32(sbase + c, v);
+          tmem_wait_ld();
+          if (!unmasked) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {  // four 16-byte chunks of 8 keys
-          uint32_t w4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = q4 * 8 + e * 2;
-            const uint32_t pr = cvt_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-            const unsigned long long t2 = f2_fma(f2_pack(bf16lo(pr), bf16hi(pr)), cs2, nm2);
-            float t0, t1;
-            f2_unpack(t2, t0, t1);
-            const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-            w4[e] = cvt_bf16x2(p0, p1);
-            rs2 = f2_add(rs2, f2_pack(p0, p1));
+            for (int e = 0; e < 32; ++e)
+              if (!key_allowed(k0 + c + e, Pq, lo, hi, args.pad_mask)) v[e] = __float_as_uint(-INFINITY);
           }
-          const int sw = (ch0 + q4) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
-          *reinterpret_cast<uint4*>(prow + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+            mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+          }
         }
+        const float mt = bf16lo(cvt_bf16x2(fmaxf(mx0, mx1), 0.f)) * c_scale;
+        const bool rescale = mt > m_used + kRescaleLog2;  // m_used = -inf: any finite maximum
+        const float m_new = rescale ? mt : m_used;
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = rescale ? ex2_approx(m_used - m_new) : 1.f;  // -inf -> 0
+        // pass 2: t = bf16(s) * scale * log2(e) - m, p = 2^t (<= 256), bf16 into P_i
+        float rs = 0.f;
+        softmax_tile_pass(S.p[gi], sbase, row, k0, unmasked, Pq, lo, hi, args.pad_mask, c_scale, m_use, rs);
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          // O_i row *= alpha in tensor memory before the next P.V accumulates into
+          // it (the whole warp executes the TMEM accesses; rows without a rescale
+          // have alpha = 1)
+#pragma unroll 1
+          for (int c = 0; c < AT_D; c += 32) {
+            uint32_t v[32];
+            tmem_ld_x32(obase + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_x32(obase + c, v);
+          }
+          tmem_wait_st();
+        }
+        l = l * alpha + rs;
+        m_used = m_new;
       }
-      float rs0, rs1;
-      f2_unpack(rs2, rs0, rs1);
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&S.s_empty[b]);
-        mbar_arrive(&S.p_full[b]);
-      }
-      l = l * alpha + (rs0 + rs1);  // this warp's half of the row sum
-      m = m_new;
-      // fold in this warp's 32 columns of O_{j-1}
-      if (j > 0) {
-        const uint32_t bo = (j - 1) & 1, bop = ((j - 1) >> 1) & 1;
-        if (!mbar_wait(&S.o_full[bo], bop, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t v[HD];
-        tmem_ld_x32(tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D + hf * HD, v);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.o_empty[bo]);
-        const unsigned long long ap2 = f2_pack(alpha_prev, alpha_prev);
-#pragma unroll
-        for (int i = 0; i < HD; i += 2) {
-          const unsigned long long r2 =
-              f2_fma(f2_pack(o[i], o[i + 1]), ap2, f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
-          f2_unpack(r2, o[i], o[i + 1]);
-        }
-      }
-      alpha_prev = alpha;
+      if (lane == 0) mbar_arrive(&S.p_full[gi]);
       ++j;
     }
-    if (ok && j > 0) {
-      const uint32_t bo = (j - 1) & 1, bop = ((j - 1) >> 1) & 1;
-      if (!mbar_wait(&S.o_full[bo], bop, abort_flag)) {
-        ok = false;
-      } else {
-        tc_fence_after();
-        uint32_t v[HD];
-        tmem_ld_x32(tmem + (static_cast<uint32_t>(qw * 32) << 16) + 2 * AT_K + bo * AT_D + hf * HD, v);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.o_empty[bo]);
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(v[i]));
-      }
-    }
-    // the full row sum is the sum of both halves' sums
-    if (ok) {
-      S.lsum[hf][row] = l;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.l_ready);
-      ok = mbar_wait(&S.l_ready, 0, abort_flag);
-    }
+    if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&S.p_empty[gi], (j - 1) & 1u, abort_flag));
     if (!ok) raise_abort_attn(abort_flag, args.err);
-    if (ok && q < args.T) {
-      const float lt = S.lsum[0][row] + S.lsum[1][row];
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
-      uint16_t* dst = args.out + static_cast<size_t>(q) * args.H * AT_D + h * AT_D + hf * HD;
+    uint16_t* dst = args.out + static_cast<size_t>(q) * args.H * AT_D + h * AT_D;
+    if (ok && j > 0) {
+      // the whole warp reads its O rows; rows past T only skip the stores
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < AT_D; c += 32) {
+        uint32_t v[32];
+        tmem_ld_x32(obase + c, v);
+        tmem_wait_ld();
+        if (q < args.T) {
 #pragma unroll
-      for (int c = 0; c < HD; c += 8) {
-        uint4 w;
-        w.x = cvt_bf16x2(o[c + 0] * inv, o[c + 1] * inv);
-        w.y = cvt_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
-        w.z = cvt_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
-        w.w = cvt_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + c) = w;
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            w.x = cvt_bf16x2(__uint_as_float(v[e + 0]) * inv, __uint_as_float(v[e + 1]) * inv);
+            w.y = cvt_bf16x2(__uint_as_float(v[e + 2]) * inv, __uint_as_float(v[e + 3]) * inv);
+            w.z = cvt_bf16x2(__uint_as_float(v[e + 4]) * inv, __uint_as_float(v[e + 5]) * inv);
+            w.w = cvt_bf16x2(__uint_as_float(v[e + 6]) * inv, __uint_as_float(v[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c + e) = w;
+          }
+        }
       }
+    } else if (ok && q < args.T) {
+      // no allowed key at all (a fully masked row): the context is zero
+#pragma unroll
+      for (int c = 0; c < AT_D; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
@@ -500,12 +528,12 @@ int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const 
   int dev = 0;
   NCM_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 64 || !(attr_set & (1ull << dev))) {
-    NCM_CUDA_TRY(cudaFuncSetAttribute(attention_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(ATTN_SMEM)));
+    NCM_CUDA_TRY(cudaFuncSetAttribute(attention2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(ATTN2_SMEM)));
     if (dev < 64) attr_set |= 1ull << dev;
   }
-  dim3 grid((T + AT_Q - 1) / AT_Q, H);
-  attention_bf16_kernel<<<grid, AT_THREADS, ATTN_SMEM, stream>>>(tq, tk, tv, a);
+  const int n_qp = (T + 2 * AT_Q - 1) / (2 * AT_Q);
+  attention2_bf16_kernel<<<n_qp * H, AT_THREADS, ATTN2_SMEM, stream>>>(tq, tk, tv, a);
   NCM_CUDA_TRY(cudaGetLastError());
   return NCM_OK;
 }

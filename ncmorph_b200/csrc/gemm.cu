@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tile_coords(tile, args, ta, tb);
       const uint32_t b = acc_it & 1u;
       const uint32_t ap = (acc_it >> 1) & 1u;
-      if (!mbar_wait(&S.tfull[b], ap, abort_flag)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&S.tfull[b], ap, abort_flag))) {  // warp-uniform: TMEM loads follow
         ok = false;
         break;
       }

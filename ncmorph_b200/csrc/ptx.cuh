@@ -229,6 +229,13 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
 }
 
 // 2^x on the special-function unit (PTX ex2.approx; ~2 ulp, -inf -> 0).
+// Element-wise maximum of two packed bf16 pairs.
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

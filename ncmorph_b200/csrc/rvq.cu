@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           csq_s[j] = code < args.K ? __ldg(args.csq + code) : INFINITY;
         }
         __syncwarp();
-        if (!mbar_wait(&S.tfull[b], ap, abort_flag)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&S.tfull[b], ap, abort_flag))) {  // warp-uniform: TMEM loads follow
           ok = false;
           break;
         }
