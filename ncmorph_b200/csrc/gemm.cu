@@ -26,20 +26,25 @@ constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, interleaving 16-colu
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
 
-template <int BN>
+// PAIR: clusters of two CTAs share each MMA (tcgen05 cta_group::2, M = 256):
+// each CTA loads its own 128 rows of A and half of the BN-row B tile, the even
+// CTA issues the MMAs, and each CTA's TMEM receives its own 128 rows.
+template <int BN, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+  static constexpr uint32_t STAGE_TX = PAIR ? 2u * STAGE_BYTES : STAGE_BYTES;  // counted on the leader
   static constexpr uint32_t TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
 };
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct __align__(1024) GemmSmem {
-  uint8_t a[GemmCfg<BN>::STAGES][A_BYTES];
-  uint8_t b[GemmCfg<BN>::STAGES][GemmCfg<BN>::B_BYTES];
-  uint64_t full[GemmCfg<BN>::STAGES];
-  uint64_t empty[GemmCfg<BN>::STAGES];
+  uint8_t a[GemmCfg<BN, PAIR>::STAGES][A_BYTES];
+  uint8_t b[GemmCfg<BN, PAIR>::STAGES][GemmCfg<BN, PAIR>::B_BYTES];
+  uint64_t full[GemmCfg<BN, PAIR>::STAGES];
+  uint64_t empty[GemmCfg<BN, PAIR>::STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
@@ -87,20 +92,26 @@ __device__ __forceinline__ void tile_coords(int tile, const LinearArgs& a, int& 
   }
 }
 
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     linear_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const LinearArgs args) {
-  using Cfg = GemmCfg<BN>;
+  static_assert(!(SWAP && PAIR), "the swapped (skinny) form runs on single CTAs");
+  using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  GemmSmem<BN>& S = *reinterpret_cast<GemmSmem<BN>*>(smem_raw + pad);
+  GemmSmem<BN, PAIR>& S = *reinterpret_cast<GemmSmem<BN, PAIR>*>(smem_raw + pad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nk = (args.K + BK - 1) / BK;
   const int n_tiles = args.tiles_a * args.tiles_b;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 = leader (issues the pair's MMAs)
+  const int cid = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ncl = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // first row of the 128-row A block this CTA owns in tile-row ta
+  auto a_row0 = [&](int ta) { return PAIR ? ta * 2 * BM + static_cast<int>(rank) * BM : ta * BM; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -109,21 +120,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S.tfull[b], 1);
-      mbar_init(&S.tempty[b], EPI_WARPS);
+      mbar_init(&S.tempty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);  // a pair's leader hears both epilogues
     }
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&S.tmem_base, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&S.tmem_base, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&S.tmem_base, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair's barriers must be initialised in both CTAs before either signals the other
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort_flag = &S.abort_flag;
+  auto abort_all = [&]() {
+    *abort_flag = 1;
+    atomicOr(args.err, kErrWaitTimeout);
+    if constexpr (PAIR) st_shared_cluster_u32(mapa_shared(smem_u32(&S.abort_flag), rank ^ 1u), 1u);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -135,28 +158,43 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued_parity[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      for (int tile = cid; ok && tile < n_tiles; tile += ncl) {
         int ta, tb;
         tile_coords(tile, args, ta, tb);
+        const int ar = a_row0(ta);
         for (int kc = 0; kc < nk; ++kc) {
           if (!mbar_wait(&S.empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_BYTES);
+          // A: this CTA's rows (conv: row -1 of the first tile is outside the
+          // tensor and TMA fills it with zeros)
+          int ax = kc * BK, ay = ar;
           if (args.taps > 1) {
-            // row -1 of the first tile is outside the tensor: TMA fills it with zeros
             const int tap = kc / args.nk_tap;
-            tma_load_2d(&tmA, &S.full[stage], S.a[stage], (kc - tap * args.nk_tap) * BK, ta * BM + tap - 1);
-          } else {
-            tma_load_2d(&tmA, &S.full[stage], S.a[stage], kc * BK, ta * BM);
+            ax = (kc - tap * args.nk_tap) * BK;
+            ay = ar + tap - 1;
           }
-          if (args.mode == 1) {
-            // gate rows and the matching up rows side by side in one tile
-            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * (BN / 2));
-            tma_load_2d(&tmB, &S.full[stage], S.b[stage] + (BN / 2) * BK * 2, kc * BK, args.F + tb * (BN / 2));
+          if constexpr (PAIR) {
+            // both CTAs' copies complete on the leader's full barrier, which
+            // alone posts the expected bytes; B: this CTA's half of the tile
+            // (SwiGLU: the leader the gate rows, the follower the up rows)
+            if (rank == 0) mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_TX);
+            const uint32_t fb = mapa_shared(smem_u32(&S.full[stage]), 0);
+            tma_load_2d_pair(&tmA, fb, S.a[stage], ax, ay);
+            const int by = args.mode == 1 ? (rank == 0 ? 0 : args.F) + tb * (BN / 2)
+                                          : tb * BN + static_cast<int>(rank) * (BN / 2);
+            tma_load_2d_pair(&tmB, fb, S.b[stage], kc * BK, by);
           } else {
-            tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * BN);
+            mbar_arrive_expect_tx(&S.full[stage], Cfg::STAGE_TX);
+            tma_load_2d(&tmA, &S.full[stage], S.a[stage], ax, ay);
+            if (args.mode == 1) {
+              // gate rows and the matching up rows side by side in one tile
+              tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * (BN / 2));
+              tma_load_2d(&tmB, &S.full[stage], S.b[stage] + (BN / 2) * BK * 2, kc * BK, args.F + tb * (BN / 2));
+            } else {
+              tma_load_2d(&tmB, &S.full[stage], S.b[stage], kc * BK, tb * BN);
+            }
           }
           issued[stage] = true;
           issued_parity[stage] = phase;
@@ -167,20 +205,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) {
-        *abort_flag = 1;
-        atomicOr(args.err, kErrWaitTimeout);
-        for (int s = 0; s < STAGES; ++s)
-          if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+        abort_all();
+        // let this thread's copies land before the CTA exits (a pair's
+        // follower cannot observe the leader's barrier: it waits 20 us)
+        if (!PAIR || rank == 0) {
+          for (int s = 0; s < STAGES; ++s)
+            if (issued[s]) mbar_wait(&S.full[s], issued_parity[s], nullptr);
+        } else {
+          __nanosleep(20000);
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      const uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      for (int tile = cid; ok && tile < n_tiles; tile += ncl) {
         const uint32_t b = acc_it & 1u;
         const uint32_t ap = (acc_it >> 1) & 1u;
         if (!mbar_wait(&S.tempty[b], ap ^ 1u, abort_flag)) {
@@ -199,23 +242,36 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b0 = smem_u32(S.b[stage]);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
-                       (kc | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              tc_mma_f16_pair(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                              (kc | k) != 0 ? 1u : 0u);
+            else
+              tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                         (kc | k) != 0 ? 1u : 0u);
           }
-          tc_commit(&S.empty[stage]);
+          // the stage is free again (in both CTAs of a pair)
+          if constexpr (PAIR)
+            tc_commit_pair(&S.empty[stage], 0x3);
+          else
+            tc_commit(&S.empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&S.tfull[b]);
+        if constexpr (PAIR)
+          tc_commit_pair(&S.tfull[b], 0x3);
+        else
+          tc_commit(&S.tfull[b]);
         ++acc_it;
       }
       if (!ok) {
-        *abort_flag = 1;
-        atomicOr(args.err, kErrWaitTimeout);
-        tc_commit(&S.drain);
+        abort_all();
+        if constexpr (PAIR)
+          tc_commit_pair(&S.drain, 0x1);
+        else
+          tc_commit(&S.drain);
         mbar_wait(&S.drain, 0, nullptr);
       }
     }
@@ -224,7 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int c0 = ((warp - 2) >> 2) * 16;  // first 16-column chunk of this warp; chunks step by 32
     uint32_t acc_it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    for (int tile = cid; tile < n_tiles; tile += ncl) {
       int ta, tb;
       tile_coords(tile, args, ta, tb);
       const uint32_t b = acc_it & 1u;
@@ -235,7 +291,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
-      const int arow = ta * BM + q * 32 + lane;  // row of the 128-row operand this thread owns
+      const int arow = a_row0(ta) + q * 32 + lane;  // row of the 128-row operand this thread owns
       if (!SWAP && args.mode == 1) {
         // SwiGLU (decoder.zig:205-210): y = bf16(bf16(silu(bf16(g))) * bf16(u))
         const int m = arow;
@@ -567,41 +623,159 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.tempty[b]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&S.tempty[b]), 0));  // the leader's barrier
+        else
+          mbar_arrive(&S.tempty[b]);
+      }
       ++acc_it;
     }
-    if (!ok) {
-      *abort_flag = 1;
-      atomicOr(args.err, kErrWaitTimeout);
-    }
+    if (!ok) abort_all();
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  // a pair's partner may still read this CTA's shared memory (the leader's
+  // MMAs) or arrive on its barriers until both are done
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
 }
 
-template <int BN, bool SWAP>
-cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const LinearArgs& a, int grid,
-                          cudaStream_t stream) {
-  constexpr size_t smem = sizeof(GemmSmem<BN>) + 1024;
-  // the shared-memory opt-in is per device: remember which devices have it
+template <int BN, bool SWAP, bool PAIR>
+constexpr size_t linear_smem_bytes() {
+  return sizeof(GemmSmem<BN, PAIR>) + 1024;
+}
+
+// Sets the dynamic shared-memory opt-in of one instantiation on the current
+// device (once per device).
+template <int BN, bool SWAP, bool PAIR>
+cudaError_t linear_prepare() {
   static unsigned long long attr_set = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 64 || !(attr_set & (1ull << dev))) {
-    e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    if (dev < 64) attr_set |= 1ull << dev;
+  if (dev < 64 && (attr_set & (1ull << dev))) return cudaSuccess;
+  e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(linear_smem_bytes<BN, SWAP, PAIR>()));
+  if (e == cudaSuccess && dev < 64) attr_set |= 1ull << dev;
+  return e;
+}
+
+cudaLaunchAttribute pair_cluster_attr() {
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 2;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  return at;
+}
+
+template <int BN, bool SWAP, bool PAIR>
+cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const LinearArgs& a, int grid,
+                          cudaStream_t stream) {
+  cudaError_t e = linear_prepare<BN, SWAP, PAIR>();
+  if (e != cudaSuccess) return e;
+  constexpr size_t smem = linear_smem_bytes<BN, SWAP, PAIR>();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1] = {pair_cluster_attr()};
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_bf16_kernel<BN, SWAP, PAIR>, tmA, tmB, a);
+  } else {
+    linear_bf16_kernel<BN, SWAP, PAIR><<<grid, THREADS, smem, stream>>>(tmA, tmB, a);
+    return cudaGetLastError();
   }
-  linear_bf16_kernel<BN, SWAP><<<grid, THREADS, smem, stream>>>(tmA, tmB, a);
-  return cudaGetLastError();
+}
+
+// How many 2-CTA clusters of the 256-wide pair kernel fit at once (cluster
+// placement can leave SMs idle); cached per device, 0 if none.
+int max_pairs_linear(int num_sms) {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] != 0) return cached[dev] > 0 ? cached[dev] : 0;
+  int n = 0;
+  if (linear_prepare<256, false, true>() == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (num_sms / 2));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = linear_smem_bytes<256, false, true>();
+    cudaLaunchAttribute at[1] = {pair_cluster_attr()};
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, linear_bf16_kernel<256, false, true>, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cached[dev] = n > 0 ? std::min(n, num_sms / 2) : -1;
+  return n > 0 ? cached[dev] : 0;
+}
+
+// Tile shape of a non-swapped GEMM with `rows` output rows and `cols` output
+// columns (mode 1: cols = F, each tile holding bn/2 gate and bn/2 up columns).
+// CTA pairs of 256-wide tiles when their tiles fill every pair; otherwise one
+// CTA per tile with the widest tile that still fills the SMs.
+struct GemmShape {
+  int bn;
+  bool pair;
+};
+GemmShape choose_shape(ncm_ctx* ctx, int64_t rows, int64_t cols, int mode) {
+  const int pairs = max_pairs_linear(ctx->num_sms);
+  const int64_t col_tiles_256 = mode == 1 ? cols / 128 : ceil_div(cols, 256);
+  if (pairs > 0 && ceil_div(rows, 2 * BM) * col_tiles_256 >= pairs) return {256, true};
+  const long long mt = ceil_div(rows, BM);
+  if (mode == 1 || mt * ceil_div(cols, 256) >= ctx->num_sms) return {256, false};
+  if (mt * ceil_div(cols, 128) >= ctx->num_sms) return {128, false};
+  return {64, false};
+}
+
+// Builds the tensor maps for shape `sh` (A: [a_rows, a_cols] with 128-row
+// boxes; B: [b_rows, k_cols] with boxes of the rows one CTA loads; a_cols =
+// k_cols except for the kernel-3 convolution, whose B holds three taps), fills
+// the tile counts of `a` (a.M output rows, a.N output columns) and launches.
+int launch_shape(ncm_ctx* ctx, const GemmShape& sh, const void* A, int64_t a_rows, int64_t a_cols, const void* B,
+                 int64_t b_rows, int64_t k_cols, LinearArgs& a, KernelId kid, cudaStream_t stream) {
+  const uint32_t b_box = (sh.pair || a.mode == 1) ? sh.bn / 2 : sh.bn;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap_bf16_2d(&tmA, A, a_rows, a_cols, BM) || !make_tmap_bf16_2d(&tmB, B, b_rows, k_cols, b_box))
+    return ncm_fail(NCM_EINVAL, "gemm: tensor map encoding failed (rows=%lld K=%lld N=%lld)", (long long)a.M,
+                    (long long)k_cols, (long long)a.N);
+  a.tiles_a = ceil_div(a.M, sh.pair ? 2 * BM : BM);
+  a.tiles_b = a.mode == 1 ? static_cast<int>(a.F / (sh.bn / 2)) : ceil_div(a.N, sh.bn);
+  // keep the smaller operand L2-resident: walk the tiles of the larger one slowly
+  const double a_bytes = double(a_rows) * a_cols * 2, b_bytes = double(b_rows) * k_cols * 2;
+  a.a_fast = a_bytes <= b_bytes ? 1 : 0;
+  const int tiles = a.tiles_a * a.tiles_b;
+  int grid;
+  if (sh.pair)
+    grid = 2 * std::min(tiles, max_pairs_linear(ctx->num_sms));
+  else
+    grid = std::min(tiles, ctx->num_sms);
+  cudaError_t e;
+  Launch _launch(ctx, kid, stream);
+  if (sh.pair) {
+    e = launch_linear<256, false, true>(tmA, tmB, a, grid, stream);
+  } else {
+    switch (sh.bn) {
+      case 256: e = launch_linear<256, false, false>(tmA, tmB, a, grid, stream); break;
+      case 128: e = launch_linear<128, false, false>(tmA, tmB, a, grid, stream); break;
+      default: e = launch_linear<64, false, false>(tmA, tmB, a, grid, stream); break;
+    }
+  }
+  if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  return NCM_OK;
 }
 
 }  // namespace
@@ -628,53 +802,25 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
   a.K = static_cast<int>(K);
   a.vec_ok = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0) &&
              ((reinterpret_cast<uintptr_t>(bias) & 15) == 0);
-  const bool swap = M <= 64;
+  if (M > 64)
+    return launch_shape(ctx, choose_shape(ctx, M, mode == 1 ? F : N, mode), x, M, K, w, N, K, a, KID_LINEAR, stream);
+  // Skinny problems (decode-time GEMV shapes) run swapped: W is the 128-row
+  // MMA operand and the tokens the narrow side
+  const int bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
   CUtensorMap tmA, tmB;
-  int bn;
-  if (swap) {
-    bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
-    if (!make_tmap_bf16_2d(&tmA, w, N, K, BM) || !make_tmap_bf16_2d(&tmB, x, M, K, bn))
-      return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
-                      (long long)K, (long long)N);
-    a.tiles_a = ceil_div(N, BM);
-    a.tiles_b = ceil_div(M, bn);
-    a.a_fast = 1;
-  } else {
-    const long long mt = ceil_div(M, BM);
-    const int sms = ctx->num_sms;
-    if (mode == 1 || mt * ceil_div(N, 256) >= sms)
-      bn = 256;
-    else if (mt * ceil_div(N, 128) >= sms)
-      bn = 128;
-    else
-      bn = 64;
-    // SwiGLU tiles are two 128-row boxes (gate rows, up rows) of W
-    if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, mode == 1 ? bn / 2 : bn))
-      return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
-                      (long long)K, (long long)N);
-    a.tiles_a = static_cast<int>(mt);
-    a.tiles_b = mode == 1 ? static_cast<int>(F / (bn / 2)) : ceil_div(N, bn);
-    // Keep the smaller operand L2-resident: walk the tiles of the larger one
-    // slowly, so concurrently running CTAs share its tile.
-    const double a_bytes = double(M) * K * 2, b_bytes = double(N) * K * 2;
-    a.a_fast = a_bytes <= b_bytes ? 1 : 0;
-  }
-  const int tiles = a.tiles_a * a.tiles_b;
-  const int grid = std::min(tiles, ctx->num_sms);
+  if (!make_tmap_bf16_2d(&tmA, w, N, K, BM) || !make_tmap_bf16_2d(&tmB, x, M, K, bn))
+    return ncm_fail(NCM_EINVAL, "linear: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
+                    (long long)K, (long long)N);
+  a.tiles_a = ceil_div(N, BM);
+  a.tiles_b = ceil_div(M, bn);
+  a.a_fast = 1;
+  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
   cudaError_t e;
   Launch _launch(ctx, KID_LINEAR, stream);
-  if (swap) {
-    switch (bn) {
-      case 16: e = launch_linear<16, true>(tmA, tmB, a, grid, stream); break;
-      case 32: e = launch_linear<32, true>(tmA, tmB, a, grid, stream); break;
-      default: e = launch_linear<64, true>(tmA, tmB, a, grid, stream); break;
-    }
-  } else {
-    switch (bn) {
-      case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
-      case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
-      default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
-    }
+  switch (bn) {
+    case 16: e = launch_linear<16, true, false>(tmA, tmB, a, grid, stream); break;
+    case 32: e = launch_linear<32, true, false>(tmA, tmB, a, grid, stream); break;
+    default: e = launch_linear<64, true, false>(tmA, tmB, a, grid, stream); break;
   }
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
   return NCM_OK;
@@ -698,25 +844,8 @@ int linear_qkv_rope(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const ui
   a.rope_sin = sin_bf;
   a.vt = vt;
   a.voff = static_cast<int>(voff);
-  const long long mt = ceil_div(M, BM);
-  const int bn = (mt * ceil_div(N, 256) >= ctx->num_sms) ? 256 : (mt * ceil_div(N, 128) >= ctx->num_sms ? 128 : 64);
-  CUtensorMap tmA, tmB;
-  if (!make_tmap_bf16_2d(&tmA, x, M, K, BM) || !make_tmap_bf16_2d(&tmB, w, N, K, bn))
-    return ncm_fail(NCM_EINVAL, "qkv projection: tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
-                    (long long)K, (long long)N);
-  a.tiles_a = static_cast<int>(mt);
-  a.tiles_b = ceil_div(N, bn);
-  a.a_fast = double(M) <= double(N) ? 1 : 0;
-  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
-  cudaError_t e;
-  Launch _launch(ctx, KID_LINEAR, stream);
-  switch (bn) {
-    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
-    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
-    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
-  }
-  if (e != cudaSuccess) return ncm_set_cuda_error(e);
-  return NCM_OK;
+  a.vec_ok = 1;
+  return launch_shape(ctx, choose_shape(ctx, M, N, 5), x, M, K, w, N, K, a, KID_LINEAR, stream);
 }
 
 int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
@@ -735,31 +864,7 @@ int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codeb
   a.head_scal = scal;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   a.vec_ok = K % 4 == 0 && al(logits) && al(esq) && al(bias);
-  const long long mt = ceil_div(T, BM);
-  int bn;
-  if (mt * ceil_div(K, 256) >= ctx->num_sms)
-    bn = 256;
-  else if (mt * ceil_div(K, 128) >= ctx->num_sms)
-    bn = 128;
-  else
-    bn = 64;
-  CUtensorMap tmA, tmB;
-  if (!make_tmap_bf16_2d(&tmA, z, T, d, BM) || !make_tmap_bf16_2d(&tmB, codebook, K, d, bn))
-    return ncm_fail(NCM_EINVAL, "tied head: tensor map encoding failed (T=%lld d=%lld K=%lld)", (long long)T,
-                    (long long)d, (long long)K);
-  a.tiles_a = static_cast<int>(mt);
-  a.tiles_b = ceil_div(K, bn);
-  a.a_fast = double(T) <= double(K) ? 1 : 0;
-  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
-  cudaError_t e;
-  Launch _launch(ctx, KID_LINEAR, stream);
-  switch (bn) {
-    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
-    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
-    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
-  }
-  if (e != cudaSuccess) return ncm_set_cuda_error(e);
-  return NCM_OK;
+  return launch_shape(ctx, choose_shape(ctx, T, K, 4), z, T, d, codebook, K, d, a, KID_LINEAR, stream);
 }
 
 int conv3_gemm(ncm_ctx* ctx, const uint16_t* a_pad, const uint16_t* w_pack, const SegMap& map, int64_t dp,
@@ -780,32 +885,8 @@ int conv3_gemm(ncm_ctx* ctx, const uint16_t* a_pad, const uint16_t* w_pack, cons
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   a.vec_ok = width % 4 == 0 && al(ep.x_f32) && al(ep.x_bf16) && al(ep.out_f32) && al(ep.out_bf16) &&
              al(ep.resid) && al(ep.acc_f32) && al(ep.bias);
-  const long long mt = ceil_div(Mp, BM);
-  int bn;
-  if (mt * ceil_div(width, 256) >= ctx->num_sms)
-    bn = 256;
-  else if (mt * ceil_div(width, 128) >= ctx->num_sms)
-    bn = 128;
-  else
-    bn = 64;
-  CUtensorMap tmA, tmB;
-  if (!make_tmap_bf16_2d(&tmA, a_pad, Mp, dp, BM) || !make_tmap_bf16_2d(&tmB, w_pack, width, 3 * dp, bn))
-    return ncm_fail(NCM_EINVAL, "conv: tensor map encoding failed (rows=%lld width=%lld)", (long long)Mp,
-                    (long long)width);
-  a.tiles_a = static_cast<int>(mt);
-  a.tiles_b = ceil_div(width, bn);
-  const double a_bytes = double(Mp) * dp * 2, b_bytes = double(width) * 3 * dp * 2;
-  a.a_fast = a_bytes <= b_bytes ? 1 : 0;
-  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
-  cudaError_t e;
-  Launch _launch(ctx, KID_CONV, stream);
-  switch (bn) {
-    case 256: e = launch_linear<256, false>(tmA, tmB, a, grid, stream); break;
-    case 128: e = launch_linear<128, false>(tmA, tmB, a, grid, stream); break;
-    default: e = launch_linear<64, false>(tmA, tmB, a, grid, stream); break;
-  }
-  if (e != cudaSuccess) return ncm_set_cuda_error(e);
-  return NCM_OK;
+  return launch_shape(ctx, choose_shape(ctx, Mp, width, 3), a_pad, Mp, dp, w_pack, width, 3 * dp, a, KID_CONV,
+                      stream);
 }
 
 }  // namespace ncm
