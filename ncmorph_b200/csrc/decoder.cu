@@ -19,7 +19,11 @@ namespace {
 
 // ---------------------------------------------------------------- RMSNorm
 // One warp per row. y = bf16(bf16(x * inv) * bf16(w)) (+ bias, rounded),
-// inv = 1 / sqrt(mean(x^2) + eps) in f32.
+// inv = 1 / sqrt(mean(x^2) + eps) in f32. NCH > 0: the row (at most NCH * 256
+// columns) is read once into registers; NCH = 0: any width, read twice.
+// Rounding is the hardware round-to-nearest-even (the reference rule for
+// every non-NaN value).
+template <int NCH>
 __global__ void __launch_bounds__(256) rms_norm_bf16_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ w,
                                                             const uint16_t* __restrict__ bias,
@@ -29,23 +33,35 @@ __global__ void __launch_bounds__(256) rms_norm_bf16_kernel(const uint16_t* __re
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const uint16_t* xr = x + static_cast<size_t>(row) * width;
+  constexpr int REG = NCH > 0 ? NCH : 1;
+  uint4 keep[REG];
   float ss = 0.f;
-  for (int i = lane * 8; i < width; i += 256) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+  auto add_sq = [&ss](const uint4& v) {
     const uint32_t p[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float a = bf16lo(p[e]), b = bf16hi(p[e]);
-      ss += a * a + b * b;
+      ss = fmaf(a, a, ss);
+      ss = fmaf(b, b, ss);
     }
+  };
+  if constexpr (NCH > 0) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = c * 256 + lane * 8;
+      keep[c] = i < width ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) add_sq(keep[c]);
+  } else {
+    for (int i = lane * 8; i < width; i += 256) add_sq(*reinterpret_cast<const uint4*>(xr + i));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float ms = ss / static_cast<float>(width);
   const float inv = 1.0f / sqrtf(ms + eps);
   uint16_t* yr = y + static_cast<size_t>(row) * width;
-  for (int i = lane * 8; i < width; i += 256) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+  auto emit = [&](int i, const uint4& v) {
     const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + i));
     uint4 bv = make_uint4(0, 0, 0, 0);
     if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + i));
@@ -55,17 +71,23 @@ __global__ void __launch_bounds__(256) rms_norm_bf16_kernel(const uint16_t* __re
     uint32_t o4[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float n0 = bf16_to_f32(f32_to_bf16(bf16lo(p[e]) * inv));
-      const float n1 = bf16_to_f32(f32_to_bf16(bf16hi(p[e]) * inv));
-      float y0 = bf16_to_f32(f32_to_bf16(n0 * bf16lo(q[e])));
-      float y1 = bf16_to_f32(f32_to_bf16(n1 * bf16hi(q[e])));
-      if (bias != nullptr) {
-        y0 += bf16lo(r[e]);
-        y1 += bf16hi(r[e]);
-      }
-      o4[e] = pack_bf16x2(y0, y1);
+      const uint32_t n = cvt_bf16x2(bf16lo(p[e]) * inv, bf16hi(p[e]) * inv);
+      const uint32_t m = cvt_bf16x2(bf16lo(n) * bf16lo(q[e]), bf16hi(n) * bf16hi(q[e]));
+      if (bias != nullptr)
+        o4[e] = cvt_bf16x2(bf16lo(m) + bf16lo(r[e]), bf16hi(m) + bf16hi(r[e]));
+      else
+        o4[e] = m;
     }
     *reinterpret_cast<uint4*>(yr + i) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  };
+  if constexpr (NCH > 0) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = c * 256 + lane * 8;
+      if (i < width) emit(i, keep[c]);
+    }
+  } else {
+    for (int i = lane * 8; i < width; i += 256) emit(i, *reinterpret_cast<const uint4*>(xr + i));
   }
 }
 
@@ -198,7 +220,15 @@ inline unsigned blocks_for(long long n, long long per_block) { return static_cas
 
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* y, int rows,
                                  int width, float eps, cudaStream_t st) {
-  rms_norm_bf16_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(x, w, b, y, rows, width, eps);
+  const int blocks = (rows + 7) / 8;
+  if (width <= 1024)
+    rms_norm_bf16_kernel<4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+  else if (width <= 2048)
+    rms_norm_bf16_kernel<8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+  else if (width <= 4096)
+    rms_norm_bf16_kernel<16><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+  else
+    rms_norm_bf16_kernel<0><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
   return cudaGetLastError();
 }
 
