@@ -249,6 +249,40 @@ NCM_API int ncm_multiscale_decode(ncm_ctx_t* ctx, const ncm_tokenizer_config_t* 
                                   const uint16_t* codebooks, const uint16_t* phi_weight, const float* phi_bias,
                                   uint16_t* recon, ncm_stream_t stream);
 
+/* ---------------------------- quantiser pieces around the RVQ levels */
+
+/* Pre-quantisation GroupNorm, affine=False (research/reference/
+ * vq_forward_semantics.md:43-49): x, y [batch, T, C] f32 (channels
+ * contiguous); per sample and group of C/groups channels, statistics over all
+ * T positions; y = (x - mean) / sqrt(var + eps), biased variance. */
+NCM_API int ncm_group_norm(ncm_ctx_t* ctx, const float* x, float* y, int64_t batch, int64_t T, int64_t C,
+                           int32_t groups, float eps, ncm_stream_t stream);
+
+/* One stage of the learned level-0 cascade (vq_forward_semantics.md:127-139):
+ * down: Conv1d(C, C, kernel 4, stride 4) over time, x [batch, L, C] ->
+ * y [batch, L/4, C]; weight [C, C, 4] bf16 (Conv1d layout), bias [C] or NULL.
+ * up: ConvTranspose1d(C, C, kernel 4, stride 4), x [batch, L, C] ->
+ * y [batch, 4L, C]; weight [C_in, C_out, 4] bf16 (ConvTranspose1d layout).
+ * Both run as one tcgen05 GEMM (bf16 operands, f32 accumulation, bf16 out). */
+NCM_API int ncm_conv_down4(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* weight, const uint16_t* bias,
+                           uint16_t* y, int64_t batch, int64_t L, int64_t C, ncm_stream_t stream);
+NCM_API int ncm_conv_up4(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* weight, const uint16_t* bias,
+                         uint16_t* y, int64_t batch, int64_t L, int64_t C, ncm_stream_t stream);
+
+/* Codebook EMA of one level (vq_forward_semantics.md:141-173), in two steps
+ * so a multi-GPU caller can sum the statistics across ranks in between:
+ * stats: counts[k] = rows whose code is k, sums[k, :] = sum of those rows of
+ *   u [N, D] f32 (in increasing row order: the same result on every run);
+ * update: N <- decay N + (1 - decay) counts; n = sum N;
+ *   N_hat = (N + eps) / (n + K eps) * n; m <- decay m + (1 - decay) sums;
+ *   e = m / N_hat into codebook_f32 and/or codebook_bf16 (either NULL).
+ * ema_count [K] and ema_sum [K, D] f32 are the persistent EMA buffers. */
+NCM_API int ncm_ema_code_stats(ncm_ctx_t* ctx, const float* u, const int32_t* codes, float* counts, float* sums,
+                               int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+NCM_API int ncm_ema_update(ncm_ctx_t* ctx, const float* counts, const float* sums, float* ema_count, float* ema_sum,
+                           float* codebook_f32, uint16_t* codebook_bf16, int64_t K, int64_t D, float decay,
+                           float eps, ncm_stream_t stream);
+
 /* ------------------------------------------------- checkpoint loading */
 
 /* safetensors element types the loader reads (packages/safetensors/root.zig:34-54) */

@@ -133,6 +133,11 @@ SIGNATURES: dict[str, list] = {
     "ncm_rvq_encode_sharded": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_load_tensor_bf16": [c_vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64, c_i32, c_vp, c_vp],
     "ncm_qkv_projection_rope": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_i32, c_vp],
+    "ncm_group_norm": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, ctypes.c_float, c_vp],
+    "ncm_conv_down4": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_conv_up4": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_ema_code_stats": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_ema_update": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, ctypes.c_float, c_vp],
     "ncm_upsample": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp],
     "ncm_conv1d_k3": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, ctypes.c_float, ctypes.c_float,
                       c_vp],

@@ -34,12 +34,10 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
 constexpr int UPD_WARPS = 8;  // residual-update warps (rows split evenly among them)
 constexpr int UPD_ROWS = BM / UPD_WARPS;
 constexpr int THREADS = 64 + 128 + 32 * UPD_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
 // Stage layout of one CTA. PAIR: the CTA holds half of each 256-code tile

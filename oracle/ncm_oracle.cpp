@@ -859,4 +859,85 @@ void orc_tied_head(const float* z, const uint16_t* cb, const float* esq_in, cons
   }
 }
 
+// Pre-quantisation GroupNorm, affine=False: x, y [B, T, C]; statistics per
+// (sample, group) over T x C/G values in f64, biased variance.
+void orc_group_norm(const float* x, float* y, size_t B, size_t T, size_t C, size_t G, float eps) {
+  const size_t cg = C / G;
+  for (size_t b = 0; b < B; ++b)
+    for (size_t g = 0; g < G; ++g) {
+      double s = 0.0, ss = 0.0;
+      for (size_t t = 0; t < T; ++t)
+        for (size_t c = 0; c < cg; ++c) {
+          const double v = x[(b * T + t) * C + g * cg + c];
+          s += v;
+          ss += v * v;
+        }
+      const double n = static_cast<double>(T * cg);
+      const double mean = s / n, var = std::max(ss / n - mean * mean, 0.0);
+      const float m = static_cast<float>(mean), r = static_cast<float>(1.0 / std::sqrt(var + eps));
+      for (size_t t = 0; t < T; ++t)
+        for (size_t c = 0; c < cg; ++c) {
+          const size_t o = (b * T + t) * C + g * cg + c;
+          y[o] = (x[o] - m) * r;
+        }
+    }
+}
+
+// Conv1d(C, C, 4, stride 4) on x [B, L, C] (w [C, C, 4], b [C] or null) ->
+// y [B, L/4, C]; f64 sums of the given (bf16-valued) operands, rounded to f32.
+void orc_conv_down4(const float* x, const float* w, const float* b, float* y, size_t B, size_t L, size_t C) {
+  const size_t Lo = L / 4;
+  for (size_t bb = 0; bb < B; ++bb)
+    for (size_t j = 0; j < Lo; ++j)
+      for (size_t o = 0; o < C; ++o) {
+        double acc = b != nullptr ? b[o] : 0.0;
+        for (size_t t = 0; t < 4; ++t)
+          for (size_t i = 0; i < C; ++i)
+            acc += static_cast<double>(w[(o * C + i) * 4 + t]) * x[(bb * L + 4 * j + t) * C + i];
+        y[(bb * Lo + j) * C + o] = static_cast<float>(acc);
+      }
+}
+
+// ConvTranspose1d(C, C, 4, stride 4) on x [B, L, C] (w [C_in, C_out, 4]) -> y [B, 4L, C].
+void orc_conv_up4(const float* x, const float* w, const float* b, float* y, size_t B, size_t L, size_t C) {
+  for (size_t bb = 0; bb < B; ++bb)
+    for (size_t j = 0; j < L; ++j)
+      for (size_t t = 0; t < 4; ++t)
+        for (size_t o = 0; o < C; ++o) {
+          double acc = b != nullptr ? b[o] : 0.0;
+          for (size_t i = 0; i < C; ++i)
+            acc += static_cast<double>(w[(i * C + o) * 4 + t]) * x[(bb * L + j) * C + i];
+          y[(bb * 4 * L + 4 * j + t) * C + o] = static_cast<float>(acc);
+        }
+}
+
+// Codebook EMA of one level (models/quant.py:485-500 as restated in
+// vq_forward_semantics.md:141-173): counts and row sums per code (rows in
+// increasing order, f32), then the EMA update in f32 with the count total in f64.
+void orc_ema(const float* u, const int32_t* codes, size_t N, size_t D, size_t K, float* ema_count, float* ema_sum,
+             float* codebook, float decay, float eps, float* counts_out, float* sums_out) {
+  std::vector<float> cnt(K, 0.f), sum(K * D, 0.f);
+  for (size_t n = 0; n < N; ++n) {
+    const size_t k = static_cast<size_t>(codes[n]);
+    cnt[k] += 1.f;
+    for (size_t d = 0; d < D; ++d) sum[k * D + d] += u[n * D + d];
+  }
+  double tot = 0.0;
+  for (size_t k = 0; k < K; ++k) {
+    ema_count[k] = decay * ema_count[k] + (1.f - decay) * cnt[k];
+    tot += ema_count[k];
+  }
+  const float nt = static_cast<float>(tot);
+  for (size_t k = 0; k < K; ++k) {
+    const float nhat = (ema_count[k] + eps) / (nt + static_cast<float>(K) * eps) * nt;
+    for (size_t d = 0; d < D; ++d) {
+      const size_t i = k * D + d;
+      ema_sum[i] = decay * ema_sum[i] + (1.f - decay) * sum[i];
+      codebook[i] = ema_sum[i] / nhat;
+    }
+  }
+  if (counts_out) std::memcpy(counts_out, cnt.data(), sizeof(float) * K);
+  if (sums_out) std::memcpy(sums_out, sum.data(), sizeof(float) * K * D);
+}
+
 }  // extern "C"

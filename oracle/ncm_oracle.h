@@ -99,6 +99,11 @@ void orc_rvq_level(float* resid, const uint16_t* cb, const float* sqnorm, const 
 void orc_rvq_decode(const int32_t* codes, const uint16_t* cbs, size_t L, float* recon_f32, size_t N, size_t D,
                     size_t K);
 void orc_pool_avg(const float* x, float* y, size_t B, size_t T, size_t D, size_t f);
+void orc_group_norm(const float* x, float* y, size_t B, size_t T, size_t C, size_t G, float eps);
+void orc_conv_down4(const float* x, const float* w, const float* b, float* y, size_t B, size_t L, size_t C);
+void orc_conv_up4(const float* x, const float* w, const float* b, float* y, size_t B, size_t L, size_t C);
+void orc_ema(const float* u, const int32_t* codes, size_t N, size_t D, size_t K, float* ema_count, float* ema_sum,
+             float* codebook, float decay, float eps, float* counts_out, float* sums_out);
 void orc_tied_head(const float* z, const uint16_t* cb, const float* esq_in, const float* bias, float log_inv_T,
                    float* logits, int32_t* codes, float* gap, size_t T, size_t d, size_t K);
 void orc_upsample(const float* q, float* out, size_t B, size_t Tq, size_t T, size_t D, int mode);

@@ -96,6 +96,11 @@ def lib() -> ctypes.CDLL:
         "orc_scale_update": ([i32p, u16p, sz, f32p, f32p, sz, sz, sz, sz, sz], None),
         "orc_tied_head": ([f32p, u16p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_void_p, sz, sz, sz], None),
+        "orc_group_norm": ([f32p, f32p, sz, sz, sz, sz, ctypes.c_float], None),
+        "orc_conv_down4": ([f32p, f32p, ctypes.c_void_p, f32p, sz, sz, sz], None),
+        "orc_conv_up4": ([f32p, f32p, ctypes.c_void_p, f32p, sz, sz, sz], None),
+        "orc_ema": ([f32p, i32p, sz, sz, sz, f32p, f32p, f32p, ctypes.c_float, ctypes.c_float, ctypes.c_void_p,
+                     ctypes.c_void_p], None),
         "orc_upsample": ([f32p, f32p, sz, sz, sz, sz, ctypes.c_int], None),
         "orc_conv1d_k3": ([f32p, ctypes.c_void_p, f32p, ctypes.c_void_p, f32p, sz, sz, ctypes.c_void_p, sz,
                            ctypes.c_float, ctypes.c_float], None),
@@ -352,6 +357,46 @@ def tied_head(z, cb_bits, log_inv_T=0.0, bias=None, esq=None, want_logits=True):
     gap = np.empty(T, np.float32)
     lib().orc_tied_head(z, cb_bits, _ptr(esq), _ptr(bias), log_inv_T, _ptr(logits), _ptr(codes), _ptr(gap), T, d, K)
     return logits, codes, gap
+
+
+def group_norm(x, groups, eps=1e-5):
+    x = _c(x, np.float32)
+    B, T, C = x.shape
+    y = np.empty_like(x)
+    lib().orc_group_norm(x, y, B, T, C, groups, eps)
+    return y
+
+
+def conv_down4(x, w, b=None):
+    """Conv1d(C, C, 4, stride 4) over axis 1 of x [B, L, C]; w [C, C, 4]."""
+    x = _c(x, np.float32)
+    B, L, C = x.shape
+    y = np.empty((B, L // 4, C), np.float32)
+    lib().orc_conv_down4(x, _c(w, np.float32), _ptr(None if b is None else _c(b, np.float32)), y, B, L, C)
+    return y
+
+
+def conv_up4(x, w, b=None):
+    """ConvTranspose1d(C, C, 4, stride 4) over axis 1 of x [B, L, C]; w [C_in, C_out, 4]."""
+    x = _c(x, np.float32)
+    B, L, C = x.shape
+    y = np.empty((B, 4 * L, C), np.float32)
+    lib().orc_conv_up4(x, _c(w, np.float32), _ptr(None if b is None else _c(b, np.float32)), y, B, L, C)
+    return y
+
+
+def ema(u, codes, ema_count, ema_sum, decay, eps):
+    """One EMA step; returns (ema_count, ema_sum, codebook, counts, sums) as new arrays."""
+    u = _c(u, np.float32)
+    N, D = u.shape
+    K = ema_count.shape[0]
+    cnt = _c(ema_count, np.float32).copy()
+    sm = _c(ema_sum, np.float32).copy()
+    cb = np.empty((K, D), np.float32)
+    counts = np.empty(K, np.float32)
+    sums = np.empty((K, D), np.float32)
+    lib().orc_ema(u, _c(codes, np.int32), N, D, K, cnt, sm, cb, decay, eps, _ptr(counts), _ptr(sums))
+    return cnt, sm, cb, counts, sums
 
 
 def upsample(q: np.ndarray, T: int, mode: str = "linear") -> np.ndarray:

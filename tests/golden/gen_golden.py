@@ -13,6 +13,9 @@ Outputs
                    (the quantiser's U_i, vq_forward_semantics.md:82)
   conv1d_k3.npz    torch F.conv1d(kernel 3, padding 1) in float64 on seeded
                    inputs (the Phi / post-upsample convolution)
+  level0.npz       torch F.group_norm (affine=False), F.conv1d(kernel 4,
+                   stride 4) and F.conv_transpose1d(kernel 4, stride 4) in
+                   float64 (pre-quant GroupNorm and the level-0 cascade stage)
 """
 from __future__ import annotations
 
@@ -81,6 +84,24 @@ def conv1d_k3() -> None:
     np.savez_compressed(HERE / "conv1d_k3.npz", **out)
 
 
+def level0() -> None:
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(777)
+    out = {}
+    x = torch.randn(2, 32, 24, generator=g, dtype=torch.float32)
+    out["gn_x"] = x.numpy()
+    out["gn_y"] = F.group_norm(x.transpose(1, 2).double(), 8, eps=1e-5).transpose(1, 2).contiguous().numpy()
+    w = torch.randn(24, 24, 4, generator=g, dtype=torch.float32) * 0.1
+    b = torch.randn(24, generator=g, dtype=torch.float32)
+    out["conv_x"], out["conv_w"], out["conv_b"] = x.numpy(), w.numpy(), b.numpy()
+    xt = x.transpose(1, 2).double()
+    out["down_y"] = F.conv1d(xt, w.double(), b.double(), stride=4).transpose(1, 2).contiguous().numpy()
+    out["up_y"] = F.conv_transpose1d(xt, w.double(), b.double(), stride=4).transpose(1, 2).contiguous().numpy()
+    np.savez_compressed(HERE / "level0.npz", **out)
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         raise SystemExit("usage: python tests/golden/gen_golden.py <path-to-ncmorph-checkout>")
@@ -88,4 +109,5 @@ if __name__ == "__main__":
     pool_area()
     upsample()
     conv1d_k3()
+    level0()
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".txt", ".npz")))

@@ -264,3 +264,36 @@ def test_scale_update_ex_nearest_without_phi_is_scale_update(orc):
     orc.scale_update(codes, cbs, r1, a1, B, T, f)
     orc.scale_update_ex(codes, cbs, r2, a2, B, T, f, mode="nearest")
     assert np.array_equal(r1, r2) and np.array_equal(a1, a2)
+
+
+def test_group_norm_and_stride4_convs_match_torch(orc):
+    """Pre-quant GroupNorm (affine=False) and the level-0 cascade's stride-4
+    Conv1d / ConvTranspose1d against committed float64 torch outputs."""
+    z = _golden_npz("level0.npz")
+    assert np.abs(orc.group_norm(z["gn_x"], 8) - z["gn_y"]).max() < 1e-5
+    x, w, b = z["conv_x"], z["conv_w"], z["conv_b"]
+    scale = np.abs(x).max() * np.abs(w).sum(axis=(1, 2)).max() + np.abs(b).max()
+    assert np.abs(orc.conv_down4(x, w, b) - z["down_y"]).max() <= 1e-6 * scale
+    assert np.abs(orc.conv_up4(x, w, b) - z["up_y"]).max() <= 1e-6 * scale
+
+
+def test_ema_matches_the_spec_equations(orc):
+    """One EMA step restated with numpy from vq_forward_semantics.md:141-173."""
+    rng = np.random.default_rng(9)
+    N, D, K, decay, eps = 500, 16, 40, 0.99, 1e-5
+    u = rng.standard_normal((N, D)).astype(np.float32)
+    codes = rng.integers(0, K, N).astype(np.int32)
+    cnt0 = rng.random(K).astype(np.float32) * 3
+    m0 = rng.standard_normal((K, D)).astype(np.float32)
+    cnt, m, e, counts, sums = orc.ema(u, codes, cnt0, m0, decay, eps)
+    n_k = np.bincount(codes, minlength=K).astype(np.float64)
+    s_k = np.zeros((K, D))
+    np.add.at(s_k, codes, u.astype(np.float64))
+    N_k = decay * cnt0.astype(np.float64) + (1 - decay) * n_k
+    n = N_k.sum()
+    N_hat = (N_k + eps) / (n + K * eps) * n
+    m_k = decay * m0.astype(np.float64) + (1 - decay) * s_k
+    assert np.array_equal(counts, n_k.astype(np.float32))
+    assert np.allclose(sums, s_k, atol=1e-4)
+    assert np.allclose(cnt, N_k, rtol=1e-6)
+    assert np.allclose(e, m_k / N_hat[:, None], rtol=1e-5, atol=1e-6)
