@@ -7,18 +7,21 @@
 //                         reading its whole S row from TMEM; P (bf16) into a
 //                         128-byte-swizzled smem tile, the A operand of P.V
 //   O_i += P_i . V        tcgen05.mma M=128 N=64 K=128, accumulated in TMEM
-// The MMA warp interleaves the two tiles (P.V and the next S of one run while
-// the other group computes its softmax). Key tiles that the mask removes
-// entirely are never loaded, and CTAs launch heaviest first (late query
-// tiles see the most keys). K tiles come straight from the fused QKV rows by
+// A group's S buffer is released (s_free) as soon as its softmax threads hold
+// the scores in registers, so the MMA warp issues the next tile's S for both
+// groups while their exponentials run, then each group's P.V when its P is
+// written (p_full); a softmax pass therefore rarely waits for its S. Key tiles
+// that the mask removes entirely are never loaded, and CTAs launch heaviest
+// first (late query tiles see the most keys). K tiles come straight from the fused QKV rows by
 // TMA; V is read transposed ([kv_head*64 + d][t]) so both MMAs take K-major
 // operands.
 //
-// Softmax in the log2 domain with a lagging reference maximum: after a row's
-// first tile, a tile runs in one pass against the running reference (p may
-// exceed 1; f32 sums and bf16 P carry it exactly up to 2^64); only a row
-// without a reference, or whose maximum jumped by more than 2^64, makes its
-// warp redo the tile in two passes (maximum first) and rescale O_i in TMEM.
+// Softmax in the log2 domain with a lagging reference maximum: each softmax
+// thread reads its whole S row into registers (one wait), takes the row
+// maximum there, and computes p against the running reference m, which moves
+// only when the row maximum exceeds it by more than 2^64 (p may exceed 1;
+// f32 sums and bf16 P carry it exactly); a moved reference rescales the row
+// of O_i in TMEM.
 //
 // Score rounding follows ncmorph's bf16 attention (packages/kernels/root.zig:
 // 546-548): the raw score q.k is rounded to bf16 before scaling. Probabilities
@@ -86,17 +89,13 @@ __device__ __forceinline__ bool tile_needed(int t, int P, int A, int B) {
   return k0 < P || (k0 < B && k0 + AT_K > A);
 }
 
-__device__ __forceinline__ bool key_allowed(int k, int P, int lo, int hi, unsigned long long pad_mask) {
-  return k < P ? !((pad_mask >> k) & 1ull) : (k >= lo && k < hi);
-}
-
 __device__ __forceinline__ void raise_abort_attn(volatile int* abort_flag, int* err) {
   *abort_flag = 1;
   atomicOr(err, kErrWaitTimeout);
 }
 
 constexpr int A2_STAGES = 3;
-constexpr float kRescaleLog2 = 8.0f;
+constexpr float kLagLog2 = 64.0f;  // largest lag of the reference maximum (log2 domain)
 
 struct __align__(1024) Attn2Smem {
   uint8_t q[2][AT_Q * AT_D * 2];              // 2 x 16 KB
@@ -107,6 +106,7 @@ struct __align__(1024) Attn2Smem {
   uint64_t kv_full[A2_STAGES];
   uint64_t kv_empty[A2_STAGES];
   uint64_t s_full[2];   // S_i computed
+  uint64_t s_free[2];   // S_i read into registers: the 4 warps of group i (the next S_i may overwrite it)
   uint64_t p_full[2];   // P_i written (and O_i rescaled): the 4 warps of group i
   uint64_t p_empty[2];  // P_i . V done: P_i and O_i free again
   uint64_t drain;
@@ -116,52 +116,78 @@ struct __align__(1024) Attn2Smem {
 constexpr size_t ATTN2_SMEM = sizeof(Attn2Smem) + 1024;
 static_assert(ATTN2_SMEM <= 232448, "attention smem budget");
 
-// One pass over a 128-key S row in tensor memory: p = 2^(bf16(s) * c_scale -
-// m_use) for allowed keys (0 for masked ones) stored as bf16 into the row of
-// the 128-byte-swizzled P tile (two 64-key halves), their sum added to rs.
-// Returns the row's maximum bf16-rounded score times c_scale (log2 domain).
-__device__ __forceinline__ float softmax_tile_pass(uint8_t (*p_half)[AT_Q * 64 * 2], uint32_t sbase, int row,
-                                                   int k0, bool unmasked, int Pq, int lo, int hi,
-                                                   unsigned long long pad_mask, float c_scale, float m_use,
-                                                   float& rs) {
-  const unsigned long long cs2 = f2_pack(c_scale, c_scale), nm2 = f2_pack(-m_use, -m_use);
-  unsigned long long rs2 = f2_pack(0.f, 0.f);
-  uint32_t mx2 = 0xFF80FF80u;  // bf16x2 -inf
-#pragma unroll 1
-  for (int c = 0; c < AT_K; c += 32) {
-    uint32_t v[32];
-    tmem_ld_x32(sbase + c, v);
+// The row's 128 scores from tensor memory (four loads, one wait), rounded to
+// bf16 pairs (ncmorph rounds the raw score q.k to bf16), masked keys set to
+// bf16 -inf, and the row maximum of the rounded scores times c_scale (log2
+// domain). Four independent maximum chains keep the dependency depth short.
+// A masked tile's allowed keys are the row's window [lo, hi) plus, in tile 0,
+// the unpadded prefix keys [0, Pq) (Pq <= 64).
+__device__ __forceinline__ float load_scores(uint32_t sbase, int k0, bool unmasked, int Pq, int lo, int hi,
+                                             unsigned long long pad_mask, float c_scale,
+                                             uint32_t (&pr)[AT_K / 2]) {
+  {
+    uint32_t v[AT_K];
+#pragma unroll
+    for (int c = 0; c < AT_K; c += 32) tmem_ld_x32(sbase + c, *reinterpret_cast<uint32_t(*)[32]>(&v[c]));
     tmem_wait_ld();
-    if (!unmasked) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (!key_allowed(k0 + c + e, Pq, lo, hi, pad_mask)) v[e] = __float_as_uint(-INFINITY);
+    for (int i = 0; i < AT_K / 2; ++i) pr[i] = cvt_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+  }
+  if (!unmasked) {
+    const int a = lo - k0, b = hi - k0;
+    uint32_t m[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int l0 = max(a - 32 * w, 0), h0 = min(b - 32 * w, 32);
+      m[w] = h0 > l0 ? (h0 >= 32 ? 0xFFFFFFFFu : (1u << h0) - 1u) & ~((1u << l0) - 1u) : 0u;
     }
-    uint8_t* prow = p_half[c >> 6] + row * 128;
-    const int ch0 = (c & 63) >> 3;
+    if (k0 < Pq) {
+      const unsigned long long pm = ~pad_mask & (Pq >= 64 ? ~0ull : (1ull << Pq) - 1ull);
+      m[0] |= static_cast<uint32_t>(pm);
+      m[1] |= static_cast<uint32_t>(pm >> 32);
+    }
 #pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {  // four 16-byte chunks of 8 keys
-      uint32_t w4[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int ii = q4 * 8 + e * 2;
-        const uint32_t pr = cvt_bf16x2(__uint_as_float(v[ii]), __uint_as_float(v[ii + 1]));
-        mx2 = bf16x2_max(mx2, pr);
-        const unsigned long long t2 = f2_fma(f2_pack(bf16lo(pr), bf16hi(pr)), cs2, nm2);
-        float t0, t1;
-        f2_unpack(t2, t0, t1);
-        const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-        w4[e] = cvt_bf16x2(p0, p1);
-        rs2 = f2_add(rs2, f2_pack(p0, p1));
-      }
-      const int sw = (ch0 + q4) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
-      *reinterpret_cast<uint4*>(prow + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    for (int i = 0; i < AT_K / 2; ++i) {
+      const uint32_t b2 = (m[i >> 4] >> ((2 * i) & 31)) & 3u;
+      const uint32_t keep = ((b2 & 1u) ? 0x0000FFFFu : 0u) | ((b2 & 2u) ? 0xFFFF0000u : 0u);
+      pr[i] = (pr[i] & keep) | (0xFF80FF80u & ~keep);
     }
   }
+  uint32_t mx[4] = {0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u};  // bf16x2 -inf
+#pragma unroll
+  for (int i = 0; i < AT_K / 2; ++i) mx[i & 3] = bf16x2_max(mx[i & 3], pr[i]);
+  const uint32_t m2 = bf16x2_max(bf16x2_max(mx[0], mx[1]), bf16x2_max(mx[2], mx[3]));
+  return fmaxf(bf16lo(m2), bf16hi(m2)) * c_scale;
+}
+
+// p = 2^(bf16(s) * c_scale - m_use) for the row's 128 keys (masked keys give
+// 2^-inf = 0), stored as bf16 into the row of the 128-byte-swizzled P tile
+// (two 64-key halves); returns the f32 sum of the p (four partial sums).
+__device__ __forceinline__ float exp_pass(uint8_t (*p_half)[AT_Q * 64 * 2], int row, const uint32_t (&pr)[AT_K / 2],
+                                          float c_scale, float m_use) {
+  const unsigned long long cs2 = f2_pack(c_scale, c_scale), nm2 = f2_pack(-m_use, -m_use);
+  unsigned long long rs2[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) rs2[e] = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int c8 = 0; c8 < AT_K / 8; ++c8) {  // sixteen 16-byte chunks of 8 keys
+    uint32_t w4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t p2 = pr[c8 * 4 + e];
+      const unsigned long long t2 = f2_fma(f2_pack(bf16lo(p2), bf16hi(p2)), cs2, nm2);
+      float t0, t1;
+      f2_unpack(t2, t0, t1);
+      const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+      w4[e] = cvt_bf16x2(p0, p1);
+      rs2[e] = f2_add(rs2[e], f2_pack(p0, p1));
+    }
+    const int sw = (c8 & 7) ^ (row & 7);  // 128-byte swizzle: 16-byte chunk XOR row%8
+    *reinterpret_cast<uint4*>(p_half[c8 >> 3] + row * 128 + sw * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
   float r0, r1;
-  f2_unpack(rs2, r0, r1);
-  rs += r0 + r1;
-  return fmaxf(bf16lo(mx2), bf16hi(mx2)) * c_scale;
+  f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), r0, r1);
+  return r0 + r1;
 }
 
 struct TileSpan {
@@ -202,6 +228,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.s_full[i], 1);
+      mbar_init(&S.s_free[i], 4);
       mbar_init(&S.p_full[i], 4);
       mbar_init(&S.p_empty[i], 1);
     }
@@ -270,12 +297,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           if (need_any(u)) return u;
         return -1;
       };
+      // Shared-memory descriptors are computed once: a tile's descriptor is its
+      // base's plus the tile offset / 16, and a 16-element K step adds 32 B
+      // (2 in the address field), so each MMA costs one 64-bit add per operand.
+      const uint64_t dq0 = smem_desc_k_sw128(smem_u32(S.q[0]));
+      const uint64_t dk0 = smem_desc_k_sw128(smem_u32(S.k[0]));
+      const uint64_t dv0 = smem_desc_k_sw128(smem_u32(S.vt[0][0]));
+      const uint64_t dp0 = smem_desc_k_sw128(smem_u32(S.p[0][0]));
+      constexpr uint64_t kQ16 = AT_Q * AT_D * 2 / 16, kK16 = AT_K * AT_D * 2 / 16;
+      constexpr uint64_t kH16 = AT_D * 64 * 2 / 16, kP16 = AT_Q * 64 * 2 / 16;  // V^T and P half tiles
       auto issue_s = [&](int i, int st) {
-        const uint32_t qa = smem_u32(S.q[i]), ka = smem_u32(S.k[st]);
+        const uint64_t da = dq0 + i * kQ16, db = dk0 + st * kK16;
+        const uint32_t d = tmem + i * AT_K;
 #pragma unroll
-        for (int k = 0; k < AT_D / 16; ++k)
-          tc_mma_f16(tmem + i * AT_K, smem_desc_k_sw128(qa + k * 32), smem_desc_k_sw128(ka + k * 32), idesc_s,
-                     k != 0 ? 1u : 0u);
+        for (int k = 0; k < AT_D / 16; ++k) tc_mma_f16(d, da + 2 * k, db + 2 * k, idesc_s, k != 0 ? 1u : 0u);
         tc_commit(&S.s_full[i]);
       };
       int cur = next_needed(-1);
@@ -293,37 +328,45 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int nstage = stage + 1;
         uint32_t nphase = phase;
         if (nstage == A2_STAGES) nstage = 0, nphase ^= 1u;
-        bool kv_ready = false;
-        for (int i = 0; i < 2; ++i) {
-          if (span[i].need(cur)) {
-            // O_i (+)= P_i . V_cur once the softmax of group i released the tile
-            if (!mbar_wait(&S.p_full[i], npv[i] & 1u, abort_flag)) {
+        // S of the next tile first: a group's S buffer is free as soon as its
+        // softmax holds the current scores in registers (s_free), so the next
+        // S is computed while that softmax still runs its exponentials. (A
+        // group without the current tile last read its S before a p_full that
+        // was already waited for.)
+        if (nxt >= 0) {
+          if (!mbar_wait(&S.kv_full[nstage], nphase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int i = 0; i < 2; ++i) {
+            if (!span[i].need(nxt)) continue;
+            if (span[i].need(cur) && !mbar_wait(&S.s_free[i], npv[i] & 1u, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < AT_K / 16; ++kk) {
-              const uint32_t pa = smem_u32(S.p[i][kk >> 2]) + (kk & 3) * 32;
-              const uint32_t va = smem_u32(S.vt[stage][kk >> 2]) + (kk & 3) * 32;
-              tc_mma_f16(tmem + 2 * AT_K + i * AT_D, smem_desc_k_sw128(pa), smem_desc_k_sw128(va), idesc_o,
-                         (npv[i] > 0 || kk != 0) ? 1u : 0u);
-            }
-            tc_commit(&S.p_empty[i]);
-            ++npv[i];
-          }
-          if (nxt >= 0 && span[i].need(nxt)) {
-            // the S_i buffer is free: its softmax finished reading (p_full waited above, or long ago)
-            if (!kv_ready) {
-              if (!mbar_wait(&S.kv_full[nstage], nphase, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              kv_ready = true;
-            }
             issue_s(i, nstage);
           }
+          if (!ok) break;
+        }
+        for (int i = 0; i < 2; ++i) {
+          if (!span[i].need(cur)) continue;
+          // O_i (+)= P_i . V_cur once the softmax of group i wrote P_i
+          if (!mbar_wait(&S.p_full[i], npv[i] & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = dp0 + 2 * i * kP16, db = dv0 + 2 * stage * kH16;
+          const uint32_t d = tmem + 2 * AT_K + i * AT_D;
+          const uint32_t acc0 = npv[i] > 0 ? 1u : 0u;
+#pragma unroll
+          for (int kk = 0; kk < AT_K / 16; ++kk)
+            tc_mma_f16(d, da + (kk >> 2) * kP16 + 2 * (kk & 3), db + (kk >> 2) * kH16 + 2 * (kk & 3), idesc_o,
+                       kk != 0 ? 1u : acc0);
+          tc_commit(&S.p_empty[i]);
+          ++npv[i];
         }
         if (!ok) break;
         tc_commit(&S.kv_empty[stage]);
@@ -372,72 +415,42 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tc_fence_after();
       const int k0 = t * AT_K;
       const bool unmasked = __all_sync(0xffffffffu, k0 >= Pq && k0 >= lo && k0 + AT_K <= hi);
+      // The row maximum is known before any exponential (the scores stay in
+      // registers), so every tile takes one pass. The reference m_used lags
+      // the true maximum: it moves (and O_i is rescaled) only when a tile's
+      // maximum exceeds it by more than 2^kLagLog2, so p may exceed 1, which
+      // f32 sums and bf16 P carry exactly.
+      uint32_t pr[AT_K / 2];
+      const float mt = load_scores(sbase, k0, unmasked, Pq, lo, hi, args.pad_mask, c_scale, pr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.s_free[gi]);  // S_i may now be overwritten by the next tile's S
       // P_i and O_i are free once P.V of this group's previous tile completed
       if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&S.p_empty[gi], (j - 1) & 1u, abort_flag))) {
         ok = false;
         break;
       }
-      // One pass against the running reference m_used when every row of the
-      // warp has one: probabilities may then exceed 1 (the reference lags the
-      // true maximum), which f32 sums and bf16 P carry exactly up to 2^64. A
-      // row without a reference yet, or whose maximum jumped past m_used + 64,
-      // makes the warp redo the tile in two passes with a rescale.
-      bool two_pass = __any_sync(0xffffffffu, m_used == -INFINITY);
-      if (!two_pass) {
-        float rs = 0.f;
-        const float mt = softmax_tile_pass(S.p[gi], sbase, row, k0, unmasked, Pq, lo, hi, args.pad_mask, c_scale,
-                                           m_used, rs);
-        if (__any_sync(0xffffffffu, mt > m_used + 64.f)) {
-          two_pass = true;
-        } else {
-          l += rs;
-        }
+      const bool rescale = mt > m_used + kLagLog2;  // m_used = -inf: any finite maximum
+      const float m_new = rescale ? mt : m_used;
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = rescale ? ex2_approx(m_used - m_new) : 1.f;  // -inf -> 0
+      const float rs = exp_pass(S.p[gi], row, pr, c_scale, m_use);
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        // O_i row *= alpha in tensor memory before the next P.V accumulates into
+        // it (the whole warp executes the TMEM accesses; rows without a rescale
+        // have alpha = 1)
+        uint32_t v[AT_D];
+        tmem_ld_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < AT_D; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+        tmem_st_x32(obase, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_st_x32(obase + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_st();
       }
-      if (two_pass) {
-        // pass 1: row maximum of the raw scores (rounding to bf16 is monotonic)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < AT_K; c += 32) {
-          uint32_t v[32];
-          tmem_ld_x32(sbase + c, v);
-          tmem_wait_ld();
-          if (!unmasked) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (!key_allowed(k0 + c + e, Pq, lo, hi, args.pad_mask)) v[e] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(v[e]));
-            mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
-          }
-        }
-        const float mt = bf16lo(cvt_bf16x2(fmaxf(mx0, mx1), 0.f)) * c_scale;
-        const bool rescale = mt > m_used + kRescaleLog2;  // m_used = -inf: any finite maximum
-        const float m_new = rescale ? mt : m_used;
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = rescale ? ex2_approx(m_used - m_new) : 1.f;  // -inf -> 0
-        // pass 2: t = bf16(s) * scale * log2(e) - m, p = 2^t (<= 256), bf16 into P_i
-        float rs = 0.f;
-        softmax_tile_pass(S.p[gi], sbase, row, k0, unmasked, Pq, lo, hi, args.pad_mask, c_scale, m_use, rs);
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-          // O_i row *= alpha in tensor memory before the next P.V accumulates into
-          // it (the whole warp executes the TMEM accesses; rows without a rescale
-          // have alpha = 1)
-#pragma unroll 1
-          for (int c = 0; c < AT_D; c += 32) {
-            uint32_t v[32];
-            tmem_ld_x32(obase + c, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_x32(obase + c, v);
-          }
-          tmem_wait_st();
-        }
-        l = l * alpha + rs;
-        m_used = m_new;
-      }
+      l = l * alpha + rs;
+      m_used = m_new;
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();

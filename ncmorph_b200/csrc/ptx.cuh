@@ -228,7 +228,6 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   return r;
 }
 
-// 2^x on the special-function unit (PTX ex2.approx; ~2 ulp, -inf -> 0).
 // Element-wise maximum of two packed bf16 pairs.
 __device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -236,6 +235,7 @@ __device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
   return r;
 }
 
+// 2^x on the special-function unit (PTX ex2.approx; ~2 ulp, -inf -> 0).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -277,7 +277,6 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
-
 // ------------------------------------------------- CTA pairs (cta_group::2)
 //
 // Two CTAs of a cluster share one tcgen05.mma (M = 256): each holds its own

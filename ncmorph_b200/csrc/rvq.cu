@@ -750,51 +750,78 @@ __global__ void __launch_bounds__(256) scale_advance_kernel(const int32_t* __res
   const int ch = static_cast<int>(wg - p * nch);
   const int lane = threadIdx.x & 31;
   if (p >= rows_pooled) return;
-  for (int l = 0; l < L; ++l) {
-    const int c = codes[static_cast<size_t>(l) * rows_pooled + p];
-    if (c < 0 || c >= K) {
+  // Levels in groups of eight: lanes 0-7 read the group's codes (checked
+  // before any use), then the eight codeword gathers are issued together and
+  // summed in level order.
+  const int d = ch * 128 + lane * 4;
+  const bool act = d < D;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int l0 = 0; l0 < L; l0 += 8) {
+    const int nl = min(8, L - l0);
+    const int mc = lane < nl ? __ldg(codes + static_cast<size_t>(l0 + lane) * rows_pooled + p) : 0;
+    if (__any_sync(0xffffffffu, lane < nl && (mc < 0 || mc >= K))) {
       if (lane == 0 && ch == 0) atomicOr(err, kErrBadIndex);
       return;
     }
+    uint2 ev[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = __shfl_sync(0xffffffffu, mc, j);
+      ev[j] = make_uint2(0u, 0u);
+      if (j < nl && act)
+        ev[j] = __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l0 + j) * K + c) * D + d));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < nl) {
+        q.x += bf16lo(ev[j].x);
+        q.y += bf16hi(ev[j].x);
+        q.z += bf16lo(ev[j].y);
+        q.w += bf16hi(ev[j].y);
+      }
+    }
   }
-  const int d = ch * 128 + lane * 4;
-  if (d >= D) return;
-  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int l = 0; l < L; ++l) {
-    const int c = __ldg(codes + static_cast<size_t>(l) * rows_pooled + p);
-    const uint2 ev = __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
-    q.x += bf16lo(ev.x);
-    q.y += bf16hi(ev.x);
-    q.z += bf16lo(ev.y);
-    q.w += bf16hi(ev.y);
-  }
+  if (!act) return;
   *reinterpret_cast<float4*>(q_out + static_cast<size_t>(p) * D + d) = q;
   if (!update_r) return;
   float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int i = 0; i < f; ++i) {
-    const size_t row = static_cast<size_t>(p) * f + i;
-    float4 r = *reinterpret_cast<const float4*>(resid + row * D + d);
-    r.x -= q.x;
-    r.y -= q.y;
-    r.z -= q.z;
-    r.w -= q.w;
-    *reinterpret_cast<float4*>(resid + row * D + d) = r;
-    if (g <= 0) continue;
-    if (i % g == 0) {
-      sum = r;
-    } else {
-      sum.x += r.x;
-      sum.y += r.y;
-      sum.z += r.z;
-      sum.w += r.w;
-    }
-    if (i % g == g - 1) {
-      const float gf = static_cast<float>(g);
-      const float4 u = make_float4(sum.x / gf, sum.y / gf, sum.z / gf, sum.w / gf);
-      const size_t urow = row / g;
-      *reinterpret_cast<float4*>(u_next + urow * D + d) = u;
-      *reinterpret_cast<uint2*>(u_next_bf16 + urow * D + d) = make_uint2(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w));
+  // The rows are read in batches of kBatch before any of them is written back:
+  // loads and stores share one pointer with a run-time row stride, so without
+  // the batching each load would wait for the previous row's store.
+  constexpr int kBatch = 4;
+  for (int i0 = 0; i0 < f; i0 += kBatch) {
+    float4 r[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (i0 + j < f)
+        r[j] = *reinterpret_cast<const float4*>(resid + (static_cast<size_t>(p) * f + i0 + j) * D + d);
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = i0 + j;
+      if (i >= f) break;
+      const size_t row = static_cast<size_t>(p) * f + i;
+      r[j].x -= q.x;
+      r[j].y -= q.y;
+      r[j].z -= q.z;
+      r[j].w -= q.w;
+      *reinterpret_cast<float4*>(resid + row * D + d) = r[j];
+      if (g <= 0) continue;
+      if (i % g == 0) {
+        sum = r[j];
+      } else {
+        sum.x += r[j].x;
+        sum.y += r[j].y;
+        sum.z += r[j].z;
+        sum.w += r[j].w;
+      }
+      if (i % g == g - 1) {
+        const float gf = static_cast<float>(g);
+        const float4 u = make_float4(sum.x / gf, sum.y / gf, sum.z / gf, sum.w / gf);
+        const size_t urow = row / g;
+        *reinterpret_cast<float4*>(u_next + urow * D + d) = u;
+        *reinterpret_cast<uint2*>(u_next_bf16 + urow * D + d) =
+            make_uint2(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w));
+      }
     }
   }
 }

@@ -81,6 +81,34 @@ def test_attention_matches_oracle(orc, cuda_dev, mode, T, prefix, levels, pad, H
     print(f"{mode} T={T}: max |err| {err.max():.3g}, mean {err.mean():.3g}")
 
 
+@pytest.mark.parametrize("step", [128, 512])
+def test_attention_running_maximum_jumps(orc, cuda_dev, step):
+    """Scores that rise tile by tile, so the running reference maximum lags
+    (step 128: by 23 per tile in the log2 domain, moved every third tile)
+    or moves at every tile (step 512: 92 per tile, O rescaled by 2^-92).
+    Integer-valued Q and K without RoPE make every score exact in f32 and in
+    bf16, so the GPU and the oracle round the same scores."""
+    from ncmorph_b200 import _lib, ncm_model
+    T, H, Hkv = 512, 2, 1
+    rng = np.random.default_rng(step)
+    x = np.zeros((T, (H + 2 * Hkv) * 64), np.float32)
+    x[:, 0:8] = 1.0                      # query head 0: ones on the first 8 dims
+    x[:, 64:72] = 1.0                    # query head 1
+    t = np.arange(T)
+    x[:, H * 64:H * 64 + 8] = (step // 8 * (t // 128) + t % 8)[:, None]   # key: q.k = step * tile + 8 (t % 8)
+    x[:, (H + Hkv) * 64:] = rng.standard_normal((T, Hkv * 64))
+    qkv_bits = orc.bf16_bits(x)
+    assert np.array_equal(orc.bf16_widen(qkv_bits)[:, H * 64:H * 64 + 8], x[:, H * 64:H * 64 + 8])
+    mask = ncm_model.make_mask("causal", 0, (), ())
+    ctx = ncm_model.attention_bf16(to_dev_bf16(qkv_bits, cuda_dev), H, Hkv, mask)
+    got = orc.bf16_widen(from_dev_bf16(ctx))
+    cos = np.ones((T, 64), np.float32)
+    sin = np.zeros((T, 64), np.float32)
+    ref = oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, orc.causal_mask(t, t))
+    err = np.abs(got - ref)
+    assert np.all(err <= 2e-2 * np.abs(ref) + 1e-2 * np.abs(x[:, (H + Hkv) * 64:]).max()), err.max()
+
+
 def test_rope_in_place_matches_rotate_head(orc, cuda_dev):
     from ncmorph_b200 import ncm_model
     rng = np.random.default_rng(3)
