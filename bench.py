@@ -52,7 +52,7 @@ def parse_args():
                    help="tokenizer workload: upsampling mode of each scale's reconstruction")
     p.add_argument("--phi", action="store_true",
                    help="tokenizer workload: apply the quantiser's Phi convolution after each upsampling")
-    p.add_argument("--workload", choices=["rvq", "tokenizer", "linear", "decoder"], default="rvq",
+    p.add_argument("--workload", choices=["rvq", "tokenizer", "linear", "decoder", "aux"], default="rvq",
                    help="rvq = BASELINE config 5 (the headline); tokenizer = config 2; linear = config 3 sweep; "
                         "decoder = config 4")
     return p.parse_args()
@@ -405,6 +405,151 @@ def _tokenizer_e2e(x, x_host, codes_host, forward, steps):
     return e0.elapsed_time(e1) / max(steps, 1)
 
 
+def _event_ms(fn, reps, flush=None):
+    """Median CUDA-event time of fn over reps calls; flush() (an L2-sized
+    write) runs before each call, outside the timed window."""
+    import torch
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return sorted(times)[len(times) // 2]
+
+
+def _write_safetensors(path, tensors):
+    """Minimal safetensors writer: 8-byte little-endian header length, JSON
+    header with dtype/shape/data_offsets, then the raw little-endian bytes."""
+    import json as _json
+    import struct
+    header, blobs, off = {}, [], 0
+    for name, (dtype, arr) in tensors.items():
+        b = arr.tobytes()
+        header[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = _json.dumps(header).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+    return 8 + len(h) + off
+
+
+def _aux_suite(a, dev, rnd, peaks, peak_kind):
+    """The next-row pieces measured against their rooflines: the tied
+    codebook head (tensor), the device loader (host-to-device copy), and the
+    training-time quantiser pieces (HBM / tensor)."""
+    import os
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    from ncmorph_b200 import loader, ncm_model, quantizer
+    hbm = float(peaks["hbm_gbs"])
+    tensor = float(peaks["bf16_tflops"])
+    scratch = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
+    flush = scratch.zero_
+    reps = max(a.steps, 5)
+    out = {}
+
+    # (f)3 tied codebook head at the NCM shapes: T = 4096 positions, d = 1024, K = 4096 codes
+    T, d, K = 4096, 1024, 4096
+    z, cb = rnd((T, d)), rnd((K, d))
+    bias = torch.zeros(K, dtype=torch.float32, device=dev)
+    flops = 2.0 * T * K * d
+    for name, fn in (("tied_head_logits", lambda: ncm_model.tied_head_logits(z, cb, 0.5, bias)),
+                     ("tied_head_argmax", lambda: ncm_model.tied_head_argmax(z, cb, 0.5, bias))):
+        for _ in range(3):
+            fn()
+        ms = _event_ms(fn, reps, flush)
+        ach = flops / (ms * 1e-3) / 1e12
+        out[name] = {"value": ach, "unit": "TFLOP/s", "ms": ms, "shape": [T, d, K],
+                     "roofline": {"bound": "tensor", "achieved": ach, "peak": tensor, "unit": "TFLOP/s",
+                                  "frac": ach / tensor, "peak_source": f"{peak_kind} bf16_tflops (burst)"}}
+
+    # (f)2 device loader: a synthetic checkpoint (bf16, f16 and f32 tensors) read from the page cache
+    rng = np.random.default_rng(a.seed)
+    tmp = tempfile.mkdtemp()
+    path = os.path.join(tmp, "synthetic.safetensors")
+    try:
+        w32 = rng.standard_normal((4096, 4096), dtype=np.float32)
+        tensors = {"bf16": ("BF16", (rng.standard_normal((8192, 8192), dtype=np.float32).view(np.uint32) >> 16)
+                            .astype(np.uint16)),
+                   "f16": ("F16", w32[:, :].astype(np.float16).reshape(8192, 2048)),
+                   "f32": ("F32", w32)}
+        nbytes = _write_safetensors(path, tensors)
+        loader.load_all_bf16(path, dev)               # warm the page cache and the staging buffers
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            loaded = loader.load_all_bf16(path, dev)
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+        sec = sorted(times)[1]
+        host = torch.empty(nbytes // 4, dtype=torch.float32).pin_memory()
+        devbuf = torch.empty_like(host, device=dev)
+        h2d_ms = _event_ms(lambda: devbuf.copy_(host, non_blocking=True), 3)
+        h2d = host.numel() * 4 / (h2d_ms * 1e-3) / 1e9
+        gbs = nbytes / sec / 1e9
+        out["loader"] = {"value": gbs, "unit": "GB/s (file bytes)", "file_bytes": nbytes,
+                         "tensors": {k: list(v.shape) for k, v in loaded.items()},
+                         "roofline": {"bound": "host-to-device copy", "achieved": gbs, "peak": h2d, "unit": "GB/s",
+                                      "frac": gbs / h2d,
+                                      "peak_source": "pinned-host to device copy of the same bytes, this run"}}
+        del loaded, host, devbuf
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+        os.rmdir(tmp)
+
+    # (f)4 pre-quant GroupNorm (8 groups) over [8, 2048, 1024] f32: read + write
+    x = torch.randn((8, 2048, 1024), device=dev)
+    ms = _event_ms(lambda: quantizer.group_norm(x, 8), reps, flush)
+    gbs = 2 * x.numel() * 4 / (ms * 1e-3) / 1e9
+    out["group_norm"] = {"value": gbs, "unit": "GB/s", "ms": ms, "shape": list(x.shape),
+                         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}}
+    # one level-0 cascade stage at the tokenizer width: x [8, 2048, 1024] bf16
+    xb = rnd((8, 2048, 1024))
+    wd, wu = rnd((1024, 1024, 4), 0.02), rnd((1024, 1024, 4), 0.02)
+    for name, fn in (("conv_down4", lambda: quantizer.conv_down4(xb, wd)),
+                     ("conv_up4", lambda: quantizer.conv_up4(xb, wu))):
+        f = 2.0 * 8 * 2048 * 1024 * 4096 / (4 if name == "conv_down4" else 1)
+        ms = _event_ms(fn, reps, flush)
+        ach = f / (ms * 1e-3) / 1e12
+        out[name] = {"value": ach, "unit": "TFLOP/s", "ms": ms,
+                     "roofline": {"bound": "tensor", "achieved": ach, "peak": tensor, "unit": "TFLOP/s",
+                                  "frac": ach / tensor}}
+    # codebook EMA of one level at scale 5 of the tokenizer: N = 16384 rows, D = 1024, K = 4096
+    N, D, K = 16384, 1024, 4096
+    u = torch.randn((N, D), device=dev)
+    codes = torch.randint(0, K, (N,), dtype=torch.int32, device=dev)
+    ema = quantizer.CodebookEMA(torch.randn((K, D), device=dev))
+    ms = _event_ms(lambda: ema.stats(u, codes), reps, flush)
+    byt = N * D * 4 + K * D * 4 + N * 4 * 4  # rows read once, sums written, codes/order passes
+    gbs = byt / (ms * 1e-3) / 1e9
+    out["ema_code_stats"] = {"value": gbs, "unit": "GB/s", "ms": ms,
+                             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                          "frac": gbs / hbm}}
+    cbb = torch.empty((K, D), dtype=torch.bfloat16, device=dev)
+    ms = _event_ms(lambda: ema.update(u, codes, codebook_bf16=cbb), reps, flush)
+    out["ema_stats_and_update"] = {"value": ms, "unit": "ms"}
+    return {"metric": "tied_head_logits_tflops", "value": out["tied_head_logits"]["value"], "unit": "TFLOP/s",
+            "config": {"workload": "next-row pieces: tied head, device loader, GroupNorm, level-0 convs, EMA"},
+            "results": out, "roofline": out["tied_head_logits"]["roofline"],
+            "gpu_launches": None}
+
+
 def _graphed(fn, enabled):
     """Returns fn itself, or a replay of one CUDA-graph capture of fn (after a
     warm-up call, the library's calls allocate nothing and do no host sync)."""
@@ -552,6 +697,8 @@ def run_secondary(a):
             "roofline": {"bound": "min(tensor, hbm x intensity) per shape",
                          "peak_source": f"{peak_kind} bf16_tflops / hbm_gbs"},
             "clocks": clocks})
+    elif a.workload == "aux":
+        line.update(_aux_suite(a, dev, rnd, peaks, peak_kind))
     else:  # decoder
         cfg = ncm_model.Config(hidden_size=2048, vq_width=1024, num_attention_heads=32, num_key_value_heads=8,
                                intermediate_size=8192, level_lengths=(256, 256, 512, 1024, 2048),

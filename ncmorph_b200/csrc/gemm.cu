@@ -68,10 +68,10 @@ struct LinearArgs {
   int taps, nk_tap;
   ConvEpilogue conv;
   SegMap map;
-  // mode 4 (codebook-tied head logits into y_f32): esq [N], bias [N] or null,
-  // scal = {d_scale, exp(log_inv_T)} on the device
-  const float* head_esq;
-  const float* head_bias;
+  // mode 4 (codebook-tied head logits into y_f32): logits = fmaf(2 s, acc, -c[n])
+  // with per-code offsets c [N] = s E_sq - bias and scal[2] = -2 s on the device
+  // (s = exp(log_inv_T) / d_scale)
+  const float* head_c;
   const float* head_scal;
   // mode 5 (fused QKV projection): RoPE on the Q and K columns (n < voff) with
   // per-token tables cos/sin [M, 64]; V columns also written transposed to
@@ -401,37 +401,37 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       } else if (!SWAP && args.mode == 4) {
-        // logits = (2 acc - esq) / d_scale * exp(log_inv_T) + bias (_TiedCodebookHead)
-        const float dsc = __ldg(args.head_scal), esc = __ldg(args.head_scal + 1);
+        // logits = (2 acc - esq) / d_scale * exp(log_inv_T) + bias (_TiedCodebookHead),
+        // evaluated as fmaf(2 s, acc, -c) with the argmax form's operands
+        const float s2 = -__ldg(args.head_scal + 2);
         const int m = arow;
 #pragma unroll 1
         for (int c = c0; c < BN; c += 32) {
           uint32_t v[16];
           tmem_ld_x16(tbase + c, v);
+          const int n0 = tb * BN + c;
+          float4 cv[4];
+          const bool vec = args.vec_ok && n0 + 16 <= args.N;
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) cv[j] = __ldg(reinterpret_cast<const float4*>(args.head_c + n0 + 4 * j));
+          }
           tmem_wait_ld();
           if (m >= args.M) continue;
-          const int n0 = tb * BN + c;
           float* dst = args.y_f32 + static_cast<size_t>(m) * args.N + n0;
-          if (args.vec_ok && n0 + 16 <= args.N) {
+          if (vec) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 e = __ldg(reinterpret_cast<const float4*>(args.head_esq + n0 + j));
-              const float4 bb = args.head_bias != nullptr
-                                    ? __ldg(reinterpret_cast<const float4*>(args.head_bias + n0 + j))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < 4; ++j) {
               float4 l;
-              l.x = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j]), -e.x), dsc), esc) + bb.x;
-              l.y = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 1]), -e.y), dsc), esc) + bb.y;
-              l.z = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 2]), -e.z), dsc), esc) + bb.z;
-              l.w = __fmul_rn(__fdiv_rn(fmaf(2.f, __uint_as_float(v[j + 3]), -e.w), dsc), esc) + bb.w;
-              *reinterpret_cast<float4*>(dst + j) = l;
+              l.x = fmaf(s2, __uint_as_float(v[4 * j + 0]), -cv[j].x);
+              l.y = fmaf(s2, __uint_as_float(v[4 * j + 1]), -cv[j].y);
+              l.z = fmaf(s2, __uint_as_float(v[4 * j + 2]), -cv[j].z);
+              l.w = fmaf(s2, __uint_as_float(v[4 * j + 3]), -cv[j].w);
+              *reinterpret_cast<float4*>(dst + 4 * j) = l;
             }
           } else {
-            for (int j = 0; j < 16 && n0 + j < args.N; ++j) {
-              const float t = fmaf(2.f, __uint_as_float(v[j]), -__ldg(args.head_esq + n0 + j));
-              dst[j] = __fmul_rn(__fdiv_rn(t, dsc), esc) +
-                       (args.head_bias != nullptr ? __ldg(args.head_bias + n0 + j) : 0.f);
-            }
+            for (int j = 0; j < 16 && n0 + j < args.N; ++j)
+              dst[j] = fmaf(s2, __uint_as_float(v[j]), -__ldg(args.head_c + n0 + j));
           }
         }
       } else if (!SWAP && args.mode == 3) {
@@ -848,9 +848,8 @@ int linear_qkv_rope(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const ui
   return launch_shape(ctx, choose_shape(ctx, M, N, 5), x, M, K, w, N, K, a, KID_LINEAR, stream);
 }
 
-int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
-                          const float* bias, const float* scal, float* logits, int64_t T, int64_t d, int64_t K,
-                          cudaStream_t stream) {
+int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* c,
+                          const float* scal, float* logits, int64_t T, int64_t d, int64_t K, cudaStream_t stream) {
   LinearArgs a{};
   a.mode = 4;
   a.taps = 1;
@@ -859,11 +858,10 @@ int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codeb
   a.N = static_cast<int>(K);
   a.K = static_cast<int>(d);
   a.y_f32 = logits;
-  a.head_esq = esq;
-  a.head_bias = bias;
+  a.head_c = c;
   a.head_scal = scal;
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  a.vec_ok = K % 4 == 0 && al(logits) && al(esq) && al(bias);
+  a.vec_ok = K % 4 == 0 && al(logits) && al(c);
   return launch_shape(ctx, choose_shape(ctx, T, K, 4), z, T, d, codebook, K, d, a, KID_LINEAR, stream);
 }
 

@@ -2,14 +2,16 @@
 // PROJECT.md:222; decision D18 at PROJECT.md:471):
 //     E_sq[k]  = sum_d E[k,d]^2            d_scale = mean_k E_sq[k]
 //     logits   = (2 z.E^T - E_sq) / d_scale * exp(log_inv_T) + bias
-// It is the RVQ distance GEMM with another epilogue. Two forms:
+// It is the RVQ distance GEMM with another epilogue. With s = exp(log_inv_T)
+// / d_scale and per-code offsets c_k = s E_sq[k] - bias[k], logits =
+// fmaf(2 s, z.E_k, -c_k) (one FMA per logit; the module's own order, with a
+// division per element, differs from it by rounding only). Two forms:
 //   * ncm_tied_head_logits writes the [T, K] logits (tcgen05 GEMM, mode-4
 //     epilogue in gemm.cu);
 //   * ncm_tied_head_argmax returns argmax_k logits (the temperature-0 pick of
-//     _sample_level_raw) without materialising them: with s = exp(log_inv_T)
-//     / d_scale, -logits = fmaf(-2 s, z.E_k, s E_sq[k] - bias[k]), so the RVQ
-//     argmin kernel runs with multiplier -2 s and per-code offsets
-//     c_k = s E_sq[k] - bias[k].
+//     _sample_level_raw) without materialising them: -logits =
+//     fmaf(-2 s, z.E_k, c_k), so the RVQ argmin kernel runs with multiplier
+//     -2 s and the offsets c_k.
 #include <algorithm>
 
 #include "internal.h"
@@ -90,9 +92,11 @@ int ncm_tied_head_logits(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* code
   WsCarver cv;
   const size_t o_sq = cv.take(esq ? 0 : sizeof(float) * K);
   const size_t o_sc = cv.take(4 * sizeof(float));
+  const size_t o_c = cv.take(sizeof(float) * K);
   uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
   if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "tied head: workspace allocation failed");
   float* scal = reinterpret_cast<float*>(ws + o_sc);
+  float* c = reinterpret_cast<float*>(ws + o_c);
   if (esq == nullptr) {
     float* sq = reinterpret_cast<float*>(ws + o_sq);
     Launch _launch(ctx, KID_SQNORM, st);
@@ -101,10 +105,10 @@ int ncm_tied_head_logits(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* code
   }
   {
     Launch _launch(ctx, KID_CAST, st);
-    head_prep_kernel<<<1, 1024, 0, st>>>(esq, bias, static_cast<int>(K), log_inv_T, scal, nullptr);
+    head_prep_kernel<<<1, 1024, 0, st>>>(esq, bias, static_cast<int>(K), log_inv_T, scal, c);
     NCM_CUDA_TRY(cudaGetLastError());
   }
-  return tied_head_logits_gemm(ctx, z, codebook, esq, bias, scal, logits, T, d, K, st);
+  return tied_head_logits_gemm(ctx, z, codebook, c, scal, logits, T, d, K, st);
 }
 
 int ncm_tied_head_argmax(ncm_ctx_t* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,

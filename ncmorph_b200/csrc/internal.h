@@ -247,11 +247,11 @@ int linear_qkv_rope(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const ui
                     int64_t voff, cudaStream_t stream);
 
 // ---- codebook-tied head (head.cu, gemm.cu)
-// logits [T, K] f32 = (2 z.E^T - esq) / scal[0] * scal[1] + bias, z [T, d] and
-// E [K, d] bf16; scal = {d_scale, exp(log_inv_T)} in device memory.
-int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* esq,
-                          const float* bias, const float* scal, float* logits, int64_t T, int64_t d, int64_t K,
-                          cudaStream_t stream);
+// logits [T, K] f32 = fmaf(2 s, z.E^T, -c) with c [K] = s esq - bias, z [T, d]
+// and E [K, d] bf16; scal = {d_scale, exp(log_inv_T), -2 s} in device memory
+// (s = exp(log_inv_T) / d_scale).
+int tied_head_logits_gemm(ncm_ctx* ctx, const uint16_t* z, const uint16_t* codebook, const float* c,
+                          const float* scal, float* logits, int64_t T, int64_t d, int64_t K, cudaStream_t stream);
 
 // ---- kernel-3 convolution over row segments (conv.cu, gemm.cu)
 //

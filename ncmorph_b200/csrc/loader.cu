@@ -1,8 +1,8 @@
 // Device-side safetensors tensor loader (the bf16-native form of
 // src/loader.zig:286-345 `read_tensor` + `decode_chunk`): a tensor's bytes
 // stream from the file through two pinned staging buffers straight into
-// device memory, with the file read of chunk i+1 overlapping the
-// host-to-device copy of chunk i. BF16 bytes are stored as they are (no f32
+// device memory, with the file read of chunk i+1 (four reader threads, one
+// slice each) overlapping the host-to-device copy of chunk i. BF16 bytes are stored as they are (no f32
 // widening); F16 and F32 are rounded to bf16 on the device with the bf16
 // package's rule (packages/bf16/root.zig:17-31: round to nearest even,
 // NaN -> 0x7FC0), the operand rounding the bf16 linears apply anyway.
@@ -12,13 +12,46 @@
 
 #include <cerrno>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "internal.h"
 
 namespace ncm {
 namespace {
 
-constexpr size_t kChunk = 8u << 20;  // bytes per staged chunk (a multiple of every element size)
+constexpr size_t kChunk = 16u << 20;  // bytes per staged chunk (a multiple of every element size)
+constexpr int kReaders = 4;           // threads reading one chunk, a contiguous slice each
+
+// n bytes at file offset off into h: 0, an errno value, or -1 at an early end of file
+int read_slice(int fd, uint8_t* h, size_t n, uint64_t off) {
+  size_t got = 0;
+  while (got < n) {
+    const ssize_t r = pread(fd, h + got, n - got, static_cast<off_t>(off + got));
+    if (r < 0 && errno == EINTR) continue;
+    if (r < 0) return errno != 0 ? errno : EIO;
+    if (r == 0) return -1;
+    got += static_cast<size_t>(r);
+  }
+  return 0;
+}
+
+// the chunk split over kReaders threads (one thread below 1 MiB); the first failure is returned
+int read_chunk(int fd, uint8_t* h, size_t n, uint64_t off) {
+  if (n < (1u << 20)) return read_slice(fd, h, n, off);
+  const size_t slice = (n / kReaders + 4095) / 4096 * 4096;
+  int res[kReaders] = {0};
+  std::vector<std::thread> th;
+  for (int r = 1; r < kReaders; ++r) {
+    const size_t a = std::min(n, r * slice), b = std::min(n, (r + 1) * slice);
+    if (b > a) th.emplace_back([&, r, a, b]() { res[r] = read_slice(fd, h + a, b - a, off + a); });
+  }
+  res[0] = read_slice(fd, h, std::min(n, slice), off);
+  for (auto& t : th) t.join();
+  for (int r = 0; r < kReaders; ++r)
+    if (res[r] != 0) return res[r];
+  return 0;
+}
 
 __global__ void __launch_bounds__(256) f16_to_bf16_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                                                           long long n) {
@@ -115,18 +148,12 @@ int ncm_load_tensor_bf16(ncm_ctx_t* ctx, const char* path, uint64_t offset, uint
       }
     }
     uint8_t* h = static_cast<uint8_t*>(ctx->load_h[b]);
-    size_t got = 0;
-    while (got < n) {
-      const ssize_t r = pread(fd, h + got, n - got, static_cast<off_t>(offset + done_bytes + got));
-      if (r < 0 && errno == EINTR) continue;
-      if (r <= 0) {
-        const int err = errno;
-        cleanup();
-        return ncm_fail(NCM_EINVAL, "load_tensor: read of %s at %llu failed: %s", path,
-                        (unsigned long long)(offset + done_bytes + got), r == 0 ? "unexpected end of file"
-                                                                                 : std::strerror(err));
-      }
-      got += static_cast<size_t>(r);
+    const int rerr = read_chunk(fd, h, n, offset + done_bytes);
+    if (rerr != 0) {
+      cleanup();
+      return ncm_fail(NCM_EINVAL, "load_tensor: read of %s in [%llu, %llu) failed: %s", path,
+                      (unsigned long long)(offset + done_bytes), (unsigned long long)(offset + done_bytes + n),
+                      rerr < 0 ? "unexpected end of file" : std::strerror(rerr));
     }
     cudaError_t e;
     const long long elems = static_cast<long long>(n / esize);

@@ -3,7 +3,7 @@
 //
 //  * pre-quantisation GroupNorm, affine=False (:43-49; upstream
 //    models/vqvae.py:66, :82, :86): per sample and group, statistics over all
-//    positions and the group's channels, y = (x - mean) / sqrt(var + eps);
+//    positions and the group's channels (f64 sums), y = (x - mean) * rstd;
 //  * the learned level-0 cascade (:127-139): Conv1d(C, C, kernel 4,
 //    stride 4) down and ConvTranspose1d(C, C, kernel 4, stride 4) up. On
 //    [B, L, C] rows both are GEMMs on the tcgen05 linear kernel: four
@@ -30,45 +30,92 @@ namespace {
 int blocks_of(long long n, int per) { return static_cast<int>((n + per - 1) / per); }
 
 // ------------------------------------------------------------- GroupNorm
-// One block per (sample, group): sum and sum of squares in f64 over T rows x
-// cg channels, then the normalised values (f32).
-__global__ void __launch_bounds__(256) group_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int T,
-                                                         int C, int G, float eps) {
-  const int b = blockIdx.x / G, g = blockIdx.x - (blockIdx.x / G) * G;
-  const int cg = C / G;
-  const float* xb = x + static_cast<size_t>(b) * T * C + g * cg;
-  float* yb = y + static_cast<size_t>(b) * T * C + g * cg;
-  const long long n = static_cast<long long>(T) * cg;
+// Three passes so every SM takes part: (1) block (sample*group, chunk) sums a
+// slab of rows of one group in f64 into partials[sg][chunk]; (2) one thread
+// per (sample, group) adds its partials in chunk order (the same bits every
+// run) into mean and 1/sqrt(var + eps); (3) an elementwise pass normalises
+// four channels per thread.
+constexpr int kGnChunks = 32;
+
+// VEC: the group's channels are read as float4 (C / G a multiple of 4, x 16-byte aligned)
+template <bool VEC>
+__global__ void __launch_bounds__(256) group_norm_partial_kernel(const float* __restrict__ x, int T, int C, int G,
+                                                                 double2* __restrict__ part) {
+  const int sg = blockIdx.x;
+  const int b = sg / G, g = sg - (sg / G) * G;
+  constexpr int W = VEC ? 4 : 1;
+  const unsigned cw = static_cast<unsigned>(C / G / W);  // vectors per row of the group
+  const int t0 = static_cast<int>((static_cast<long long>(T) * blockIdx.y) / kGnChunks);
+  const int t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.y + 1)) / kGnChunks);
+  const float* xb = x + static_cast<size_t>(b) * T * C + static_cast<size_t>(g) * (C / G);
+  // rows of a chunk x vectors of a row stay below 2^32 for any T, C below 2^31 split 32 ways
+  const unsigned n = static_cast<unsigned>(t1 - t0) * cw;
   double s = 0.0, ss = 0.0;
-  for (long long i = threadIdx.x; i < n; i += blockDim.x) {
-    const long long t = i / cg;
-    const float v = xb[t * C + (i - t * cg)];
-    s += v;
-    ss += static_cast<double>(v) * v;
+  for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned r = i / cw;
+    const float* px = xb + static_cast<size_t>(t0 + r) * C + (i - r * cw) * W;
+    if constexpr (VEC) {
+      const float4 v = *reinterpret_cast<const float4*>(px);
+      s += static_cast<double>(v.x) + static_cast<double>(v.y) + static_cast<double>(v.z) + static_cast<double>(v.w);
+      ss = __fma_rn(static_cast<double>(v.x), v.x, ss);
+      ss = __fma_rn(static_cast<double>(v.y), v.y, ss);
+      ss = __fma_rn(static_cast<double>(v.z), v.z, ss);
+      ss = __fma_rn(static_cast<double>(v.w), v.w, ss);
+    } else {
+      const float v = *px;
+      s += v;
+      ss = __fma_rn(static_cast<double>(v), v, ss);
+    }
   }
-  __shared__ double red[2][8];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     s += __shfl_xor_sync(0xffffffffu, s, o);
     ss += __shfl_xor_sync(0xffffffffu, ss, o);
   }
+  __shared__ double red[2][8];
   if ((threadIdx.x & 31) == 0) red[0][threadIdx.x >> 5] = s, red[1][threadIdx.x >> 5] = ss;
   __syncthreads();
-  __shared__ float stat[2];
   if (threadIdx.x == 0) {
     double a = 0.0, q = 0.0;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) a += red[0][w], q += red[1][w];
-    const double mean = a / n;
-    const double var = std::max(q / n - mean * mean, 0.0);  // biased variance, as GroupNorm
-    stat[0] = static_cast<float>(mean);
-    stat[1] = static_cast<float>(1.0 / sqrt(var + eps));
+    part[static_cast<size_t>(sg) * kGnChunks + blockIdx.y] = make_double2(a, q);
   }
-  __syncthreads();
-  const float mean = stat[0], rstd = stat[1];
-  for (long long i = threadIdx.x; i < n; i += blockDim.x) {
-    const long long t = i / cg;
-    const long long o = t * C + (i - t * cg);
-    yb[o] = (xb[o] - mean) * rstd;
+}
+
+__global__ void __launch_bounds__(256) group_norm_stats_kernel(const double2* __restrict__ part, int n_sg,
+                                                               long long count, float eps, float2* __restrict__ stat) {
+  const int sg = blockIdx.x * blockDim.x + threadIdx.x;
+  if (sg >= n_sg) return;
+  double a = 0.0, q = 0.0;
+  for (int c = 0; c < kGnChunks; ++c) {
+    const double2 v = part[static_cast<size_t>(sg) * kGnChunks + c];
+    a += v.x;
+    q += v.y;
+  }
+  const double mean = a / count;
+  const double var = fmax(q / count - mean * mean, 0.0);  // biased variance, as GroupNorm
+  stat[sg] = make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + eps)));
+}
+
+// VEC: four elements per thread (C / G a multiple of 4, 16-byte aligned
+// buffers: the four share a group); otherwise one element per thread
+template <bool VEC>
+__global__ void __launch_bounds__(256) group_norm_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                               long long n, int T, int C, int G,
+                                                               const float2* __restrict__ stat) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  constexpr int W = VEC ? 4 : 1;
+  if (i * W >= n) return;
+  const long long e = i * W;
+  const int c = static_cast<int>(e % C);
+  const long long b = e / (static_cast<long long>(T) * C);
+  const float2 st = stat[b * G + c / (C / G)];
+  if constexpr (VEC) {
+    const float4 v = *reinterpret_cast<const float4*>(x + e);
+    *reinterpret_cast<float4*>(y + e) =
+        make_float4((v.x - st.x) * st.y, (v.y - st.x) * st.y, (v.z - st.x) * st.y, (v.w - st.x) * st.y);
+  } else {
+    y[e] = (x[e] - st.x) * st.y;
   }
 }
 
@@ -279,14 +326,35 @@ int ncm_group_norm(ncm_ctx_t* ctx, const float* x, float* y, int64_t batch, int6
                    float eps, ncm_stream_t stream) {
   int rc = check_ctx_aux(ctx);
   if (rc) return rc;
-  if (batch <= 0 || T <= 0 || C <= 0 || groups <= 0 || C % groups != 0 || batch * groups > INT32_MAX)
+  if (batch <= 0 || T <= 0 || C <= 0 || groups <= 0 || C % groups != 0 || batch * groups > INT32_MAX ||
+      T > INT32_MAX || C > INT32_MAX)
     return ncm_fail(NCM_EINVAL, "group_norm: bad shape (B=%lld T=%lld C=%lld groups=%d)", (long long)batch,
                     (long long)T, (long long)C, groups);
   if (!x || !y) return ncm_fail(NCM_EINVAL, "group_norm: null buffer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n_sg = static_cast<int>(batch * groups);
+  WsCarver cv;
+  const size_t o_part = cv.take(sizeof(double2) * n_sg * kGnChunks), o_stat = cv.take(sizeof(float2) * n_sg);
+  uint8_t* ws = static_cast<uint8_t*>(ctx_workspace(ctx, cv.offset));
+  if (ws == nullptr) return ncm_fail(NCM_ENOMEM, "group_norm: workspace allocation failed");
+  double2* part = reinterpret_cast<double2*>(ws + o_part);
+  float2* stat = reinterpret_cast<float2*>(ws + o_stat);
   Launch _launch(ctx, KID_DECODER_ELEMENTWISE, st);
-  group_norm_kernel<<<static_cast<int>(batch * groups), 256, 0, st>>>(x, y, static_cast<int>(T), static_cast<int>(C),
-                                                                      groups, eps);
+  const bool vec = (C / groups) % 4 == 0 && al16(x) && al16(y);
+  if (vec)
+    group_norm_partial_kernel<true><<<dim3(n_sg, kGnChunks), 256, 0, st>>>(x, static_cast<int>(T),
+                                                                           static_cast<int>(C), groups, part);
+  else
+    group_norm_partial_kernel<false><<<dim3(n_sg, kGnChunks), 256, 0, st>>>(x, static_cast<int>(T),
+                                                                            static_cast<int>(C), groups, part);
+  group_norm_stats_kernel<<<blocks_of(n_sg, 256), 256, 0, st>>>(part, n_sg, T * (C / groups), eps, stat);
+  const long long n = batch * T * C;
+  if (vec)
+    group_norm_apply_kernel<true><<<blocks_of(n / 4, 256), 256, 0, st>>>(x, y, n, static_cast<int>(T),
+                                                                         static_cast<int>(C), groups, stat);
+  else
+    group_norm_apply_kernel<false><<<blocks_of(n, 256), 256, 0, st>>>(x, y, n, static_cast<int>(T),
+                                                                      static_cast<int>(C), groups, stat);
   NCM_CUDA_TRY(cudaGetLastError());
   return NCM_OK;
 }
@@ -349,7 +417,8 @@ int ncm_ema_code_stats(ncm_ctx_t* ctx, const float* u, const int32_t* codes, flo
   if (!u || !codes || !counts || !sums) return ncm_fail(NCM_EINVAL, "ema_code_stats: null buffer");
   if (!al16(u) || !al16(sums)) return ncm_fail(NCM_EINVAL, "ema_code_stats: u and sums must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int chunk = 4096;
+  // about 256 chunks (one scatter warp each), at least 256 rows per chunk
+  const int chunk = static_cast<int>(std::max<int64_t>(256, ((N + 255) / 256 + 31) / 32 * 32));
   const int nchunks = static_cast<int>((N + chunk - 1) / chunk);
   WsCarver cv;
   const size_t o_hist = cv.take(sizeof(int) * K), o_start = cv.take(sizeof(int) * (K + 1));

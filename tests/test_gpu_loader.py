@@ -1,7 +1,8 @@
 """Device-side safetensors loading (ncm_load_tensor_bf16): BF16 tensors
 arrive bit for bit; F16 and F32 arrive rounded to bf16 with the bf16
 package's rule (checked against the oracle's restatement of
-packages/bf16/root.zig:17-31). Sizes span several 8 MiB staging chunks."""
+packages/bf16/root.zig:17-31). Sizes span several 16 MiB staging chunks (each read
+by four threads)."""
 import time
 
 import numpy as np
@@ -17,7 +18,7 @@ pytestmark = pytest.mark.gpu
 def test_load_bf16_f16_f32(orc, cuda_dev, tmp_path):
     from ncmorph_b200 import loader
     rng = np.random.default_rng(3)
-    n_big = 3 * (8 << 20) // 2 + 12345            # bf16 tensor spanning 4 chunks, ragged tail
+    n_big = 3 * (16 << 20) // 2 + 12345           # bf16 tensor spanning 4 chunks, ragged tail
     bf = rng.integers(0, 1 << 16, size=n_big, dtype=np.uint16)
     f16 = rng.standard_normal(1 << 20).astype(np.float16)
     f16[:4] = [np.inf, -np.inf, 0.0, -0.0]
