@@ -74,6 +74,29 @@ def config_dict(a, world):
 
 
 # ---------------------------------------------------------------- clocks
+_RESULT_FD = None
+
+
+def _claim_stdout():
+    """The JSON result line is the only thing this program writes to stdout:
+    library and runtime messages (NCCL's version banner, warnings) that would
+    go to file descriptor 1 are sent to stderr instead."""
+    global _RESULT_FD
+    if _RESULT_FD is None:
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -89,9 +112,17 @@ class ClockSampler:
             self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # the first sample lands before the timed region starts, so even a short
+        # region (a few 30 ms steps at 8 GPUs) is covered by the sampling loop
+        t0 = time.time()
+        while time.time() - t0 < 2.0 and self.proc.poll() is None:
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.01)
 
     def stop(self):
         if self.proc is None:
@@ -185,7 +216,7 @@ def run_reference(a):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -341,7 +372,7 @@ def run_ours(a):
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -761,11 +792,12 @@ def run_secondary(a):
                          "other_ms_per_step": prof["*"][0] / a.steps},
             "gpu_launches": int(ln_n + at_n + prof["*"][1]), "clocks": clocks})
     ndev.sync(dev)
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
 def main():
+    _claim_stdout()
     a = parse_args()
     if a.workload != "rvq":
         return run_secondary(a)
