@@ -67,7 +67,8 @@ def config_dict(a, world):
         "codebook_size": a.codes,
         "rows_per_gpu": a.rows // world,
         "parallelism": f"row-sharded x{world}, codebooks replicated",
-        "collective": "NCCL all_gather of codes and bf16 reconstructions" if world > 1 else "none (1 GPU)",
+        "collective": ("NCCL all_gather of codes and bf16 reconstructions, on a second stream overlapping the "
+                       "next step's encode") if world > 1 else "none (1 GPU)",
         "l2": "inputs exceed L2 (bf16 rows 2 GiB/N, f32 residual 4 GiB/N); codebooks (32 MiB/level) stay L2-resident by design",
         "data": "synthetic seeded N(0,1) rows, N(0,0.6^l) codebooks",
     }
@@ -252,7 +253,8 @@ def run_ours(a):
     lib = _lib.load()
     if world > 1:
         from ncmorph_b200.sharded import ShardedEncoder
-        encoder = ShardedEncoder(cbs, a.rows, torch.bfloat16, sq)
+        # batches stream: a step's all-gathers overlap the next step's encode
+        encoder = ShardedEncoder(cbs, a.rows, torch.bfloat16, sq, overlap=True)
     result = {}
 
     def step():
@@ -273,7 +275,10 @@ def run_ours(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(fn, steps):
+    def timed(fn, steps, finish=None):
+        """Device time per step, max over ranks; finish() makes the current
+        stream wait for work the steps left on other streams, so the closing
+        event covers it."""
         barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -281,6 +286,8 @@ def run_ours(a):
         e0.record()
         for _ in range(steps):
             fn()
+        if finish is not None:
+            finish()
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -296,7 +303,7 @@ def run_ours(a):
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
-    ms = timed(step, a.steps)
+    ms = timed(step, a.steps, encoder.wait if world > 1 else None)
     clocks = sampler.stop() if sampler else None
     lib.ncm_profile_enable(ctx, 0)
     tot = ctypes.c_double()
@@ -320,17 +327,52 @@ def run_ours(a):
     codes_host = torch.empty((L, a.rows), dtype=torch.int32).pin_memory()
     recon_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory() if world == 1 else None
 
-    def step_e2e():
-        if world == 1:
+    if world == 1:
+        def step_e2e():
             vq.rvq_encode_host(x_host, cbs, sq, codes_host=codes_host, recon_host=recon_host)
-        else:
-            x.copy_(x_host, non_blocking=True)
-            step()
-            codes_host.copy_(result["codes"], non_blocking=True)
+        finish_e2e = None
+    else:
+        # streaming batches: step i+1's rows are copied in on a second stream
+        # (into the other of two row buffers) and step i's gathered codes are
+        # copied out on a third, while the encode and its all-gathers proceed
+        cp, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        xbuf = [x, torch.empty_like(x)]
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        consumed = [torch.cuda.Event(), torch.cuda.Event()]
+        st = {"i": 0, "n": 1}
+
+        def step_e2e():
+            i = st["i"]
+            b = i & 1
+            cur = torch.cuda.current_stream()
+            if i == 0:
+                with torch.cuda.stream(cp):
+                    cp.wait_stream(cur)
+                    xbuf[0].copy_(x_host, non_blocking=True)
+                    copied[0].record(cp)
+            if i + 1 < st["n"]:
+                with torch.cuda.stream(cp):  # the next step's rows
+                    if i >= 1:
+                        cp.wait_event(consumed[b ^ 1])
+                    xbuf[b ^ 1].copy_(x_host, non_blocking=True)
+                    copied[b ^ 1].record(cp)
+            cur.wait_event(copied[b])
+            codes_d, _ = encoder(xbuf[b])
+            consumed[b].record(cur)
+            with torch.cuda.stream(d2h):
+                encoder.wait()
+                codes_host.copy_(codes_d, non_blocking=True)
+            st["i"] = i + 1
+
+        def finish_e2e():
+            torch.cuda.current_stream().wait_stream(d2h)
+            torch.cuda.current_stream().wait_stream(cp)
 
     step_e2e()
     torch.cuda.synchronize()
-    ms_e2e = timed(step_e2e, a.steps)
+    if world > 1:
+        st.update(i=0, n=a.steps)
+    ms_e2e = timed(step_e2e, a.steps, finish_e2e)
     ndev.sync(dev)
 
     value = a.rows / (ms * 1e-3)
@@ -360,7 +402,8 @@ def run_ours(a):
         "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": ms_e2e, "h2d_bytes_per_step": n * D * 2,
                 "d2h_bytes_per_step": int(codes_host.numel() * 4 + (recon_host.numel() * 2 if recon_host is not None else 0)),
                 "path": "ncm_rvq_encode_host (chunked H2D/encode/D2H pipeline)" if world == 1
-                        else "H2D rows, sharded encode, NCCL all-gather, D2H codes"},
+                        else ("H2D rows (next step's on a copy stream), sharded encode, NCCL all-gather on a "
+                              "second stream, D2H codes on a third")},
         "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",

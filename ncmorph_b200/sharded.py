@@ -39,10 +39,16 @@ class ShardedEncoder:
     ([L, n] int32 and [n, D]); it defaults to the tcgen05 path
     (ncmorph_b200.vq.rvq_encode). Buffers are allocated once; the tensors a
     call returns are views of them, valid until the next call.
+
+    overlap=True streams batches: the all-gathers of a call run on a second
+    stream while the next call already encodes (two buffer sets, so results
+    stay valid until the call after next). Call `wait()` before the current
+    stream reads a call's results; a device-wide synchronize also covers them.
     """
 
     def __init__(self, codebooks: torch.Tensor, total_rows: int, x_dtype: torch.dtype = torch.bfloat16,
-                 sqnorms: torch.Tensor | None = None, group=None, encode: Callable | None = None):
+                 sqnorms: torch.Tensor | None = None, group=None, encode: Callable | None = None,
+                 overlap: bool = False):
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.group = group
@@ -54,30 +60,61 @@ class ShardedEncoder:
         L, D = codebooks.shape[0], codebooks.shape[-1]
         dev = codebooks.device
         self.L = L
-        self.codes_pad = torch.zeros((L, self.n), dtype=torch.int32, device=dev)
-        self.recon_pad = torch.zeros((self.n, D), dtype=x_dtype, device=dev)
+        self.overlap = overlap
+        sets = 2 if overlap else 1
+        self.codes_pad = [torch.zeros((L, self.n), dtype=torch.int32, device=dev) for _ in range(sets)]
+        self.recon_pad = [torch.zeros((self.n, D), dtype=x_dtype, device=dev) for _ in range(sets)]
         # outputs concatenated along dim 0 (the layout every backend accepts)
-        self.codes_all = torch.empty((self.world * L, self.n), dtype=torch.int32, device=dev)
-        self.recon_all = torch.empty((self.world * self.n, D), dtype=x_dtype, device=dev)
+        self.codes_all = [torch.empty((self.world * L, self.n), dtype=torch.int32, device=dev) for _ in range(sets)]
+        self.recon_all = [torch.empty((self.world * self.n, D), dtype=x_dtype, device=dev) for _ in range(sets)]
+        self.codes_out = [torch.empty((L, self.world * self.n), dtype=torch.int32, device=dev) for _ in range(sets)]
+        self.calls = 0
+        if overlap:
+            self.comm = torch.cuda.Stream(device=dev)
+            self.encoded = [torch.cuda.Event() for _ in range(sets)]
+            self.gathered = [torch.cuda.Event() for _ in range(sets)]
+            self.used = [False] * sets
 
     @property
     def rows(self) -> int:
         return self.stop - self.start
 
+    def _gather(self, b: int) -> None:
+        dist.all_gather_into_tensor(self.codes_all[b], self.codes_pad[b], group=self.group)
+        dist.all_gather_into_tensor(self.recon_all[b], self.recon_pad[b], group=self.group)
+        self.codes_out[b].view(self.L, self.world, self.n).copy_(
+            self.codes_all[b].view(self.world, self.L, self.n).permute(1, 0, 2))
+
+    def wait(self) -> None:
+        """Makes the current stream wait for the last call's all-gathers (overlap mode)."""
+        if self.overlap and self.calls > 0:
+            torch.cuda.current_stream().wait_event(self.gathered[(self.calls - 1) & 1])
+
     def __call__(self, x_local: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         valid = self.rows
         if x_local.shape[0] != valid:
             raise ValueError(f"rank {self.rank} owns rows [{self.start}, {self.stop}) but got {x_local.shape[0]}")
+        b = self.calls & 1 if self.overlap else 0
+        cur = torch.cuda.current_stream() if self.overlap else None
+        if self.overlap and self.used[b]:
+            cur.wait_event(self.gathered[b])  # this buffer set's previous gathers have finished
         if valid == self.n:
-            self.encode(x_local, self.codebooks, self.sqnorms, self.codes_pad, self.recon_pad)
+            self.encode(x_local, self.codebooks, self.sqnorms, self.codes_pad[b], self.recon_pad[b])
         elif valid > 0:  # short last shard: encode into dense buffers, then pad
             codes = torch.empty((self.L, valid), dtype=torch.int32, device=x_local.device)
-            self.encode(x_local, self.codebooks, self.sqnorms, codes, self.recon_pad[:valid])
-            self.codes_pad[:, :valid] = codes
-        dist.all_gather_into_tensor(self.codes_all, self.codes_pad, group=self.group)
-        dist.all_gather_into_tensor(self.recon_all, self.recon_pad, group=self.group)
-        codes = self.codes_all.view(self.world, self.L, self.n).permute(1, 0, 2).reshape(self.L, -1)
-        return codes[:, : self.total], self.recon_all[: self.total]
+            self.encode(x_local, self.codebooks, self.sqnorms, codes, self.recon_pad[b][:valid])
+            self.codes_pad[b][:, :valid] = codes
+        if self.overlap:
+            self.encoded[b].record(cur)
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(self.encoded[b])
+                self._gather(b)
+                self.gathered[b].record(self.comm)
+            self.used[b] = True
+        else:
+            self._gather(b)
+        self.calls += 1
+        return self.codes_out[b][:, : self.total], self.recon_all[b][: self.total]
 
 
 def sharded_encode(x_local: torch.Tensor, codebooks: torch.Tensor, total_rows: int,
@@ -87,7 +124,7 @@ def sharded_encode(x_local: torch.Tensor, codebooks: torch.Tensor, total_rows: i
     recon [total_rows, D]) on every rank."""
     enc = ShardedEncoder(codebooks, total_rows, x_local.dtype, sqnorms, group, encode)
     codes, recon = enc(x_local)
-    return codes.contiguous(), recon
+    return codes, recon
 
 
 # ---------------------------------------------------------------- C ABI form

@@ -45,3 +45,59 @@ def test_sharded_encode_capi_two_gpus(tmp_path):
             pytest.fail("sharded encode did not finish within 240 s")
     for r in range(2):
         assert (tmp_path / f"rank{r}").read_text() == "ok"
+
+
+def _worker_overlap(rank, nranks, port, n_local, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    from ncmorph_b200 import sharded, vq
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=rank, world_size=nranks, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        N, D, K, L = n_local * nranks, 256, 1024, 3
+        g = torch.Generator(device=dev).manual_seed(6)
+        xs = [torch.randn((N, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+        cbs = torch.randn((L, K, D), generator=g, device=dev).to(torch.bfloat16)
+        enc = sharded.ShardedEncoder(cbs, N, overlap=True)
+        ok = True
+        # three calls: both buffer sets, the first one reused by the third call
+        outs = [enc(x[rank * n_local:(rank + 1) * n_local].contiguous()) for x in xs]
+        enc.wait()
+        torch.cuda.synchronize(dev)
+        for x, (codes, recon) in zip(xs[1:], outs[1:]):  # the first call's buffers were reused by the third
+            ref_codes, ref_recon, _ = vq.rvq_encode(x, cbs)
+            ok = ok and torch.equal(codes, ref_codes) and torch.equal(recon.view(torch.int16),
+                                                                     ref_recon.view(torch.int16))
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_encoder_overlapped_gathers_two_gpus(tmp_path):
+    """ShardedEncoder(overlap=True): the all-gathers run on a second stream
+    while the next call encodes; results equal a single-GPU encode."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+    import time
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.start_processes(_worker_overlap, args=(2, port, 4096, str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.time() + 240
+    while not ctx.join(timeout=5):
+        if time.time() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("overlapped sharded encode did not finish within 240 s")
+    for r in range(2):
+        assert (tmp_path / f"rank{r}").read_text() == "ok"
