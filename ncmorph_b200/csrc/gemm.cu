@@ -651,6 +651,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <int BN, bool SWAP, bool PAIR>
 constexpr size_t linear_smem_bytes() {
+  static_assert(sizeof(GemmSmem<BN, PAIR>) + 1024 <= 232448, "GEMM shared memory budget");
   return sizeof(GemmSmem<BN, PAIR>) + 1024;
 }
 
