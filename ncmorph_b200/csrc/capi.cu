@@ -255,6 +255,7 @@ int ncm_ctx_destroy(ncm_ctx_t* ctx) {
   cudaDeviceSynchronize();
   comm_release(ctx);
   if (ctx->rvq_counters) cudaFree(ctx->rvq_counters);
+  if (ctx->kpart) cudaFree(ctx->kpart);
   for (int i = 0; i < 2; ++i) {
     if (ctx->load_h[i]) cudaFreeHost(ctx->load_h[i]);
     if (ctx->load_ev[i]) cudaEventDestroy(ctx->load_ev[i]);

@@ -59,6 +59,10 @@ struct LinearArgs {
   int* err;
   int M, N, K;
   int tiles_a, tiles_b;  // tiles along the 128-row operand and the BN operand
+  // split-K (swapped form only): unit = (tile, split); split s sums k-chunks
+  // [s * nk_split, (s + 1) * nk_split) into f32 partials part[s][m][n]
+  int ksplit, nk_split;
+  float* part;
   int a_fast;            // raster: 1 = consecutive tiles walk the A-operand tiles
   int vec_ok;            // y rows are 16-byte aligned (N % 8 == 0)
   int mode;              // 0 plain, 1 SwiGLU (y[M,F]), 2 residual add into y, 3 kernel-3 convolution
@@ -107,6 +111,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int nk = (args.K + BK - 1) / BK;
   const int n_tiles = args.tiles_a * args.tiles_b;
+  const int ksplit = SWAP ? args.ksplit : 1;
+  const int n_units = n_tiles * ksplit;  // unit u: tile u / ksplit, k split u % ksplit
+  auto k_range = [&](int unit, int& k0, int& k1) {
+    if (ksplit == 1) {
+      k0 = 0;
+      k1 = nk;
+      return;
+    }
+    const int sp = unit % ksplit;
+    k0 = sp * args.nk_split;
+    k1 = min(nk, k0 + args.nk_split);
+  };
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 = leader (issues the pair's MMAs)
   const int cid = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int ncl = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
@@ -158,11 +174,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued_parity[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
       bool ok = true;
-      for (int tile = cid; ok && tile < n_tiles; tile += ncl) {
-        int ta, tb;
-        tile_coords(tile, args, ta, tb);
+      for (int unit = cid; ok && unit < n_units; unit += ncl) {
+        int ta, tb, k0, k1;
+        tile_coords(unit / ksplit, args, ta, tb);
+        k_range(unit, k0, k1);
         const int ar = a_row0(ta);
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = k0; kc < k1; ++kc) {
           if (!mbar_wait(&S.empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -223,7 +240,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int tile = cid; ok && tile < n_tiles; tile += ncl) {
+      for (int unit = cid; ok && unit < n_units; unit += ncl) {
+        int k0, k1;
+        k_range(unit, k0, k1);
         const uint32_t b = acc_it & 1u;
         const uint32_t ap = (acc_it >> 1) & 1u;
         if (!mbar_wait(&S.tempty[b], ap ^ 1u, abort_flag)) {
@@ -232,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t dt = tmem + b * BN;
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = k0; kc < k1; ++kc) {
           if (!mbar_wait(&S.full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -244,10 +263,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             if constexpr (PAIR)
               tc_mma_f16_pair(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
-                              (kc | k) != 0 ? 1u : 0u);
+                              (kc != k0 || k != 0) ? 1u : 0u);
             else
               tc_mma_f16(dt, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
-                         (kc | k) != 0 ? 1u : 0u);
+                         (kc != k0 || k != 0) ? 1u : 0u);
           }
           // the stage is free again (in both CTAs of a pair)
           if constexpr (PAIR)
@@ -280,9 +299,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int c0 = ((warp - 2) >> 2) * 16;  // first 16-column chunk of this warp; chunks step by 32
     uint32_t acc_it = 0;
     bool ok = true;
-    for (int tile = cid; tile < n_tiles; tile += ncl) {
+    for (int unit = cid; unit < n_units; unit += ncl) {
       int ta, tb;
-      tile_coords(tile, args, ta, tb);
+      tile_coords(unit / ksplit, args, ta, tb);
       const uint32_t b = acc_it & 1u;
       const uint32_t ap = (acc_it >> 1) & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(&S.tfull[b], ap, abort_flag))) {  // warp-uniform: TMEM loads follow
@@ -603,7 +622,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else {
           // arow = output n, columns = tokens m
           const int n = arow;
-          if (n < args.N) {
+          if (n < args.N && ksplit > 1) {
+            // split-K: this split's f32 partial sums (bias and output in linear_ksplit_reduce_kernel)
+            float* pp = args.part + static_cast<size_t>(unit % ksplit) * args.M * args.N + n;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = tb * BN + c + j;
+              if (m < args.M) pp[static_cast<size_t>(m) * args.N] = __uint_as_float(v[j]);
+            }
+          } else if (n < args.N) {
             const float bv = args.bias != nullptr ? bf16_to_f32(__ldg(args.bias + n)) : 0.f;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -779,6 +806,45 @@ int launch_shape(ncm_ctx* ctx, const GemmShape& sh, const void* A, int64_t a_row
   return NCM_OK;
 }
 
+// y[m][n] = bf16(sum_s part[s][m][n] + bias[n]) in split order (mode 2:
+// y = bf16(y + bf16(sum + bias)); f32 outputs when y_f32 is given): the
+// epilogue of the split-K skinny GEMM, one thread per output.
+__global__ void __launch_bounds__(256) linear_ksplit_reduce_kernel(const float* __restrict__ part, int ksplit,
+                                                                   int M, int N, const uint16_t* __restrict__ bias,
+                                                                   uint16_t* __restrict__ y, float* __restrict__ y_f32,
+                                                                   int mode) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long MN = static_cast<long long>(M) * N;
+  if (i >= MN) return;
+  float acc = part[i];
+  for (int s = 1; s < ksplit; ++s) acc += part[s * MN + i];
+  if (bias != nullptr) acc += bf16_to_f32(__ldg(bias + i % N));
+  if (mode == 2) acc = bf16_to_f32(f32_to_bf16(acc)) + bf16_to_f32(y[i]);
+  if (y_f32 != nullptr)
+    y_f32[i] = acc;
+  else
+    y[i] = f32_to_bf16(acc);
+}
+
+// The context's split-K partial buffer, grown on demand (freeing the old one
+// waits for the device, so no launch still uses it).
+float* ksplit_buffer(ncm_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->kpart_bytes) return ctx->kpart;
+  if (ctx->kpart != nullptr) {
+    cudaFree(ctx->kpart);
+    ctx->kpart = nullptr;
+    ctx->kpart_bytes = 0;
+  }
+  const size_t want = std::max<size_t>(bytes, size_t(8) << 20);
+  if (cudaMalloc(&ctx->kpart, want) != cudaSuccess) {
+    cudaGetLastError();
+    ctx->kpart = nullptr;
+    return nullptr;
+  }
+  ctx->kpart_bytes = want;
+  return ctx->kpart;
+}
+
 }  // namespace
 
 int linear_bf16(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* y, float* y_f32,
@@ -815,7 +881,25 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
   a.tiles_a = ceil_div(N, BM);
   a.tiles_b = ceil_div(M, bn);
   a.a_fast = 1;
-  const int grid = std::min(a.tiles_a * a.tiles_b, ctx->num_sms);
+  // Few tiles (decode-time GEMV shapes): split K so that about one unit per SM
+  // streams its share of W, each split at least four 64-wide k-chunks; f32
+  // partials, summed in split order by linear_ksplit_reduce_kernel (the sum
+  // order differs from one accumulator's: within the f32-accumulation bar).
+  const int nk = ceil_div(K, BK);
+  const int tiles = a.tiles_a * a.tiles_b;
+  a.ksplit = 1;
+  if (mode == 0 || mode == 2) {
+    const int want = std::min(ctx->num_sms / std::max(tiles, 1), nk / 4);
+    if (want >= 3) {  // at least three times the CTAs, or the extra reduce pass does not pay
+      a.nk_split = ceil_div(nk, want);
+      a.ksplit = ceil_div(nk, a.nk_split);
+    }
+  }
+  if (a.ksplit > 1) {
+    a.part = ksplit_buffer(ctx, sizeof(float) * a.ksplit * static_cast<size_t>(M) * N);
+    if (a.part == nullptr) return ncm_fail(NCM_ENOMEM, "linear: split-K buffer allocation failed");
+  }
+  const int grid = std::min(tiles * a.ksplit, ctx->num_sms);
   cudaError_t e;
   Launch _launch(ctx, KID_LINEAR, stream);
   switch (bn) {
@@ -824,6 +908,12 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
     default: e = launch_linear<64, true, false>(tmA, tmB, a, grid, stream); break;
   }
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
+  if (a.ksplit > 1) {
+    const long long mn = M * N;
+    linear_ksplit_reduce_kernel<<<static_cast<unsigned>((mn + 255) / 256), 256, 0, stream>>>(
+        a.part, a.ksplit, static_cast<int>(M), static_cast<int>(N), bias, y, y_f32, mode);
+    NCM_CUDA_TRY(cudaGetLastError());
+  }
   return NCM_OK;
 }
 

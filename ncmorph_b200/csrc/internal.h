@@ -66,6 +66,10 @@ struct ncm_ctx {
   // split-fixup arrival counters of the RVQ argmin kernel (kept zero between launches)
   int* rvq_counters = nullptr;
   int64_t rvq_counter_len = 0;
+  // f32 partial sums of the split-K skinny GEMM (its own buffer: the callers'
+  // activations may live in the workspace, which must not move under them)
+  float* kpart = nullptr;
+  size_t kpart_bytes = 0;
   // pinned staging buffers and their events of the checkpoint loader (first use)
   void* load_h[2] = {nullptr, nullptr};
   cudaEvent_t load_ev[2] = {nullptr, nullptr};
