@@ -257,6 +257,24 @@ def test_ncm_forward_small_matches_oracle(orc, cuda_dev, mask, prefix, levels):
     assert frac_bad == 0.0
 
 
+def test_ncm_forward_decode_size_split_k_matches_oracle(orc, cuda_dev):
+    """40 positions (at most 64 rows: the swapped GEMM form) and a width that
+    makes the projections split K, so the f32 partial reduction carries the
+    bias, the residual adds and the output rounding."""
+    from ncmorph_b200 import ncm_model
+    cfg = ncm_model.Config(hidden_size=1024, vq_width=64, num_attention_heads=16, num_key_value_heads=4,
+                           intermediate_size=2048, level_lengths=(8, 16, 16), prefix_length=0, mask="block_causal")
+    w = _rand_weights(cfg, cuda_dev, 7, layers=2)
+    rng = np.random.default_rng(8)
+    inputs = gen_bf16(rng, (cfg.seq_len, cfg.vq_width))
+    out = ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(out))
+    ref = oracle_ncm_forward(orc, cfg, w, inputs)
+    err = np.abs(got - ref)
+    rms = np.sqrt((ref ** 2).mean(axis=1, keepdims=True))
+    assert (err > 3e-2 * np.abs(ref) + 3e-2 * rms).mean() == 0.0, err.max()
+
+
 def test_ncm_forward_post_upsample_convs_match_oracle(orc, cuda_dev):
     """weights.post_upsample_convs (ncm_model.zig:141-153): each level's input
     rows pass through x + bias + Conv1d_k3(x) with that level's kernel first."""
