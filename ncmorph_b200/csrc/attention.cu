@@ -243,6 +243,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // the prologue above overlaps the previous kernel's tail (programmatic launch)
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t tmem = S.tmem_base;  // S_i at columns 128 i, O_i at 256 + 64 i
   volatile int* abort_flag = &S.abort_flag;
 
@@ -546,8 +549,8 @@ int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const 
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int n_qp = (T + 2 * AT_Q - 1) / (2 * AT_Q);
-  attention2_bf16_kernel<<<n_qp * H, AT_THREADS, ATTN2_SMEM, stream>>>(tq, tk, tv, a);
-  NCM_CUDA_TRY(cudaGetLastError());
+  NCM_CUDA_TRY(launch_pdl(attention2_bf16_kernel, dim3(n_qp * H), dim3(AT_THREADS), ATTN2_SMEM, stream, 1, tq, tk, tv,
+                          a));
   return NCM_OK;
 }
 

@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(256) rms_norm_bf16_kernel(const uint16_t* __re
                                                             const uint16_t* __restrict__ bias,
                                                             uint16_t* __restrict__ y, int rows, int width,
                                                             float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -222,14 +224,13 @@ cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* w, const uin
                                  int width, float eps, cudaStream_t st) {
   const int blocks = (rows + 7) / 8;
   if (width <= 1024)
-    rms_norm_bf16_kernel<4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+    return launch_pdl(rms_norm_bf16_kernel<4>, dim3(blocks), dim3(256), 0, st, 1, x, w, b, y, rows, width, eps);
   else if (width <= 2048)
-    rms_norm_bf16_kernel<8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+    return launch_pdl(rms_norm_bf16_kernel<8>, dim3(blocks), dim3(256), 0, st, 1, x, w, b, y, rows, width, eps);
   else if (width <= 4096)
-    rms_norm_bf16_kernel<16><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
+    return launch_pdl(rms_norm_bf16_kernel<16>, dim3(blocks), dim3(256), 0, st, 1, x, w, b, y, rows, width, eps);
   else
-    rms_norm_bf16_kernel<0><<<blocks, 256, 0, st>>>(x, w, b, y, rows, width, eps);
-  return cudaGetLastError();
+    return launch_pdl(rms_norm_bf16_kernel<0>, dim3(blocks), dim3(256), 0, st, 1, x, w, b, y, rows, width, eps);
 }
 
 cudaError_t launch_rope_bf16(uint16_t* qkv, long long stride, int T, int heads_qk, const float* c, const float* s,

@@ -156,6 +156,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // a pair's barriers must be initialised in both CTAs before either signals the other
   if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
+  // the prologue above overlaps the previous kernel's tail (programmatic launch)
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort_flag = &S.abort_flag;
   auto abort_all = [&]() {
@@ -712,20 +715,8 @@ cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
   cudaError_t e = linear_prepare<BN, SWAP, PAIR>();
   if (e != cudaSuccess) return e;
   constexpr size_t smem = linear_smem_bytes<BN, SWAP, PAIR>();
-  if constexpr (PAIR) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute at[1] = {pair_cluster_attr()};
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, linear_bf16_kernel<BN, SWAP, PAIR>, tmA, tmB, a);
-  } else {
-    linear_bf16_kernel<BN, SWAP, PAIR><<<grid, THREADS, smem, stream>>>(tmA, tmB, a);
-    return cudaGetLastError();
-  }
+  return launch_pdl(linear_bf16_kernel<BN, SWAP, PAIR>, dim3(grid), dim3(THREADS), smem, stream, PAIR ? 2 : 1, tmA,
+                    tmB, a);
 }
 
 // How many 2-CTA clusters of the 256-wide pair kernel fit at once (cluster
@@ -813,6 +804,8 @@ __global__ void __launch_bounds__(256) linear_ksplit_reduce_kernel(const float* 
                                                                    int M, int N, const uint16_t* __restrict__ bias,
                                                                    uint16_t* __restrict__ y, float* __restrict__ y_f32,
                                                                    int mode) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long MN = static_cast<long long>(M) * N;
   if (i >= MN) return;
@@ -910,9 +903,9 @@ int linear_bf16_ex(ncm_ctx* ctx, const uint16_t* x, const uint16_t* w, const uin
   if (e != cudaSuccess) return ncm_set_cuda_error(e);
   if (a.ksplit > 1) {
     const long long mn = M * N;
-    linear_ksplit_reduce_kernel<<<static_cast<unsigned>((mn + 255) / 256), 256, 0, stream>>>(
-        a.part, a.ksplit, static_cast<int>(M), static_cast<int>(N), bias, y, y_f32, mode);
-    NCM_CUDA_TRY(cudaGetLastError());
+    NCM_CUDA_TRY(launch_pdl(linear_ksplit_reduce_kernel, dim3(static_cast<unsigned>((mn + 255) / 256)), dim3(256), 0,
+                            stream, 1, static_cast<const float*>(a.part), a.ksplit, static_cast<int>(M),
+                            static_cast<int>(N), bias, y, y_f32, mode));
   }
   return NCM_OK;
 }

@@ -99,6 +99,33 @@ class Launch {
 };
 
 // Carves consecutive 256-byte-aligned regions out of the context workspace.
+// Launch with the programmatic stream-serialization attribute (and a cluster
+// dimension when cluster_x > 1): the kernel may begin while its predecessor on
+// the stream drains; it calls pdl_wait() before touching that predecessor's data.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = cluster_x;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 struct WsCarver {
   size_t offset = 0;
   size_t take(size_t bytes) {
