@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // a pair's barriers must be initialised in both CTAs before either signals the other
   if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
+  // the prologue above overlaps the previous kernel's tail (programmatic launch)
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort_flag = &S.abort_flag;
   auto abort_all = [&]() {
@@ -570,6 +573,8 @@ struct ApplyArgs {
 };
 
 __global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.N) return;
@@ -650,6 +655,8 @@ __global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
 // exact for any realistic D, so the f32 result does not depend on order.
 __global__ void __launch_bounds__(256) code_sqnorm_kernel(const uint16_t* __restrict__ cb, float* __restrict__ out,
                                                           int K, int D) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int k = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (k >= K) return;
@@ -672,6 +679,8 @@ __global__ void __launch_bounds__(256) rvq_decode_kernel(const int32_t* __restri
                                                          uint16_t* __restrict__ out_bf16,
                                                          float* __restrict__ out_f32, int N, int D, int K,
                                                          int* err) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= N) return;
@@ -707,6 +716,8 @@ __global__ void __launch_bounds__(256) rvq_decode_kernel(const int32_t* __restri
 __global__ void __launch_bounds__(256) pool_avg_kernel(const float* __restrict__ x, float* __restrict__ y,
                                                        uint16_t* __restrict__ y_bf16, long long rows_out, int D,
                                                        int f) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int d4 = D / 4;
   if (idx >= rows_out * d4) return;
@@ -743,6 +754,8 @@ __global__ void __launch_bounds__(256) scale_advance_kernel(const int32_t* __res
                                                             float* __restrict__ u_next,
                                                             uint16_t* __restrict__ u_next_bf16, long long rows_pooled,
                                                             int D, int K, int f, int g, int update_r, int* err) {
+  pdl_wait();
+  pdl_launch_dependents();
   // one warp per (pooled row, 128-channel chunk)
   const int nch = (D + 127) / 128;
   const long long wg = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -834,6 +847,8 @@ struct ReconArgs {
 };
 __global__ void __launch_bounds__(256) multiscale_recon_kernel(const ReconArgs a, uint16_t* __restrict__ out,
                                                                long long rows, int D) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int d4 = D / 4;
   if (idx >= rows * d4) return;
@@ -853,6 +868,8 @@ __global__ void __launch_bounds__(256) multiscale_recon_kernel(const ReconArgs a
 // ------------------------------------------------------------ casts (L7)
 __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ y,
                                                           long long n) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i + 3 < n) {
     const float4 v = *reinterpret_cast<const float4*>(x + i);
@@ -864,6 +881,8 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
 
 __global__ void __launch_bounds__(256) bf16_to_f32_kernel(const uint16_t* __restrict__ x, float* __restrict__ y,
                                                           long long n) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i + 3 < n) {
     const uint2 v = *reinterpret_cast<const uint2*>(x + i);
@@ -1005,30 +1024,18 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.shadow = fu ? fu->shadow : nullptr;
   a.codebook = fu ? fu->codebook : nullptr;
   a.mul_dev = mul_dev;
-  if (plan.pair) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(plan.grid);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = argmin_smem_bytes<true>();
-    cfg.stream = stream;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, rvq_argmin_kernel<false, true>, tmA, tmB, a);
-    if (e != cudaSuccess) return e;
-  } else if (top2 != nullptr) {
+  if (plan.pair)
+    return launch_pdl(rvq_argmin_kernel<false, true>, dim3(plan.grid), dim3(THREADS), argmin_smem_bytes<true>(),
+                      stream, 2, tmA, tmB, a);
+  if (top2 != nullptr) {
     a.gap = top2->gap;
     a.a2 = top2->a2;
     a.part_d2 = top2->part_d2;
-    rvq_argmin_kernel<true, false><<<plan.grid, THREADS, argmin_smem_bytes<false>(), stream>>>(tmA, tmB, a);
-  } else {
-    rvq_argmin_kernel<false, false><<<plan.grid, THREADS, argmin_smem_bytes<false>(), stream>>>(tmA, tmB, a);
+    return launch_pdl(rvq_argmin_kernel<true, false>, dim3(plan.grid), dim3(THREADS), argmin_smem_bytes<false>(),
+                      stream, 1, tmA, tmB, a);
   }
-  return cudaGetLastError();
+  return launch_pdl(rvq_argmin_kernel<false, false>, dim3(plan.grid), dim3(THREADS), argmin_smem_bytes<false>(), stream,
+                    1, tmA, tmB, a);
 }
 
 cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_t* codes, const uint16_t* src_bf16,
@@ -1053,41 +1060,35 @@ cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_
   a.D = static_cast<int>(D);
   a.K = static_cast<int>(K);
   a.update = update ? 1 : 0;
-  rvq_apply_kernel<<<ceil_div(N, 8), 256, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(rvq_apply_kernel, dim3(ceil_div(N, 8)), dim3(256), 0, stream, 1, a);
 }
 
 cudaError_t launch_code_sqnorm(const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D, cudaStream_t stream) {
-  code_sqnorm_kernel<<<ceil_div(K, 8), 256, 0, stream>>>(codebook, sqnorm, static_cast<int>(K),
-                                                         static_cast<int>(D));
-  return cudaGetLastError();
+  return launch_pdl(code_sqnorm_kernel, dim3(ceil_div(K, 8)), dim3(256), 0, stream, 1, codebook, sqnorm,
+                    static_cast<int>(K), static_cast<int>(D));
 }
 
 cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, int L, uint16_t* recon_bf16,
                               float* recon_f32, int64_t N, int64_t D, int64_t K, int* err, cudaStream_t stream) {
-  rvq_decode_kernel<<<ceil_div(N, 8), 256, 0, stream>>>(codes, codebooks, L, recon_bf16, recon_f32,
-                                                        static_cast<int>(N), static_cast<int>(D),
-                                                        static_cast<int>(K), err);
-  return cudaGetLastError();
+  return launch_pdl(rvq_decode_kernel, dim3(ceil_div(N, 8)), dim3(256), 0, stream, 1, codes, codebooks, L, recon_bf16,
+                    recon_f32, static_cast<int>(N), static_cast<int>(D), static_cast<int>(K), err);
 }
 
 cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t B, int64_t T, int64_t D, int f,
                             cudaStream_t stream) {
   const long long rows_out = B * (T / f);
   const long long threads = rows_out * (D / 4);
-  pool_avg_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, y_bf16, rows_out,
-                                                                                   static_cast<int>(D), f);
-  return cudaGetLastError();
+  return launch_pdl(pool_avg_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, 1, x, y,
+                    y_bf16, rows_out, static_cast<int>(D), f);
 }
 
 cudaError_t launch_scale_advance(const int32_t* codes, const uint16_t* codebooks, int L, float* resid, float* q_out,
                                  float* u_next, uint16_t* u_next_bf16, int64_t rows_pooled, int64_t D, int64_t K, int f,
                                  int g, bool update_r, int* err, cudaStream_t stream) {
   const long long warps = rows_pooled * ((D + 127) / 128);
-  scale_advance_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
-      codes, codebooks, L, resid, q_out, u_next, u_next_bf16, rows_pooled, static_cast<int>(D), static_cast<int>(K), f,
-      g, update_r ? 1 : 0, err);
-  return cudaGetLastError();
+  return launch_pdl(scale_advance_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, stream, 1, codes,
+                    codebooks, L, resid, q_out, u_next, u_next_bf16, static_cast<long long>(rows_pooled),
+                    static_cast<int>(D), static_cast<int>(K), f, g, update_r ? 1 : 0, err);
 }
 
 cudaError_t launch_multiscale_recon(const float* const* q, const int* f, int S, uint16_t* out, int64_t rows, int64_t D,
@@ -1099,23 +1100,22 @@ cudaError_t launch_multiscale_recon(const float* const* q, const int* f, int S, 
     a.f[s] = f[s];
   }
   const long long threads = rows * (D / 4);
-  multiscale_recon_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(a, out, rows,
-                                                                                           static_cast<int>(D));
-  return cudaGetLastError();
+  return launch_pdl(multiscale_recon_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, 1,
+                    a, out, static_cast<long long>(rows), static_cast<int>(D));
 }
 
 cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t stream) {
   const long long threads = (n + 3) / 4;
   if (threads == 0) return cudaSuccess;
-  f32_to_bf16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, n);
-  return cudaGetLastError();
+  return launch_pdl(f32_to_bf16_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, 1, x,
+                    y, static_cast<long long>(n));
 }
 
 cudaError_t launch_bf16_to_f32(const uint16_t* x, float* y, int64_t n, cudaStream_t stream) {
   const long long threads = (n + 3) / 4;
   if (threads == 0) return cudaSuccess;
-  bf16_to_f32_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, y, n);
-  return cudaGetLastError();
+  return launch_pdl(bf16_to_f32_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, 1, x,
+                    y, static_cast<long long>(n));
 }
 
 }  // namespace ncm

@@ -243,3 +243,47 @@ def test_tokenizer_config2_phi_linear_properties(cuda_dev):
         Q = vq.upsample(q.view(B, T // f, D), T, "linear").view(B * T, D)
         acc += vq.conv1d_k3(Q, pw[s], pb[s], segments=[T] * B, alpha=0.5, beta=0.5)
     assert torch.equal(acc.to(torch.bfloat16).view(torch.int16), recon.view(B * T, D).view(torch.int16))
+
+
+def test_streamed_inputs_are_read_after_their_copy(cuda_dev):
+    """Inputs copied in on a second stream (two device buffers; three host
+    inputs cycle, so a buffer holds a different input at each use) and
+    consumed after a cross-stream event wait: every step's codes equal the
+    codes of its own input computed directly.
+    The kernels launch with programmatic stream serialization, which must not
+    let a kernel run ahead of an event the stream waits on."""
+    from ncmorph_b200 import vq
+    B, T, Din, D, K, L = 2, 256, 256, 128, 256, 2
+    factors = [4, 2, 1]
+    g = torch.Generator(device=cuda_dev).manual_seed(11)
+    xs = [torch.randn((B, T, Din), generator=g, device=cuda_dev).to(torch.bfloat16) for _ in range(3)]
+    w_in = (torch.randn((D, Din), generator=g, device=cuda_dev) * 0.05).to(torch.bfloat16)
+    w_out = (torch.randn((Din, D), generator=g, device=cuda_dev) * 0.05).to(torch.bfloat16)
+    cbs = torch.randn((len(factors), L, K, D), generator=g, device=cuda_dev).to(torch.bfloat16)
+    direct = [torch.cat([c.reshape(-1) for c in vq.tokenizer_forward(x, w_in, cbs, w_out, factors)[0]]) for x in xs]
+    hosts = [x.cpu().pin_memory() for x in xs]
+    cur, cp = torch.cuda.current_stream(), torch.cuda.Stream(device=cuda_dev)
+    bufs = [torch.empty_like(xs[0]), torch.empty_like(xs[0])]
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    consumed = [torch.cuda.Event(), torch.cuda.Event()]
+    outs = []
+    steps = 8
+    with torch.cuda.stream(cp):
+        cp.wait_stream(cur)
+        bufs[0].copy_(hosts[0], non_blocking=True)
+        copied[0].record(cp)
+    for i in range(steps):
+        b = i & 1
+        if i + 1 < steps:
+            with torch.cuda.stream(cp):
+                if i >= 1:
+                    cp.wait_event(consumed[b ^ 1])
+                bufs[b ^ 1].copy_(hosts[(i + 1) % 3], non_blocking=True)
+                copied[b ^ 1].record(cp)
+        cur.wait_event(copied[b])
+        codes = vq.tokenizer_forward(bufs[b], w_in, cbs, w_out, factors)[0]
+        consumed[b].record(cur)
+        outs.append(torch.cat([c.reshape(-1) for c in codes]))
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, direct[i % 3]), i
