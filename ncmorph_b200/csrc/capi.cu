@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <vector>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -608,15 +609,33 @@ int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* 
   if (!aligned16(codebooks) || (sqnorms && !aligned16(sqnorms)))
     return ncm_fail(NCM_EINVAL, "rvq_encode_host: device buffers must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Row chunks of about seven full waves of 128-row blocks, so chunking adds
-  // no wave-quantisation loss; two slots of device buffers alternate.
-  const int64_t wave_rows = static_cast<int64_t>(ctx->num_sms) * 128 * 7;
-  const int64_t nchunks = std::max<int64_t>(1, std::min<int64_t>(16, (N + wave_rows - 1) / wave_rows));
-  const int64_t C = ((N + nchunks - 1) / nchunks + 127) / 128 * 128;
-  const RvqPlan plan_c = rvq_plan(ctx->num_sms, C, K, true);
-  size_t part_bytes = plan_c.partial_bytes;
-  const int64_t last_rows = N - (nchunks - 1) * C;
-  if (last_rows > 0) part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, last_rows, K, true).partial_bytes);
+  // Row chunks of about seven full waves of 128-row blocks (one wave = a
+  // 128-row block per SM), so chunking adds no wave-quantisation loss; two
+  // slots of device buffers alternate. A large encode starts and ends with a
+  // two-wave chunk: the first copy in and the last copy out are the only
+  // transfers nothing overlaps.
+  const int64_t wave = static_cast<int64_t>(ctx->num_sms) * 128;
+  std::vector<int64_t> starts;
+  if (N >= 11 * wave) {
+    const int64_t mid = (N - 4 * wave) / (7 * wave);
+    starts.push_back(0);
+    starts.push_back(2 * wave);
+    for (int64_t i = 1; i <= mid; ++i) starts.push_back(2 * wave + i * 7 * wave);
+    if (N - 2 * wave > starts.back()) starts.push_back(N - 2 * wave);  // the remainder, then the last two waves
+  } else {
+    const int64_t nchunks = std::max<int64_t>(1, std::min<int64_t>(16, (N + 7 * wave - 1) / (7 * wave)));
+    const int64_t c0 = ((N + nchunks - 1) / nchunks + 127) / 128 * 128;
+    for (int64_t r = 0; r < N; r += c0) starts.push_back(r);
+  }
+  starts.push_back(N);
+  const int64_t nchunks = static_cast<int64_t>(starts.size()) - 1;
+  int64_t C = 0;
+  size_t part_bytes = 0;
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int64_t n = starts[c + 1] - starts[c];
+    C = std::max(C, n);
+    part_bytes = std::max(part_bytes, rvq_plan(ctx->num_sms, n, K, true).partial_bytes);
+  }
   WsCarver cv;
   size_t o_x[2], o_codes[2], o_rec[2];
   for (int i = 0; i < 2; ++i) {
@@ -650,8 +669,8 @@ int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const uint16_t* 
   RvqPartial* part = reinterpret_cast<RvqPartial*>(ws + o_part);
   for (int64_t c = 0; c < nchunks; ++c) {
     const int slot = static_cast<int>(c & 1);
-    const int64_t r0 = c * C;
-    const int64_t n = std::min(C, N - r0);
+    const int64_t r0 = starts[c];
+    const int64_t n = starts[c + 1] - r0;
     if (n <= 0) break;
     uint16_t* xd = reinterpret_cast<uint16_t*>(ws + o_x[slot]);
     int32_t* cd = reinterpret_cast<int32_t*>(ws + o_codes[slot]);
