@@ -421,7 +421,7 @@ def run_ours(a):
 
 # ------------------------------------------------- secondary workloads
 # Configs 1-4 are parity cases; these modes measure them on one GPU with the
-# same timing rules (CUDA events, warm-up, clocks) for the records in DESIGN.md.
+# same timing rules (CUDA events, warm-up, clocks) as the headline line.
 
 def _timed_loop(fn, steps, warmup):
     import torch
