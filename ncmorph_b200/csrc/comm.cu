@@ -100,7 +100,8 @@ int ncm_comm_unique_id(uint8_t* id_out) {
 }
 
 int ncm_ctx_comm_init(ncm_ctx_t* ctx, const uint8_t* id, int32_t rank, int32_t nranks) {
-  if (ctx == nullptr || id == nullptr) return ncm_fail(NCM_EINVAL, "comm_init: null argument");
+  if (ctx == nullptr) return ncm_fail(NCM_EINVAL, "null context");
+  if (id == nullptr) return ncm_fail(NCM_EINVAL, "comm_init: null id");
   if (nranks < 1 || rank < 0 || rank >= nranks)
     return ncm_fail(NCM_EINVAL, "comm_init: rank %d outside [0, %d)", rank, nranks);
   const NcclApi& api = nccl();

@@ -88,3 +88,39 @@ def test_sharded_encode_without_communicator_is_rejected():
     from ncmorph_b200 import _lib
     lib = _lib.load()
     assert lib.ncm_rvq_encode_sharded(None, None, None, None, 1, None, None, 1, 8, 1, None) == _lib.NCM_EINVAL
+
+
+def test_every_context_entry_point_rejects_a_null_context():
+    """Each entry point whose first parameter is the context validates it
+    before anything else: a null context returns NCM_EINVAL (no crash, no
+    CUDA call). Run in a child process so a crash cannot take pytest down."""
+    import re
+    import subprocess
+    import sys
+    header = (ROOT / "include" / "ncm_cuda.h").read_text()
+    # ncm_ctx_destroy(NULL) is a no-op that succeeds, as free(NULL) does
+    names = [n for n in re.findall(r"NCM_API int (ncm_\w+)\(ncm_ctx_t\* ctx\b", header) if n != "ncm_ctx_destroy"]
+    assert len(names) >= 30
+    code = r'''
+import ctypes, sys
+from ncmorph_b200 import _lib
+lib = _lib.load()
+bad = []
+for name in sys.argv[1:]:
+    fn = getattr(lib, name)
+    args = []
+    for t in fn.argtypes:
+        if t in (ctypes.c_int32, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32):
+            args.append(1)
+        elif t in (ctypes.c_float, ctypes.c_double):
+            args.append(1.0)
+        else:
+            args.append(None)
+    rc = fn(*args)
+    if rc != _lib.NCM_EINVAL or b"null context" not in (lib.ncm_last_error() or b""):
+        bad.append((name, rc))
+print(bad)
+'''
+    out = subprocess.run([sys.executable, "-c", code, *names], capture_output=True, text=True, cwd=ROOT, timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip() == "[]", out.stdout
