@@ -55,7 +55,12 @@ enum ncm_status {
 /* ------------------------------------------------------------ context */
 
 /* Creates a context on CUDA device `device` (must be compute capability 10.0).
- * Replaces the reference's implicit single-threaded CPU state. */
+ * Replaces the reference's implicit single-threaded CPU state: its kernels
+ * take plain slices and keep nothing between calls
+ * (packages/kernels/root.zig:96-104). The context holds the device, its
+ * workspace, the device error word and, once bound, the NCCL communicator;
+ * ncm_ctx_destroy, ncm_sync and the status and version queries after it have
+ * no reference counterpart of their own. */
 NCM_API int ncm_ctx_create(int device, ncm_ctx_t** out);
 NCM_API int ncm_ctx_destroy(ncm_ctx_t* ctx);
 /* Waits for `stream`, then checks the context's device error word. */
@@ -144,6 +149,9 @@ NCM_API int ncm_rvq_encode_host(ncm_ctx_t* ctx, const uint16_t* x_host, const ui
 
 /* Token rows shard across GPUs with the codebooks replicated; the only
  * exchange is an NCCL all-gather of codes and reconstructions over NVLink.
+ * No counterpart in the reference, which runs on one CPU thread and has no
+ * distributed mode (PROJECT.md:35); each rank's rows follow
+ * vq_forward_semantics.md:59-82 exactly as ncm_rvq_encode does.
  * One context per GPU (one process or thread each). ncm_comm_unique_id
  * fills 128 bytes on one rank, the caller ships them to every rank, and each
  * rank calls ncm_ctx_comm_init (collective; the context owns the
