@@ -491,7 +491,7 @@ def _l2_flusher(dev):
 
 def _event_ms(fn, reps, flush=None):
     """Median CUDA-event time of fn over reps calls; flush() (an L2-sized
-    write) runs before each call, outside the timed window."""
+    read) runs before each call, outside the timed window."""
     import torch
     times = []
     for _ in range(reps):
@@ -629,8 +629,34 @@ def _aux_suite(a, dev, rnd, peaks, peak_kind):
     cbb = torch.empty((K, D), dtype=torch.bfloat16, device=dev)
     ms = _event_ms(lambda: ema.update(u, codes, codebook_bf16=cbb), reps, flush)
     out["ema_stats_and_update"] = {"value": ms, "unit": "ms"}
+
+    # BASELINE config 1, the small RVQ encode: x [4096, 256], 4 levels x K = 1024.
+    # Launch- and latency-bound; reported against both rooflines, eager and as
+    # one CUDA-graph replay, with L2 flushed before every call.
+    N, D, K, L = 4096, 256, 1024, 4
+    x1 = rnd((N, D))
+    decay = torch.tensor([0.5 ** l for l in range(L)], device=dev).view(L, 1, 1)
+    cb1 = (rnd((L, K, D)).float() * decay).to(torch.bfloat16)
+    sq1 = vq.code_sqnorm(cb1)
+    codes1 = torch.empty((L, N), dtype=torch.int32, device=dev)
+    recon1 = torch.empty((N, D), dtype=torch.bfloat16, device=dev)
+    enc = lambda: vq.rvq_encode(x1, cb1, sq1, codes=codes1, recon=recon1)  # noqa: E731
+    flops = 2.0 * L * N * K * D
+    # x read, per level the f32 residual read + written, codes written and the
+    # codebook read, then the bf16 reconstruction written
+    byt = N * D * 2 + L * (N * D * 8 + N * 4 + K * D * 2) + N * D * 2
+    for name, fn in (("rvq_small_eager", enc), ("rvq_small_graph", _graphed(enc, True))):
+        for _ in range(3):
+            fn()
+        ms = _event_ms(fn, reps, flush)
+        tf = flops / (ms * 1e-3) / 1e12
+        gbs = byt / (ms * 1e-3) / 1e9
+        out[name] = {"value": N / (ms * 1e-3), "unit": "vectors/s", "ms": ms, "shape": [N, D, K, L],
+                     "tensor": {"achieved": tf, "peak": tensor, "unit": "TFLOP/s", "frac": tf / tensor},
+                     "hbm": {"achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}}
     return {"metric": "tied_head_logits_tflops", "value": out["tied_head_logits"]["value"], "unit": "TFLOP/s",
-            "config": {"workload": "next-row pieces: tied head, device loader, GroupNorm, level-0 convs, EMA"},
+            "config": {"workload": "next-row pieces: tied head, device loader, GroupNorm, level-0 convs, EMA; "
+                                   "small RVQ encode (BASELINE config 1)"},
             "results": out, "roofline": out["tied_head_logits"]["roofline"],
             "gpu_launches": None}
 

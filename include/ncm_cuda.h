@@ -177,7 +177,8 @@ NCM_API int ncm_pool_avg(ncm_ctx_t* ctx, const float* x, float* y, int64_t B, in
 
 /* Decode (vq_forward_semantics.md:69,82): recon[n,:] = bf16( sum_l e_l[codes[l,n],:] ),
  * summed over l in increasing order in f32. codes [L,N]; codebooks [L,K,D]. A code
- * outside [0,K) makes the call fail with NCM_ERANGE (reported by ncm_sync). */
+ * outside [0,K) makes the call fail with NCM_ERANGE (reported by ncm_sync); the rows
+ * holding one are left unwritten, every other row is decoded. */
 NCM_API int ncm_rvq_decode(ncm_ctx_t* ctx, const int32_t* codes, const uint16_t* codebooks, int32_t L, uint16_t* recon,
                    int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
 

@@ -674,6 +674,12 @@ __global__ void __launch_bounds__(256) code_sqnorm_kernel(const uint16_t* __rest
 
 // ------------------------------------------------------------ decode (R5)
 // One warp per row: recon[n] = sum_l e_l[codes[l,n]] in f32, level order.
+// The row's codes are checked first (lane i holds level l32 + i of each
+// 32-level group), so a row with an out-of-range code is left unwritten.
+// Each lane then covers 8 columns (16 bytes) of a 256-column chunk, and the
+// codeword pieces of up to 8 levels are all loaded before the first add: a
+// warp keeps 8 gathers in flight instead of one dependent code-then-codeword
+// pair per level.
 __global__ void __launch_bounds__(256) rvq_decode_kernel(const int32_t* __restrict__ codes,
                                                          const uint16_t* __restrict__ cbs, int L,
                                                          uint16_t* __restrict__ out_bf16,
@@ -683,30 +689,62 @@ __global__ void __launch_bounds__(256) rvq_decode_kernel(const int32_t* __restri
   pdl_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= N) return;
-  for (int l = 0; l < L; ++l) {
-    const int c = codes[static_cast<size_t>(l) * N + row];
-    if (c < 0 || c >= K) {
-      if (lane == 0) atomicOr(err, kErrBadIndex);
-      return;
+  if (row >= N) return;  // whole warps leave together
+  bool bad = false;
+  for (int l32 = 0; l32 < L; l32 += 32) {
+    if (l32 + lane < L) {
+      const int c = __ldg(codes + static_cast<size_t>(l32 + lane) * N + row);
+      bad |= (c < 0 || c >= K);
     }
   }
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0) atomicOr(err, kErrBadIndex);
+    return;
+  }
   const size_t ro = static_cast<size_t>(row) * D;
-  for (int d = lane * 4; d < D; d += 128) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int l = 0; l < L; ++l) {
-      const int c = __ldg(codes + static_cast<size_t>(l) * N + row);
-      const uint2 ev =
-          __ldg(reinterpret_cast<const uint2*>(cbs + (static_cast<size_t>(l) * K + c) * D + d));
-      acc.x += bf16lo(ev.x);
-      acc.y += bf16hi(ev.x);
-      acc.z += bf16lo(ev.y);
-      acc.w += bf16hi(ev.y);
+  for (int d0 = 0; d0 < D; d0 += 256) {
+    const int d = d0 + lane * 8;
+    const bool act = d < D;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int l32 = 0; l32 < L; l32 += 32) {
+      const int mine = (l32 + lane < L) ? __ldg(codes + static_cast<size_t>(l32 + lane) * N + row) : 0;
+      const int lend = min(L - l32, 32);
+      for (int g = 0; g < lend; g += 8) {
+        uint4 ev[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = __shfl_sync(0xffffffffu, mine, (g + j) & 31);
+          if (g + j < lend && act)
+            ev[j] = __ldg(reinterpret_cast<const uint4*>(
+                cbs + (static_cast<size_t>(l32 + g + j) * K + c) * D + d));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (g + j < lend && act) {
+            acc[0] += bf16lo(ev[j].x);
+            acc[1] += bf16hi(ev[j].x);
+            acc[2] += bf16lo(ev[j].y);
+            acc[3] += bf16hi(ev[j].y);
+            acc[4] += bf16lo(ev[j].z);
+            acc[5] += bf16hi(ev[j].z);
+            acc[6] += bf16lo(ev[j].w);
+            acc[7] += bf16hi(ev[j].w);
+          }
+        }
+      }
     }
-    if (out_bf16 != nullptr)
-      *reinterpret_cast<uint2*>(out_bf16 + ro + d) =
-          make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
-    if (out_f32 != nullptr) *reinterpret_cast<float4*>(out_f32 + ro + d) = acc;
+    if (act) {
+      if (out_bf16 != nullptr)
+        *reinterpret_cast<uint4*>(out_bf16 + ro + d) =
+            make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                       pack_bf16x2(acc[6], acc[7]));
+      if (out_f32 != nullptr) {
+        *reinterpret_cast<float4*>(out_f32 + ro + d) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(out_f32 + ro + d + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+    }
   }
 }
 

@@ -126,15 +126,18 @@ def rvq_encode_host(x_host: torch.Tensor, codebooks: torch.Tensor, sqnorms: torc
     return codes_host, recon_host
 
 
-def rvq_decode(codes: torch.Tensor, codebooks: torch.Tensor) -> torch.Tensor:
-    """recon[n] = bf16(sum_l e_l[codes[l, n]]) (R5)."""
+def rvq_decode(codes: torch.Tensor, codebooks: torch.Tensor, recon: torch.Tensor | None = None) -> torch.Tensor:
+    """recon[n] = bf16(sum_l e_l[codes[l, n]]) (R5). A row holding an
+    out-of-range code is left unwritten and the context reports NCM_ERANGE."""
     L, N = codes.shape
     L2, K, D = codebooks.shape
     if L2 != L:
         raise ValueError("codes and codebooks disagree on the number of levels")
     need(codes, torch.int32, "codes")
     need(codebooks, bf16, "codebooks")
-    recon = torch.empty((N, D), dtype=bf16, device=codes.device)
+    if recon is None:
+        recon = torch.empty((N, D), dtype=bf16, device=codes.device)
+    need(recon, bf16, "recon", (N, D))
     _lib.call("ncm_rvq_decode", context(codes.device), ptr(codes), ptr(codebooks), L, ptr(recon), N, D, K,
               stream_of(codes))
     return recon

@@ -128,6 +128,40 @@ def test_host_pipelined_encode_matches_device_encode(cuda_dev, pinned):
     assert none is None and torch.equal(codes_only, codes_d.cpu())
 
 
+@pytest.mark.parametrize("N,L,D,K", [
+    (333, 8, 1024, 4096),   # the encode's shape class: one 8-level gather group, 4 column chunks
+    (100, 40, 264, 50),     # two 32-level code groups, 5 levels past a multiple of 8, a ragged last chunk
+    (17, 3, 8, 5),          # one active lane, fewer levels than a gather group
+    (9, 64, 520, 7),        # the most levels an encode takes
+])
+def test_decode_bit_exact(orc, cuda_dev, N, L, D, K):
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(N * L + D)
+    cbs = np.stack([gen_bf16(rng, (K, D), 0.7 ** l) for l in range(L)])
+    codes = rng.integers(0, K, (L, N), dtype=np.int32)
+    got = vq.rvq_decode(torch.from_numpy(codes).to(cuda_dev), to_dev_bf16(cbs, cuda_dev))
+    assert np.array_equal(from_dev_bf16(got), orc.bf16_bits(orc.rvq_decode(codes, cbs)))
+
+
+def test_decode_skips_only_rows_with_a_bad_code(orc, cuda_dev):
+    from ncmorph_b200 import _lib, device, vq
+    rng = np.random.default_rng(11)
+    L, N, D, K = 36, 20, 136, 30
+    cbs = np.stack([gen_bf16(rng, (K, D)) for _ in range(L)])
+    codes = rng.integers(0, K, (L, N), dtype=np.int32)
+    codes[33, 4] = K        # a bad code in the second 32-level group
+    codes[0, 9] = -1
+    out = torch.full((N, D), 7, dtype=torch.int16, device=cuda_dev).view(torch.bfloat16)
+    vq.rvq_decode(torch.from_numpy(codes).to(cuda_dev), to_dev_bf16(cbs, cuda_dev), recon=out)
+    with pytest.raises(_lib.NcmError) as ei:
+        device.sync(cuda_dev)
+    assert ei.value.status == _lib.NCM_ERANGE
+    got = from_dev_bf16(out)
+    good = [n for n in range(N) if n not in (4, 9)]
+    assert np.array_equal(got[good], orc.bf16_bits(orc.rvq_decode(codes[:, good], cbs)))
+    assert (got[[4, 9]] == 7).all()   # left as they were
+
+
 def test_decode_rejects_out_of_range_codes(cuda_dev):
     from ncmorph_b200 import _lib, device, vq
     cbs = torch.zeros((2, 16, 8), dtype=torch.bfloat16, device=cuda_dev)
