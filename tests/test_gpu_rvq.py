@@ -84,22 +84,34 @@ def test_config1_encode_decode(orc, cuda_dev):
     assert clean.mean() > 0.5
 
 
-@pytest.mark.parametrize("N,D,K,L", [(148 * 128 + 37, 256, 512, 3), (300 * 128, 64, 300, 2)])
-def test_fused_update_path_matches_oracle(orc, cuda_dev, N, D, K, L):
+@pytest.mark.parametrize("N,D,K,L,keep", [
+    (148 * 128 + 37, 256, 512, 3, True),
+    (148 * 128 + 37, 256, 512, 3, False),   # the last level decodes without updating
+    (300 * 128, 64, 300, 2, True),
+    (300 * 128, 64, 300, 1, False),         # one level: its input is the bf16 rows themselves
+    (160 * 128, 72, 32, 37, False),         # two 32-level code groups in the decode
+])
+def test_fused_update_path_matches_oracle(orc, cuda_dev, N, D, K, L, keep):
     """Row blocks >= SM count: one code split, so the residual update (f32 and
-    its bf16 shadow) runs inside the distance kernel."""
+    its bf16 shadow) runs inside the distance kernel; the last level updates
+    only when the residual is kept."""
     from ncmorph_b200 import vq
-    rng = np.random.default_rng(N + K)
+    rng = np.random.default_rng(N + K + L)
     x = gen_bf16(rng, (N, D))
-    cbs = _cbs(rng, L, K, D, 0.5)
-    codes_d, recon_d, resid_d = vq.rvq_encode(to_dev_bf16(x, cuda_dev), to_dev_bf16(cbs, cuda_dev),
-                                              want_residual=True)
+    cbs = _cbs(rng, L, K, D, 0.5 if L < 8 else 0.8)
+    cbs_d = to_dev_bf16(cbs, cuda_dev)
+    codes_d, recon_d, resid_d = vq.rvq_encode(to_dev_bf16(x, cuda_dev), cbs_d, want_residual=keep)
     codes = codes_d.cpu().numpy()
     best, gaps, resid, recon = orc.rvq_encode(x, cbs, codes_in=codes)
     for l in range(L):
         check_codes(codes[l], best[l], gaps[l], f"fused level {l}")
-    assert np.array_equal(resid_d.cpu().numpy(), resid)
+    if keep:
+        assert np.array_equal(resid_d.cpu().numpy(), resid)
     assert np.array_equal(from_dev_bf16(recon_d), orc.bf16_bits(recon))
+    # the decode entry point reproduces the encode's reconstruction
+    assert torch.equal(vq.rvq_decode(codes_d, cbs_d).view(torch.int16), recon_d.view(torch.int16))
+    if L > 3:
+        return
     # single-level entry point on the same rows (f32 residual in, no shadow out)
     r = orc.bf16_widen(x).astype(np.float32).copy()
     rd = torch.from_numpy(r).to(cuda_dev)
