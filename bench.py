@@ -310,13 +310,19 @@ def run_ours(a):
     cnt = ctypes.c_int64()
     _lib.check(lib.ncm_profile_read(ctx, b"rvq_argmin", ctypes.byref(tot), ctypes.byref(cnt)))
     argmin_ms, argmin_launches = tot.value, cnt.value
+    _lib.check(lib.ncm_profile_read(ctx, b"rvq_decode", ctypes.byref(tot), ctypes.byref(cnt)))
+    decode_ms, decode_launches = tot.value, cnt.value
     other_ms = ctypes.c_double()
     other_cnt = ctypes.c_int64()
     _lib.check(lib.ncm_profile_read(ctx, b"*", ctypes.byref(other_ms), ctypes.byref(other_cnt)))
-    launches = argmin_launches + other_cnt.value
+    launches = argmin_launches + decode_launches + other_cnt.value
     ndev.sync(dev)
     argmin_avg_ms = max_over_ranks(argmin_ms / max(argmin_launches, 1))
-    kernel_share = argmin_ms / max(argmin_ms + other_ms.value, 1e-9)
+    kernel_share = argmin_ms / max(argmin_ms + decode_ms + other_ms.value, 1e-9)
+    # per-step device time of each kernel family (CUDA events around every launch)
+    kernels = {"rvq_argmin": {"ms_per_step": argmin_ms / a.steps, "launches": argmin_launches},
+               "rvq_decode": {"ms_per_step": decode_ms / a.steps, "launches": decode_launches},
+               "other": {"ms_per_step": other_ms.value / a.steps, "launches": other_cnt.value}}
 
     # ---- e2e: host rows in, codes (and at N=1 the reconstructions) out.
     # N=1: the host-buffer C-ABI entry (ncm_rvq_encode_host) with its chunked
@@ -411,6 +417,7 @@ def run_ours(a):
                      "flops_per_launch": flops_per_launch, "avg_launch_ms": argmin_avg_ms,
                      "launches": argmin_launches, "share_of_kernel_time": kernel_share,
                      "traffic": traffic},
+        "kernels": kernels,
         "cpu_baseline": cpu,
         "gpu_launches": int(launches),
         "clocks": clocks,
