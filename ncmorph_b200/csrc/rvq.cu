@@ -629,23 +629,38 @@ __global__ void __launch_bounds__(256) rvq_apply_kernel(const ApplyArgs a) {
   }
   const size_t ro = static_cast<size_t>(row) * a.D;
   const uint16_t* e = a.codebook + static_cast<size_t>(code) * a.D;
-#pragma unroll 4
-  for (int d = lane * 4; d < a.D; d += 128) {
-    float4 r;
-    if (a.src_bf16 != nullptr) {
-      const uint2 s = *reinterpret_cast<const uint2*>(a.src_bf16 + ro + d);
-      r = make_float4(bf16lo(s.x), bf16hi(s.x), bf16lo(s.y), bf16hi(s.y));
-    } else {
-      r = *reinterpret_cast<const float4*>(a.resid + ro + d);
+  // 1024 columns per batch, every load of the batch issued before the first
+  // store: the stores may alias later loads as far as the compiler knows, so
+  // a plain loop keeps one residual and one codeword load in flight per lane
+  for (int d0 = 0; d0 < a.D; d0 += 1024) {
+    float4 x[8];
+    uint2 ev[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = d0 + lane * 4 + j * 128;
+      if (d < a.D) {
+        if (a.src_bf16 != nullptr) {
+          const uint2 sv = *reinterpret_cast<const uint2*>(a.src_bf16 + ro + d);
+          x[j] = make_float4(bf16lo(sv.x), bf16hi(sv.x), bf16lo(sv.y), bf16hi(sv.y));
+        } else {
+          x[j] = *reinterpret_cast<const float4*>(a.resid + ro + d);
+        }
+        ev[j] = __ldg(reinterpret_cast<const uint2*>(e + d));
+      }
     }
-    const uint2 ev = __ldg(reinterpret_cast<const uint2*>(e + d));
-    r.x -= bf16lo(ev.x);
-    r.y -= bf16hi(ev.x);
-    r.z -= bf16lo(ev.y);
-    r.w -= bf16hi(ev.y);
-    *reinterpret_cast<float4*>(a.resid + ro + d) = r;
-    if (a.shadow != nullptr) {
-      *reinterpret_cast<uint2*>(a.shadow + ro + d) = make_uint2(pack_bf16x2(r.x, r.y), pack_bf16x2(r.z, r.w));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = d0 + lane * 4 + j * 128;
+      if (d < a.D) {
+        float4 r = x[j];
+        r.x -= bf16lo(ev[j].x);
+        r.y -= bf16hi(ev[j].x);
+        r.z -= bf16lo(ev[j].y);
+        r.w -= bf16hi(ev[j].y);
+        *reinterpret_cast<float4*>(a.resid + ro + d) = r;
+        if (a.shadow != nullptr)
+          *reinterpret_cast<uint2*>(a.shadow + ro + d) = make_uint2(pack_bf16x2(r.x, r.y), pack_bf16x2(r.z, r.w));
+      }
     }
   }
 }
