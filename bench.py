@@ -23,6 +23,7 @@ import pathlib
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -106,11 +107,13 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = str(gpu_index)
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+        # raw samples: NCM_CLOCKS_DIR when set (to keep them), else the temp directory
+        out_dir = os.environ.get("NCM_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = pathlib.Path(out_dir) / f"clocks_bench_{os.getpid()}.csv"
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
