@@ -540,13 +540,13 @@ int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const 
                make_tmap_bf16_2d(&tv, vt, static_cast<uint64_t>(Hkv) * AT_D, T, 64);
   if (!fn_ok) return ncm_fail(NCM_EINVAL, "attention: tensor map encoding failed (T=%d, stride %lld)", T,
                               (long long)qkv_stride);
-  static unsigned long long attr_set = 0;
+  static DeviceFlags attr_set;
   int dev = 0;
   NCM_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev >= 64 || !(attr_set & (1ull << dev))) {
+  if (!attr_set.test(dev)) {
     NCM_CUDA_TRY(cudaFuncSetAttribute(attention2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(ATTN2_SMEM)));
-    if (dev < 64) attr_set |= 1ull << dev;
+    attr_set.set(dev);
   }
   const int n_qp = (T + 2 * AT_Q - 1) / (2 * AT_Q);
   NCM_CUDA_TRY(launch_pdl(attention2_bf16_kernel, dim3(n_qp * H), dim3(AT_THREADS), ATTN2_SMEM, stream, 1, tq, tk, tv,

@@ -689,14 +689,14 @@ constexpr size_t linear_smem_bytes() {
 // device (once per device).
 template <int BN, bool SWAP, bool PAIR>
 cudaError_t linear_prepare() {
-  static unsigned long long attr_set = 0;
+  static DeviceFlags attr_set;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 64 && (attr_set & (1ull << dev))) return cudaSuccess;
+  if (attr_set.test(dev)) return cudaSuccess;
   e = cudaFuncSetAttribute(linear_bf16_kernel<BN, SWAP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(linear_smem_bytes<BN, SWAP, PAIR>()));
-  if (e == cudaSuccess && dev < 64) attr_set |= 1ull << dev;
+  if (e == cudaSuccess) attr_set.set(dev);
   return e;
 }
 
@@ -722,10 +722,11 @@ cudaError_t launch_linear(const CUtensorMap& tmA, const CUtensorMap& tmB, const 
 // How many 2-CTA clusters of the 256-wide pair kernel fit at once (cluster
 // placement can leave SMs idle); cached per device, 0 if none.
 int max_pairs_linear(int num_sms) {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cached[dev] != 0) return cached[dev] > 0 ? cached[dev] : 0;
+  const int known = cached[dev].load(std::memory_order_relaxed);
+  if (known != 0) return known > 0 ? known : 0;
   int n = 0;
   if (linear_prepare<256, false, true>() == cudaSuccess) {
     cudaLaunchConfig_t cfg{};
@@ -738,8 +739,9 @@ int max_pairs_linear(int num_sms) {
     if (cudaOccupancyMaxActiveClusters(&n, linear_bf16_kernel<256, false, true>, &cfg) != cudaSuccess) n = 0;
   }
   cudaGetLastError();
-  cached[dev] = n > 0 ? std::min(n, num_sms / 2) : -1;
-  return n > 0 ? cached[dev] : 0;
+  const int v = n > 0 ? std::min(n, num_sms / 2) : -1;
+  cached[dev].store(v, std::memory_order_relaxed);  // every thread computes the same value
+  return v > 0 ? v : 0;
 }
 
 // Tile shape of a non-swapped GEMM with `rows` output rows and `cols` output

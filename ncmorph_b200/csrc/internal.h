@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <utility>
 #include <vector>
 
@@ -98,7 +99,6 @@ class Launch {
   cudaEvent_t stop_ = nullptr;
 };
 
-// Carves consecutive 256-byte-aligned regions out of the context workspace.
 // Launch with the programmatic stream-serialization attribute (and a cluster
 // dimension when cluster_x > 1): the kernel may begin while its predecessor on
 // the stream drains; it calls pdl_wait() before touching that predecessor's data.
@@ -126,6 +126,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Carves consecutive 256-byte-aligned regions out of the context workspace.
 struct WsCarver {
   size_t offset = 0;
   size_t take(size_t bytes) {
@@ -133,6 +134,20 @@ struct WsCarver {
     offset += (bytes + 255) & ~static_cast<size_t>(255);
     return at;
   }
+};
+
+// Process-wide per-device state that host threads driving different GPUs
+// share (one bit per device index below 64): a kernel's shared-memory opt-in
+// is per device, so it is set once per device, from any thread.
+class DeviceFlags {
+ public:
+  bool test(int dev) const { return dev >= 0 && dev < 64 && (bits_.load(std::memory_order_acquire) >> dev) & 1ull; }
+  void set(int dev) {
+    if (dev >= 0 && dev < 64) bits_.fetch_or(1ull << dev, std::memory_order_release);
+  }
+
+ private:
+  std::atomic<unsigned long long> bits_{0};
 };
 
 // Ensures the workspace holds at least `bytes`; returns its base or nullptr.

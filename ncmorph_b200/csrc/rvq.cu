@@ -953,10 +953,11 @@ namespace {
 // How many 2-CTA clusters of the pair kernel fit on this device at once
 // (cluster placement can leave SMs idle); cached per device.
 int max_active_pairs(int num_sms) {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms / 2;
-  if (cached[dev] > 0) return cached[dev];
+  const int known = cached[dev].load(std::memory_order_relaxed);
+  if (known > 0) return known;
   int n = 0;
   const size_t smem = argmin_smem_bytes<true>();
   if (cudaFuncSetAttribute(rvq_argmin_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -975,8 +976,9 @@ int max_active_pairs(int num_sms) {
     if (cudaOccupancyMaxActiveClusters(&n, rvq_argmin_kernel<false, true>, &cfg) != cudaSuccess) n = 0;
   }
   cudaGetLastError();
-  cached[dev] = n > 0 ? std::min(n, num_sms / 2) : -1;
-  return cached[dev];
+  const int v = n > 0 ? std::min(n, num_sms / 2) : -1;
+  cached[dev].store(v, std::memory_order_relaxed);  // every thread computes the same value
+  return v;
 }
 }  // namespace
 
@@ -1039,12 +1041,12 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
                               const RvqTop2* top2, const float* mul_dev, int* counters) {
   if (plan.pair && (top2 != nullptr || plan.splits != 1)) return cudaErrorInvalidValue;
   // the shared-memory opt-in is per device and per instantiation: remember which devices have it
-  static unsigned long long attr_set[3] = {0, 0, 0};
+  static DeviceFlags attr_set[3];
   const int gi = plan.pair ? 2 : (top2 != nullptr ? 1 : 0);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 64 || !(attr_set[gi] & (1ull << dev))) {
+  if (!attr_set[gi].test(dev)) {
     if (gi == 2)
       e = cudaFuncSetAttribute(rvq_argmin_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(argmin_smem_bytes<true>()));
@@ -1055,7 +1057,7 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
       e = cudaFuncSetAttribute(rvq_argmin_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(argmin_smem_bytes<false>()));
     if (e != cudaSuccess) return e;
-    if (dev < 64) attr_set[gi] |= 1ull << dev;
+    attr_set[gi].set(dev);
   }
   ArgminArgs a{};
   a.csq = sqnorm;
