@@ -434,9 +434,10 @@ NCM_API int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, con
 
 /* No counterpart in the reference: ncmorph has no device code, so nothing
  * there allocates device memory. This is ncm_rvq_level for callers that
- * cannot call cudaMalloc — code running while a CUDA graph is captured on its
- * stream, host plugins whose application owns every device allocation, paths
- * that may not block on the allocator. It takes no context and allocates
+ * cannot call cudaMalloc: host plugins whose application owns every device
+ * allocation (its arena or caching allocator must account for all memory),
+ * and latency-bound paths that may not stall on cudaMalloc, which can
+ * synchronise the device. It takes no context and allocates
  * nothing: its scratch (the bf16 copy of the residual, the per-split argmin
  * partials, the code norms when sqnorm is NULL, an error word) is a 16 MiB
  * device array that every GPU loading the library holds until exit, so

@@ -1,10 +1,9 @@
 // ncm_rvq_level_noalloc: one RVQ level with no device allocation at all.
 //
-// Some callers cannot call cudaMalloc: code running while a CUDA graph is
-// being captured on its stream, host plugins whose embedding application
-// owns every device allocation (a fixed arena or a caching allocator that
-// must see all memory), and real-time paths that may not block on the
-// allocator. ncm_rvq_level grows the context's workspace with cudaMalloc and
+// Some callers cannot call cudaMalloc: host plugins whose embedding
+// application owns every device allocation (a fixed arena, or a caching
+// allocator that must account for all memory), and latency-bound paths that
+// may not stall on cudaMalloc, which can synchronise the device. ncm_rvq_level grows the context's workspace with cudaMalloc and
 // ncm_ctx_create allocates the context's error word, so neither is usable
 // there. This entry point needs no context and allocates nothing: its scratch
 // (the bf16 copy of the residual that the tensor cores read, the per-split

@@ -1,10 +1,10 @@
 """The no-allocation RVQ level entry point, through the C ABI.
 
-Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
-being captured on its stream (an allocation would break the capture), host
-plugins whose application owns every device allocation, and latency paths that
-may not block on the allocator. ncm_rvq_level_noalloc serves them: it takes no
-context and keeps its scratch in a fixed device array inside the library.
+Some callers cannot call cudaMalloc: host plugins whose application owns every
+device allocation (its own arena or caching allocator must account for all
+memory), and latency-bound paths that may not stall on cudaMalloc, which can
+synchronise the device. ncm_rvq_level_noalloc serves them: it takes no context
+and keeps its scratch in a fixed device array inside the library.
 
 This file is named to be collected last, so a run that stops at the first
 failure has already run every other test. It must pass alone in a fresh
