@@ -21,7 +21,11 @@
  *    reports device-side failures (a timed-out pipeline wait, a bad index).
  *  - Shapes are validated on the host; a bad shape returns NCM_EINVAL where
  *    the reference would `std.debug.assert`.
- *  - A context may be used from one host thread at a time.
+ *  - A context may be used from one host thread at a time; different
+ *    contexts (one per GPU, say) may be driven from different threads at
+ *    once. The library's process-wide state (per-device kernel attributes
+ *    and occupancy caches, the no-allocation scratch set-up) is atomic or
+ *    locked.
  */
 #ifndef NCM_CUDA_H
 #define NCM_CUDA_H
