@@ -47,6 +47,8 @@ def parse_args():
     p.add_argument("--codes", type=int, default=16384)
     p.add_argument("--cpu-rows", type=int, default=2048, help="rows per CPU-baseline sample")
     p.add_argument("--seed", type=int, default=20260)
+    p.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                   help="N>1: copy-engine pushes over CUDA IPC mappings (peer) or NCCL all-gather kernels")
     p.add_argument("--graph", action="store_true",
                    help="secondary workloads: replay one captured CUDA graph per step")
     p.add_argument("--upsample", choices=["nearest", "linear"], default="nearest",
@@ -68,7 +70,10 @@ def config_dict(a, world):
         "codebook_size": a.codes,
         "rows_per_gpu": a.rows // world,
         "parallelism": f"row-sharded x{world}, codebooks replicated",
-        "collective": ("NCCL all_gather of codes and bf16 reconstructions, on a second stream overlapping the "
+        "collective": (("copy-engine pushes of codes and bf16 reconstructions into every rank's output buffers over "
+                        "CUDA IPC mappings, between two one-element NCCL all-reduces, on a second stream overlapping "
+                        "the next step's encode") if a.transport == "peer" else
+                       "NCCL all_gather of codes and bf16 reconstructions, on a second stream overlapping the "
                        "next step's encode") if world > 1 else "none (1 GPU)",
         "l2": "inputs exceed L2 (bf16 rows 2 GiB/N, f32 residual 4 GiB/N); codebooks (32 MiB/level) stay L2-resident by design",
         "data": "synthetic seeded N(0,1) rows, N(0,0.6^l) codebooks",
@@ -197,6 +202,44 @@ def cpu_encode_sample(a, rows: int, threads: int):
     return time.perf_counter() - t0, rows
 
 
+def cpu_leg_and_parity(a, x, cbs, codes):
+    """The CPU baseline and the code parity of the headline workload, on one
+    sample of the GPU's own rows: the oracle port encodes `a.cpu_rows` rows on
+    its own (timed: the baseline), then once more teacher-forced by the GPU's
+    codes. Reports the flip rate (codes differing from the oracle's argmin on
+    the same residual), the near-tie rate (oracle top-2 gap below 1e-3 of the
+    best full squared distance), flips outside near-ties (must be 0), and how
+    many rows' free-running code sequences diverge."""
+    import torch
+    from oracle import pyoracle as orc
+    threads = os.cpu_count() or 1
+    n = x.shape[0]
+    L, K, D = cbs.shape
+    g = torch.Generator().manual_seed(a.seed + 7)
+    idx = torch.sort(torch.randperm(n, generator=g)[: min(a.cpu_rows, n)]).values
+    idx_d = idx.to(x.device)
+    xs = x[idx_d].view(torch.int16).cpu().numpy().view(np.uint16)
+    cs = codes[:, idx_d].cpu().numpy()
+    cbs_np = cbs.view(torch.int16).cpu().numpy().view(np.uint16)
+    rows = idx.numel()
+    t0 = time.perf_counter()
+    free_best, _, _, _ = orc.rvq_encode(xs, cbs_np, threads=threads)
+    sec = time.perf_counter() - t0
+    cpu = {"value": rows / sec, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": (f"{rows} of the GPU's rows x {L} levels x K={K} x D={D}, encoded free-running by the oracle "
+                      f"port (its per-level codebook transpose included)")}
+    tf_best, gaps, _, _ = orc.rvq_encode(xs, cbs_np, codes_in=cs, threads=threads)
+    flips = cs != tf_best
+    near = gaps < 1e-3
+    diverged = (cs != free_best).any(axis=0)
+    parity = {"rows": rows, "codes": int(cs.size), "flip_rate": float(flips.mean()),
+              "near_tie_rate": float(near.mean()), "flips_outside_near_ties": int((flips & ~near).sum()),
+              "free_running_diverged_rows": int(diverged.sum()),
+              "rule": ("teacher-forced: the oracle advances with the GPU's codes, so each flip is a level-local "
+                       "argmin difference; near-tie = oracle top-2 gap < 1e-3 of the best full squared distance")}
+    return cpu, parity
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -257,7 +300,7 @@ def run_ours(a):
     if world > 1:
         from ncmorph_b200.sharded import ShardedEncoder
         # batches stream: a step's all-gathers overlap the next step's encode
-        encoder = ShardedEncoder(cbs, a.rows, torch.bfloat16, sq, overlap=True)
+        encoder = ShardedEncoder(cbs, a.rows, torch.bfloat16, sq, overlap=True, transport=a.transport)
     result = {}
 
     def step():
@@ -327,14 +370,16 @@ def run_ours(a):
                "rvq_decode": {"ms_per_step": decode_ms / a.steps, "launches": decode_launches},
                "other": {"ms_per_step": other_ms.value / a.steps, "launches": other_cnt.value}}
 
-    # ---- e2e: host rows in, codes (and at N=1 the reconstructions) out.
+    # ---- e2e: host rows in, codes and reconstructions out.
     # N=1: the host-buffer C-ABI entry (ncm_rvq_encode_host) with its chunked
-    # copy/compute pipeline. N>1: rows copied in, sharded encode + all-gather,
-    # gathered codes copied out.
+    # copy/compute pipeline. N>1: rows copied in, sharded encode + all-gather;
+    # every rank copies out the gathered codes and its own rows of the
+    # gathered reconstruction, so the host receives the whole reconstruction
+    # once across the ranks, as at N=1.
     x_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(x.cpu())
     codes_host = torch.empty((L, a.rows), dtype=torch.int32).pin_memory()
-    recon_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory() if world == 1 else None
+    recon_host = torch.empty((n, D), dtype=torch.bfloat16).pin_memory()
 
     if world == 1:
         def step_e2e():
@@ -342,13 +387,16 @@ def run_ours(a):
         finish_e2e = None
     else:
         # streaming batches: step i+1's rows are copied in on a second stream
-        # (into the other of two row buffers) and step i's gathered codes are
-        # copied out on a third, while the encode and its all-gathers proceed
+        # (into the other of two row buffers) and step i's gathered codes and
+        # own reconstruction rows are copied out on a third, while the encode
+        # and its all-gathers proceed
         cp, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         xbuf = [x, torch.empty_like(x)]
         copied = [torch.cuda.Event(), torch.cuda.Event()]
         consumed = [torch.cuda.Event(), torch.cuda.Event()]
+        drained = [torch.cuda.Event(), torch.cuda.Event()]
         st = {"i": 0, "n": 1}
+        own = slice(rank * n, (rank + 1) * n)
 
         def step_e2e():
             i = st["i"]
@@ -366,11 +414,15 @@ def run_ours(a):
                     xbuf[b ^ 1].copy_(x_host, non_blocking=True)
                     copied[b ^ 1].record(cp)
             cur.wait_event(copied[b])
-            codes_d, _ = encoder(xbuf[b])
+            if i >= 2:
+                cur.wait_event(drained[b])   # step i-2's results (same buffer set) are copied out
+            codes_d, recon_d = encoder(xbuf[b])
             consumed[b].record(cur)
             with torch.cuda.stream(d2h):
                 encoder.wait()
                 codes_host.copy_(codes_d, non_blocking=True)
+                recon_host.copy_(recon_d[own], non_blocking=True)
+                drained[b].record(d2h)
             st["i"] = i + 1
 
         def finish_e2e():
@@ -392,14 +444,14 @@ def run_ours(a):
     peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
     traffic = ncu_traffic(n)
 
-    cpu = None
+    cpu = parity = extra = None
     if rank == 0 and world == 1:
-        threads = os.cpu_count() or 1
-        sec, rows = cpu_encode_sample(a, a.cpu_rows, threads)
-        cpu = {"value": rows / sec, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{rows} rows x {L} levels x K={K} x D={D} through the oracle port"}
+        cpu, parity = cpu_leg_and_parity(a, x, cbs, codes)
+        extra = run_extras(a, dev)
 
     if world > 1:
+        torch.cuda.synchronize()
+        encoder.close()   # unmaps the peers' buffers (collective)
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:
@@ -409,10 +461,10 @@ def run_ours(a):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 operands, f32 accumulation", "data": "synthetic", "config": config_dict(a, world),
         "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": ms_e2e, "h2d_bytes_per_step": n * D * 2,
-                "d2h_bytes_per_step": int(codes_host.numel() * 4 + (recon_host.numel() * 2 if recon_host is not None else 0)),
+                "d2h_bytes_per_step": int(codes_host.numel() * 4 + recon_host.numel() * 2),
                 "path": "ncm_rvq_encode_host (chunked H2D/encode/D2H pipeline)" if world == 1
-                        else ("H2D rows (next step's on a copy stream), sharded encode, NCCL all-gather on a "
-                              "second stream, D2H codes on a third")},
+                        else ("H2D rows (next step's on a copy stream), sharded encode, all-gather on a second "
+                              "stream, D2H of the gathered codes and this rank's reconstruction rows on a third")},
         "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
@@ -422,9 +474,12 @@ def run_ours(a):
                      "traffic": traffic},
         "kernels": kernels,
         "cpu_baseline": cpu,
+        "parity": parity,
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
+    if extra is not None:
+        line["extra"] = extra
     emit(line)
     return 0
 
@@ -697,12 +752,352 @@ def _profile(lib, ctx, names):
     return out
 
 
-def run_secondary(a):
-    import ctypes
-
+def _tokenizer_setup(a, dev, rnd, g):
+    """BASELINE config 2 inputs and weights (synthetic, seeded)."""
     import torch
 
-    from ncmorph_b200 import _lib, device as ndev, kernels, ncm_model, vq
+    from ncmorph_b200 import vq
+    B, T, Din, D, K, L = 8, 2048, 2048, 1024, 4096, 8
+    factors = [16, 8, 4, 2, 1]
+    S = len(factors)
+    x = rnd((B, T, Din))
+    w_in, w_out = rnd((D, Din), 0.02), rnd((Din, D), 0.02)
+    decay = torch.tensor([0.6 ** l for l in range(L)], device=dev).view(1, L, 1, 1)
+    cbs = (rnd((S, L, K, D)).float() * decay).to(torch.bfloat16)
+    sq = vq.code_sqnorm(cbs)
+    pw = pb = None
+    if a.phi:
+        bound = 1.0 / (3 * D) ** 0.5
+        pw = ((torch.rand((S, D, D, 3), generator=g, device=dev) * 2 - 1) * bound).to(torch.bfloat16)
+        pb = (torch.rand((S, D), generator=g, device=dev) * 2 - 1) * bound
+    return dict(B=B, T=T, Din=Din, D=D, K=K, L=L, factors=factors, x=x, w_in=w_in, w_out=w_out, cbs=cbs, sq=sq,
+                pw=pw, pb=pb)
+
+
+def measure_tokenizer(a, dev, lib, ctx, rnd, g, peaks, peak_kind, steps, warmup, graph):
+    """Config 2 (multiscale tokenizer forward): vectors/s, device-resident
+    (eager, or one CUDA-graph replay per step with graph=True) and end to end
+    from pinned host memory; per-kernel device time from the library's events."""
+    import torch
+
+    from ncmorph_b200 import vq
+    c = _tokenizer_setup(a, dev, rnd, g)
+    B, T, Din, D, K, L, factors = c["B"], c["T"], c["Din"], c["D"], c["K"], c["L"], c["factors"]
+    S = len(factors)
+    tok = dict(sqnorms=c["sq"], upsample=a.upsample, phi_weight=c["pw"], phi_bias=c["pb"], phi_ratio=0.5)
+    x, w_in, cbs, w_out = c["x"], c["w_in"], c["cbs"], c["w_out"]
+    step = lambda: vq.tokenizer_forward(x, w_in, cbs, w_out, factors, **tok)  # noqa: E731
+    _timed_loop(step, 0, warmup)
+    lib.ncm_profile_read(ctx, b"*", None, None)
+    lib.ncm_profile_enable(ctx, 1)
+    _timed_loop(step, steps, 0)      # per-kernel breakdown (eager launches)
+    lib.ncm_profile_enable(ctx, 0)
+    run = _graphed(step, graph)
+    _timed_loop(run, 0, warmup)
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    ms = _timed_loop(run, steps, 0)
+    clocks = sampler.stop()
+    prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "rvq_apply", "pool_avg", "scale_update", "cast",
+                               "conv_k3", "upsample", "*"])
+    rows = sum(B * T // f for f in factors)
+    dist_flops = 2.0 * rows * K * D * L
+    proj_flops = 2 * 2.0 * B * T * Din * D
+    am_ms, am_n = prof["rvq_argmin"]
+    ln_ms, _ = prof["linear_bf16"]
+    x_host = torch.empty_like(x, device="cpu").pin_memory()
+    x_host.copy_(x.cpu())
+    codes_host = torch.empty(L * rows, dtype=torch.int32).pin_memory()
+    ms_e2e = _tokenizer_e2e(x, x_host, codes_host, lambda xb: vq.tokenizer_forward(xb, w_in, cbs, w_out, factors,
+                                                                                   **tok)[0], steps)
+    achieved = dist_flops / (am_ms / steps * 1e-3) / 1e12
+    return {
+        "metric": "tokenizer_vectors_per_s", "value": B * T / (ms * 1e-3), "unit": "vectors/s",
+        "ms_per_step": ms, "steps": steps, "warmup": warmup, "cuda_graph": bool(graph),
+        "config": {"workload": "multiscale tokenizer forward (BASELINE config 2)", "batch": B, "seq_len": T,
+                   "model_width": Din, "vq_width": D, "codebook_size": K, "levels_per_scale": L,
+                   "pool_factors": factors, "rows_quantised": rows, "upsample": a.upsample, "phi": bool(a.phi),
+                   "l2": "inputs (64 MiB) and the f32 residual (64 MiB) are below L2; each step rewrites them"},
+        "e2e": {"value": B * T / (ms_e2e * 1e-3), "unit": "vectors/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": codes_host.numel() * 4,
+                "path": "vq.tokenizer_forward; the next step's input copy runs on a second stream"},
+        "roofline": {"bound": "tensor", "kernel": f"rvq_argmin_kernel (all {S * L} levels)", "achieved": achieved,
+                     "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                     "frac": achieved / float(peaks["bf16_tflops"]),
+                     "peak_source": f"{peak_kind} bf16_tflops (burst; a 2-3 ms step)",
+                     "argmin_ms_per_step": am_ms / steps, "linear_ms_per_step": ln_ms / steps,
+                     "linear_tflops": proj_flops / (ln_ms / steps * 1e-3) / 1e12,
+                     "conv_tflops": (2.0 * B * T * 3 * D * D * S / (prof["conv_k3"][0] / steps * 1e-3) / 1e12
+                                     if a.phi and prof["conv_k3"][0] > 0 else None),
+                     "share_argmin": am_ms / max(sum(v[0] for v in prof.values()), 1e-9),
+                     "ms_per_step_by_kernel": {k: v[0] / steps for k, v in prof.items()}},
+        "gpu_launches": int(sum(v[1] for v in prof.values())), "clocks": clocks}
+
+
+def cpu_tokenizer(a, threads, rows_sample=128, proj_rows=64):
+    """Config 2 on the oracle port: the RVQ cost per quantised row (all 8
+    levels, K = 4096, D = 1024) from `rows_sample` rows, and the two
+    projections' cost per token from `proj_rows` rows (the faithful bf16
+    linear), extrapolated to the whole forward (31,744 quantised rows, 16,384
+    tokens through both projections). Pooling and decode are left out."""
+    from oracle import pyoracle as orc
+    rng = np.random.default_rng(a.seed + 5)
+    D, Din, K, L, N = 1024, 2048, 4096, 8, 8 * 2048
+    rows_q = sum(N // f for f in (16, 8, 4, 2, 1))
+    u = orc.bf16_bits(rng.standard_normal((rows_sample, D)).astype(np.float32))
+    cbs = np.stack([orc.bf16_bits((rng.standard_normal((K, D)) * 0.6 ** l).astype(np.float32)) for l in range(L)])
+    t0 = time.perf_counter()
+    orc.rvq_encode(u, cbs, threads=threads)
+    t_rvq = (time.perf_counter() - t0) / rows_sample
+    xs = orc.round_bf16(rng.standard_normal((proj_rows, Din)).astype(np.float32))
+    w_in = orc.round_bf16((rng.standard_normal((D, Din)) * 0.02).astype(np.float32))
+    w_out = orc.round_bf16((rng.standard_normal((Din, D)) * 0.02).astype(np.float32))
+    t0 = time.perf_counter()
+    h = orc.matmul_bf16(xs, w_in, threads=threads)
+    orc.matmul_bf16(orc.round_bf16(h), w_out, threads=threads)
+    t_proj = (time.perf_counter() - t0) / proj_rows
+    total = rows_q * t_rvq + N * t_proj
+    return {"value": N / total, "unit": "vectors/s", "cores": threads, "kind": "port",
+            "sample": (f"extrapolated: {rows_sample} quantised rows x {L} levels (K={K}, D={D}) and {proj_rows} tokens "
+                       f"through both projections, scaled to {rows_q} quantised rows and {N} tokens")}
+
+
+def measure_linear(a, dev, rnd, peaks, peak_kind, steps, warmup):
+    """Config 3: the 25 Llama-3.2-1B shapes, median CUDA-event time per shape
+    with L2 cleaned between calls."""
+    import torch
+
+    from ncmorph_b200 import kernels
+    Ms = [1, 64, 512, 4096, 8192]
+    KNs = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)]
+    rows, tot_flops, tot_ms = [], 0.0, 0.0
+    flush = _l2_flusher(dev)  # > L2: read between timed calls
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    for M in Ms:
+        for (K, N) in KNs:
+            xx, ww = rnd((M, K)), rnd((N, K), 0.02)
+            yy = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            for _ in range(warmup):
+                kernels.linear_bf16(xx, ww, out=yy)
+            t = _event_ms(lambda: kernels.linear_bf16(xx, ww, out=yy), steps, flush)
+            fl = 2.0 * M * N * K
+            by = 2.0 * (M * K + N * K + M * N)
+            tot_flops += fl
+            tot_ms += t
+            ai = fl / by
+            roof = min(float(peaks["bf16_tflops"]) * 1e12, float(peaks["hbm_gbs"]) * 1e9 * ai)
+            rows.append({"M": M, "K": K, "N": N, "us": t * 1e3, "tflops": fl / (t * 1e-3) / 1e12,
+                         "gbs": by / (t * 1e-3) / 1e9, "frac_of_roofline": fl / (t * 1e-3) / roof})
+            del xx, ww, yy
+    clocks = sampler.stop()
+    worst = min(rows, key=lambda r: r["frac_of_roofline"])
+    return {
+        "metric": "linear_sweep_tflops", "value": tot_flops / (tot_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "ms_per_step": tot_ms, "steps": steps, "warmup": warmup,
+        "config": {"workload": "bf16 linear sweep, Llama-3.2-1B shapes (BASELINE config 3)",
+                   "l2": "256 MiB buffer read between timed calls (L2 cold and clean)", "shapes": rows},
+        "worst_shape": worst,
+        "roofline": {"bound": "min(tensor, hbm x intensity) per shape",
+                     "peak_source": f"{peak_kind} bf16_tflops / hbm_gbs",
+                     "worst_frac": worst["frac_of_roofline"]},
+        "clocks": clocks}
+
+
+def cpu_linear(threads, flops_per_shape=1e9, max_outputs=4096):
+    """Config 3 on the oracle port's faithful bf16 linear (matmul_bf16_impl's
+    pair order, FTZ and K blocks). Its cost per output element depends only
+    on K, so per (K, N) it is timed on a block of up to `max_outputs` outputs
+    and about `flops_per_shape` FLOPs, and extrapolated to every M x N of the
+    sweep; aggregate TFLOP/s over the 25 shapes."""
+    from oracle import pyoracle as orc
+    rng = np.random.default_rng(3)
+    Ms = [1, 64, 512, 4096, 8192]
+    KNs = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)]
+    tot_flops = tot_sec = 0.0
+    for (K, N) in KNs:
+        n_sub = min(N, max_outputs)
+        w = orc.round_bf16((rng.standard_normal((n_sub, K)) * 0.02).astype(np.float32))
+        m = max(1, min(8192, int(flops_per_shape // (2.0 * K * n_sub))))
+        xs = orc.round_bf16(rng.standard_normal((m, K)).astype(np.float32))
+        t0 = time.perf_counter()
+        orc.matmul_bf16(xs, w, threads=threads)
+        per_elem = (time.perf_counter() - t0) / (m * n_sub)
+        for M in Ms:
+            tot_flops += 2.0 * M * N * K
+            tot_sec += per_elem * M * N
+    return {"value": tot_flops / tot_sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": (f"extrapolated: per (K, N) the time per output element on a block of up to {max_outputs} "
+                       f"outputs and about {flops_per_shape / 1e9:g} GFLOP, scaled to the 25 shapes")}
+
+
+def _decoder_setup(dev, rnd, g):
+    import torch
+
+    from ncmorph_b200 import ncm_model
+    cfg = ncm_model.Config(hidden_size=2048, vq_width=1024, num_attention_heads=32, num_key_value_heads=8,
+                           intermediate_size=8192, level_lengths=(256, 256, 512, 1024, 2048),
+                           mask="block_causal")
+    Hd, F = cfg.hidden_size, cfg.intermediate_size
+    layers = [ncm_model.LayerWeights(ln_1=rnd((Hd,), 0.0) + 1, qkv=rnd((3072, Hd), 0.02), o=rnd((Hd, 2048), 0.02),
+                                     ln_2=rnd((Hd,), 0.0) + 1, gate_up=rnd((2 * F, Hd), 0.02),
+                                     down=rnd((Hd, F), 0.02)) for _ in range(16)]
+    w = ncm_model.Weights(input_projection=rnd((Hd, cfg.vq_width), 0.02), input_projection_bias=rnd((Hd,), 0.02),
+                          level_embedding=rnd((5, Hd), 0.02), final_norm=rnd((Hd,), 0.0) + 1, layers=layers)
+    table = rnd((4096, cfg.vq_width))
+    codes = torch.randint(0, 4096, (cfg.seq_len,), generator=g, device=dev, dtype=torch.int32)
+    return cfg, w, table, codes
+
+
+def measure_decoder(a, dev, lib, ctx, rnd, g, peaks, peak_kind, steps, warmup, graph):
+    """Config 4 (16-layer NCM decoder forward, 4096 positions, block-causal):
+    tokens/s device-resident (eager or one graph replay per step) and end to
+    end (code ids in from pinned memory, hidden states back)."""
+    import torch
+
+    from ncmorph_b200 import ncm_model
+    cfg, w, table, codes = _decoder_setup(dev, rnd, g)
+    Hd, F = cfg.hidden_size, cfg.intermediate_size
+    out = torch.empty((cfg.seq_len, Hd), dtype=torch.bfloat16, device=dev)
+
+    def step():
+        inputs = ncm_model.embedding_gather(table, codes)
+        ncm_model.forward(cfg, w, inputs, out=out)
+
+    _timed_loop(step, 0, warmup)
+    lib.ncm_profile_read(ctx, b"*", None, None)
+    lib.ncm_profile_enable(ctx, 1)
+    _timed_loop(step, steps, 0)      # per-kernel breakdown (eager launches)
+    lib.ncm_profile_enable(ctx, 0)
+    run = _graphed(step, graph)
+    _timed_loop(run, 0, warmup)
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    ms = _timed_loop(run, steps, 0)
+    clocks = sampler.stop()
+    prof = _profile(lib, ctx, ["linear_bf16", "attention", "*"])
+    T = cfg.seq_len
+    lin_flops = 16 * 2.0 * T * Hd * (3072 + 2048 + 3 * F) + 2.0 * T * cfg.vq_width * Hd
+    lv = list(cfg.level_lengths)
+    allowed = sum(n * sum(lv[: i + 1]) for i, n in enumerate(lv))
+    att_flops = 16 * 4.0 * allowed * 32 * 64
+    ln_ms, ln_n = prof["linear_bf16"]
+    at_ms, at_n = prof["attention"]
+    codes_host = codes.cpu().pin_memory()
+    out_host = torch.empty((T, Hd), dtype=torch.bfloat16).pin_memory()
+
+    def step_e2e():
+        codes.copy_(codes_host, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+
+    ms_e2e = _timed_loop(step_e2e, steps, 1)
+    lin_ach = lin_flops / (ln_ms / steps * 1e-3) / 1e12
+    return {
+        "metric": "decoder_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": steps, "warmup": warmup, "cuda_graph": bool(graph),
+        "config": {"workload": "NCM decoder forward (BASELINE config 4)", "layers": 16, "d_model": Hd,
+                   "heads": 32, "kv_heads": 8, "head_dim": 64, "ffn": F, "positions": T,
+                   "levels": lv, "mask": "block_causal", "flops_linear": lin_flops, "flops_attention": att_flops,
+                   "l2": "weights (1.9 GB) exceed L2 and stream every step"},
+        "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": T * Hd * 2},
+        "roofline": {"bound": "tensor", "kernel": "linear_bf16_kernel", "achieved": lin_ach,
+                     "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                     "frac": lin_ach / float(peaks["bf16_tflops"]), "peak_source": f"{peak_kind} bf16_tflops",
+                     "linear_ms_per_step": ln_ms / steps, "attention_ms_per_step": at_ms / steps,
+                     "attention_tflops": att_flops / (at_ms / steps * 1e-3) / 1e12,
+                     "other_ms_per_step": prof["*"][0] / steps},
+        "gpu_launches": int(ln_n + at_n + prof["*"][1]), "clocks": clocks}
+
+
+def cpu_decoder(a, threads, rows_sample=32):
+    """Config 4 on the oracle port: one layer's per-row work (its QKV, O,
+    gate/up and down projections on the faithful bf16 linear, RMSNorms, and
+    attention_impl's per-row core against all 4096 keys of the block-causal
+    mask) on `rows_sample` random rows, plus the input projection, scaled to
+    4096 rows x 16 layers. Each row's K/V projection is inside its QKV
+    projection, so the other rows' keys and values are random stand-ins."""
+    from oracle import pyoracle as orc
+    rng = np.random.default_rng(a.seed + 11)
+    T, Hd, V, H, Hkv, F, hd, eps = 4096, 2048, 1024, 32, 8, 8192, 64, 1e-5
+    levels = [256, 256, 512, 1024, 2048]
+    rb = orc.round_bf16
+
+    def wt(o, i):
+        return rb((rng.standard_normal((o, i)) * 0.02).astype(np.float32))
+
+    w_in, qkv, wo, gu, wd = wt(Hd, V), wt((H + 2 * Hkv) * hd, Hd), wt(Hd, H * hd), wt(2 * F, Hd), wt(Hd, F)
+    ln = np.ones(Hd, np.float32)
+    n_all = rb(rng.standard_normal((T, Hd)).astype(np.float32))
+    rows = np.sort(rng.choice(T, size=rows_sample, replace=False))
+    pos = np.asarray(orc.fill_level_positions(0, levels), np.int64)
+    _, c, s = orc.rope_default(hd, 500000.0, int(pos.max()) + 1)
+    cos, sin = c[pos], s[pos]
+    mask = orc.block_causal_mask(0, levels).astype(np.uint8)
+    # K and V of every row: their projection is each row's share of its timed
+    # QKV projection below, so random bf16 values stand in for them here
+    k = rb(rng.standard_normal((T, Hkv * hd)).astype(np.float32))
+    v = rb(rng.standard_normal((T, Hkv * hd)).astype(np.float32))
+    xin = rb(rng.standard_normal((rows_sample, V)).astype(np.float32))
+    t0 = time.perf_counter()
+    orc.matmul_bf16(xin, w_in, threads=threads)
+    t_in = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    hs = n_all[rows]
+    n1 = np.stack([orc.rms_norm(hs[i], ln, eps, bf16_mode=True) for i in range(rows_sample)])
+    q = orc.matmul_bf16(n1, qkv, threads=threads)[:, : H * hd].copy()
+    orc.lib().orc_rotate_rows(q, rows_sample, H, hd, np.ascontiguousarray(cos[rows]),
+                              np.ascontiguousarray(sin[rows]), 1)
+    ctx = np.empty((rows_sample, H * hd), np.float32)
+    orc.lib().orc_attention_core_rows(q, k, v, np.ascontiguousarray(mask[rows]), rows_sample, T, H, Hkv, hd, ctx, 1,
+                                      threads)
+    h2 = rb(hs + orc.matmul_bf16(ctx, wo, threads=threads))
+    n2 = np.stack([orc.rms_norm(h2[i], ln, eps, bf16_mode=True) for i in range(rows_sample)])
+    g_u = orc.matmul_bf16(n2, gu, threads=threads)
+    act = rb(orc.silu_bf16(g_u[:, :F]) * g_u[:, F:])
+    rb(h2 + orc.matmul_bf16(act, wd, threads=threads))
+    t_layer = time.perf_counter() - t0
+    per_row = (16 * t_layer + t_in) / rows_sample
+    return {"value": 1.0 / per_row, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": (f"extrapolated: one layer's per-row work on {rows_sample} random rows of 4096 (block-causal "
+                       f"attention against their allowed keys) plus the input projection, scaled to 4096 rows x 16 "
+                       f"layers")}
+
+
+def run_extras(a, dev):
+    """Configs 2-4 on the headline line (N = 1): each with its device and end-
+    to-end numbers, clocks, and a CPU baseline from the oracle port."""
+    import torch
+
+    from ncmorph_b200 import _lib, device as ndev
+    lib = _lib.load()
+    ctx = ndev.context(dev)
+    peaks, peak_kind = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(a.seed + 3)
+
+    def rnd(shape, scale=1.0):
+        return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    steps, warmup = max(5, min(a.steps, 20)), max(3, a.warmup)
+    threads = os.cpu_count() or 1
+    out = {}
+    out["tokenizer"] = measure_tokenizer(a, dev, lib, ctx, rnd, g, peaks, peak_kind, steps, warmup, graph=True)
+    out["tokenizer"]["cpu_baseline"] = cpu_tokenizer(a, threads)
+    torch.cuda.empty_cache()
+    out["decoder"] = measure_decoder(a, dev, lib, ctx, rnd, g, peaks, peak_kind, steps, warmup, graph=True)
+    out["decoder"]["cpu_baseline"] = cpu_decoder(a, threads)
+    torch.cuda.empty_cache()
+    out["linear_sweep"] = measure_linear(a, dev, rnd, peaks, peak_kind, steps, warmup)
+    out["linear_sweep"]["cpu_baseline"] = cpu_linear(threads)
+    ndev.sync(dev)
+    return out
+
+
+def run_secondary(a):
+    import torch
+
+    from ncmorph_b200 import _lib, device as ndev
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -714,173 +1109,20 @@ def run_secondary(a):
     def rnd(shape, scale=1.0):
         return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
 
-    sampler = ClockSampler(0)
     line = {"n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "none",
             "vs_baseline": None, "dtype": "bf16 operands, f32 accumulation", "data": "synthetic"}
-
+    threads = os.cpu_count() or 1
     if a.workload == "tokenizer":
-        B, T, Din, D, K, L = 8, 2048, 2048, 1024, 4096, 8
-        factors = [16, 8, 4, 2, 1]
-        x = rnd((B, T, Din))
-        w_in, w_out = rnd((D, Din), 0.02), rnd((Din, D), 0.02)
-        decay = torch.tensor([0.6 ** l for l in range(L)], device=dev).view(1, L, 1, 1)
-        cbs = (rnd((5, L, K, D)).float() * decay).to(torch.bfloat16)
-        sq = vq.code_sqnorm(cbs)
-        S = len(factors)
-        pw = pb = None
-        if a.phi:
-            bound = 1.0 / (3 * D) ** 0.5
-            pw = ((torch.rand((S, D, D, 3), generator=g, device=dev) * 2 - 1) * bound).to(torch.bfloat16)
-            pb = (torch.rand((S, D), generator=g, device=dev) * 2 - 1) * bound
-        tok = dict(sqnorms=sq, upsample=a.upsample, phi_weight=pw, phi_bias=pb, phi_ratio=0.5)
-        step = lambda: vq.tokenizer_forward(x, w_in, cbs, w_out, factors, **tok)  # noqa: E731
-        _timed_loop(step, 0, a.warmup)
-        lib.ncm_profile_read(ctx, b"*", None, None)
-        lib.ncm_profile_enable(ctx, 1)
-        _timed_loop(step, a.steps, 0)      # per-kernel breakdown (eager launches)
-        lib.ncm_profile_enable(ctx, 0)
-        run = _graphed(step, a.graph)
-        _timed_loop(run, 0, a.warmup)
-        sampler.start()
-        ms = _timed_loop(run, a.steps, 0)
-        clocks = sampler.stop()
-        prof = _profile(lib, ctx, ["rvq_argmin", "linear_bf16", "rvq_apply", "pool_avg", "scale_update", "cast",
-                                   "conv_k3", "upsample", "*"])
-        rows = sum(B * T // f for f in factors)
-        dist_flops = 2.0 * rows * K * D * L
-        proj_flops = 2 * 2.0 * B * T * Din * D
-        am_ms, am_n = prof["rvq_argmin"]
-        ln_ms, _ = prof["linear_bf16"]
-        x_host = torch.empty_like(x, device="cpu").pin_memory()
-        x_host.copy_(x.cpu())
-        codes_host = torch.empty(L * rows, dtype=torch.int32).pin_memory()
-        ms_e2e = _tokenizer_e2e(x, x_host, codes_host, lambda xb: vq.tokenizer_forward(xb, w_in, cbs, w_out, factors,
-                                                                                       **tok)[0], a.steps)
-        achieved = dist_flops / (am_ms / a.steps * 1e-3) / 1e12
-        line.update({
-            "metric": "tokenizer_vectors_per_s", "value": B * T / (ms * 1e-3), "unit": "vectors/s",
-            "ms_per_step": ms, "cuda_graph": bool(a.graph),
-            "config": {"workload": "multiscale tokenizer forward (BASELINE config 2)", "batch": B, "seq_len": T,
-                       "model_width": Din, "vq_width": D, "codebook_size": K, "levels_per_scale": L,
-                       "pool_factors": factors, "rows_quantised": rows, "upsample": a.upsample,
-                       "phi": bool(a.phi)},
-            "e2e": {"value": B * T / (ms_e2e * 1e-3), "unit": "vectors/s", "ms_per_step": ms_e2e,
-                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": codes_host.numel() * 4,
-                    "path": "vq.tokenizer_forward; the next step's input copy runs on a second stream"},
-            "roofline": {"bound": "tensor", "kernel": "rvq_argmin_kernel (all 40 levels)", "achieved": achieved,
-                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
-                         "frac": achieved / float(peaks["bf16_tflops"]),
-                         "peak_source": f"{peak_kind} bf16_tflops (burst; a 2-3 ms step)",
-                         "argmin_ms_per_step": am_ms / a.steps, "linear_ms_per_step": ln_ms / a.steps,
-                         "linear_tflops": proj_flops / (ln_ms / a.steps * 1e-3) / 1e12,
-                         "conv_tflops": (2.0 * B * T * 3 * D * D * S / (prof["conv_k3"][0] / a.steps * 1e-3) / 1e12
-                                         if a.phi and prof["conv_k3"][0] > 0 else None),
-                         "share_argmin": am_ms / max(sum(v[0] for v in prof.values()), 1e-9),
-                         "ms_per_step_by_kernel": {k: v[0] / a.steps for k, v in prof.items()}},
-            "gpu_launches": int(sum(v[1] for v in prof.values())), "clocks": clocks})
+        line.update(measure_tokenizer(a, dev, lib, ctx, rnd, g, peaks, peak_kind, a.steps, a.warmup, a.graph))
+        line["cpu_baseline"] = cpu_tokenizer(a, threads)
     elif a.workload == "linear":
-        Ms = [1, 64, 512, 4096, 8192]
-        KNs = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)]
-        rows, tot_flops, tot_ms = [], 0.0, 0.0
-        flush = _l2_flusher(dev)  # > L2: read between timed calls
-        sampler.start()
-        for M in Ms:
-            for (K, N) in KNs:
-                xx, ww = rnd((M, K)), rnd((N, K), 0.02)
-                yy = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-                for _ in range(a.warmup):
-                    kernels.linear_bf16(xx, ww, out=yy)
-                times = []
-                for _ in range(a.steps):
-                    flush()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    kernels.linear_bf16(xx, ww, out=yy)
-                    e1.record()
-                    torch.cuda.synchronize()
-                    times.append(e0.elapsed_time(e1))
-                t = sorted(times)[len(times) // 2]
-                fl = 2.0 * M * N * K
-                by = 2.0 * (M * K + N * K + M * N)
-                tot_flops += fl
-                tot_ms += t
-                ai = fl / by
-                roof = min(float(peaks["bf16_tflops"]) * 1e12, float(peaks["hbm_gbs"]) * 1e9 * ai)
-                rows.append({"M": M, "K": K, "N": N, "us": t * 1e3, "tflops": fl / (t * 1e-3) / 1e12,
-                             "gbs": by / (t * 1e-3) / 1e9, "frac_of_roofline": fl / (t * 1e-3) / roof})
-                del xx, ww, yy
-        clocks = sampler.stop()
-        line.update({
-            "metric": "linear_sweep_tflops", "value": tot_flops / (tot_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": tot_ms,
-            "config": {"workload": "bf16 linear sweep, Llama-3.2-1B shapes (BASELINE config 3)",
-                       "l2": "256 MiB buffer read between timed calls (L2 cold and clean)", "shapes": rows},
-            "roofline": {"bound": "min(tensor, hbm x intensity) per shape",
-                         "peak_source": f"{peak_kind} bf16_tflops / hbm_gbs"},
-            "clocks": clocks})
+        line.update(measure_linear(a, dev, rnd, peaks, peak_kind, a.steps, a.warmup))
+        line["cpu_baseline"] = cpu_linear(threads)
     elif a.workload == "aux":
         line.update(_aux_suite(a, dev, rnd, peaks, peak_kind))
     else:  # decoder
-        cfg = ncm_model.Config(hidden_size=2048, vq_width=1024, num_attention_heads=32, num_key_value_heads=8,
-                               intermediate_size=8192, level_lengths=(256, 256, 512, 1024, 2048),
-                               mask="block_causal")
-        Hd, F = cfg.hidden_size, cfg.intermediate_size
-        layers = [ncm_model.LayerWeights(ln_1=rnd((Hd,), 0.0) + 1, qkv=rnd((3072, Hd), 0.02), o=rnd((Hd, 2048), 0.02),
-                                         ln_2=rnd((Hd,), 0.0) + 1, gate_up=rnd((2 * F, Hd), 0.02),
-                                         down=rnd((Hd, F), 0.02)) for _ in range(16)]
-        w = ncm_model.Weights(input_projection=rnd((Hd, cfg.vq_width), 0.02), input_projection_bias=rnd((Hd,), 0.02),
-                              level_embedding=rnd((5, Hd), 0.02), final_norm=rnd((Hd,), 0.0) + 1, layers=layers)
-        table = rnd((4096, cfg.vq_width))
-        codes = torch.randint(0, 4096, (cfg.seq_len,), generator=g, device=dev, dtype=torch.int32)
-        out = torch.empty((cfg.seq_len, Hd), dtype=torch.bfloat16, device=dev)
-
-        def step():
-            inputs = ncm_model.embedding_gather(table, codes)
-            ncm_model.forward(cfg, w, inputs, out=out)
-
-        _timed_loop(step, 0, a.warmup)
-        lib.ncm_profile_read(ctx, b"*", None, None)
-        lib.ncm_profile_enable(ctx, 1)
-        _timed_loop(step, a.steps, 0)      # per-kernel breakdown (eager launches)
-        lib.ncm_profile_enable(ctx, 0)
-        run = _graphed(step, a.graph)
-        _timed_loop(run, 0, a.warmup)
-        sampler.start()
-        ms = _timed_loop(run, a.steps, 0)
-        clocks = sampler.stop()
-        prof = _profile(lib, ctx, ["linear_bf16", "attention", "*"])
-        T = cfg.seq_len
-        lin_flops = 16 * 2.0 * T * Hd * (3072 + 2048 + 3 * F) + 2.0 * T * cfg.vq_width * Hd
-        lv = list(cfg.level_lengths)
-        allowed = sum(n * sum(lv[: i + 1]) for i, n in enumerate(lv))
-        att_flops = 16 * 4.0 * allowed * 32 * 64
-        ln_ms, ln_n = prof["linear_bf16"]
-        at_ms, at_n = prof["attention"]
-        codes_host = codes.cpu().pin_memory()
-        out_host = torch.empty((T, Hd), dtype=torch.bfloat16).pin_memory()
-
-        def step_e2e():
-            codes.copy_(codes_host, non_blocking=True)
-            step()
-            out_host.copy_(out, non_blocking=True)
-
-        ms_e2e = _timed_loop(step_e2e, a.steps, 1)
-        lin_ach = lin_flops / (ln_ms / a.steps * 1e-3) / 1e12
-        line.update({
-            "metric": "decoder_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
-            "cuda_graph": bool(a.graph),
-            "config": {"workload": "NCM decoder forward (BASELINE config 4)", "layers": 16, "d_model": Hd,
-                       "heads": 32, "kv_heads": 8, "head_dim": 64, "ffn": F, "positions": T,
-                       "levels": lv, "mask": "block_causal", "flops_linear": lin_flops, "flops_attention": att_flops},
-            "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
-                    "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": T * Hd * 2},
-            "roofline": {"bound": "tensor", "kernel": "linear_bf16_kernel", "achieved": lin_ach,
-                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
-                         "frac": lin_ach / float(peaks["bf16_tflops"]), "peak_source": f"{peak_kind} bf16_tflops",
-                         "linear_ms_per_step": ln_ms / a.steps, "attention_ms_per_step": at_ms / a.steps,
-                         "attention_tflops": att_flops / (at_ms / a.steps * 1e-3) / 1e12,
-                         "other_ms_per_step": prof["*"][0] / a.steps},
-            "gpu_launches": int(ln_n + at_n + prof["*"][1]), "clocks": clocks})
+        line.update(measure_decoder(a, dev, lib, ctx, rnd, g, peaks, peak_kind, a.steps, a.warmup, a.graph))
+        line["cpu_baseline"] = cpu_decoder(a, threads)
     ndev.sync(dev)
     emit(line)
     return 0

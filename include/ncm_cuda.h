@@ -173,6 +173,31 @@ NCM_API int ncm_rvq_encode_sharded(ncm_ctx_t* ctx, const uint16_t* x_local, cons
                                    const float* sqnorms, int32_t L, int32_t* codes_all, uint16_t* recon_all,
                                    int64_t n_local, int64_t D, int64_t K, ncm_stream_t stream);
 
+/* Peer copies for the same exchange without SMs. No counterpart in the
+ * reference (single CPU thread, no distributed mode). One process per GPU on
+ * one node: a rank exports the IPC handle of a device buffer it allocated
+ * with cudaMalloc (ncm_ipc_export records the buffer's offset inside its
+ * allocation), ships the handle to the other ranks, and each maps it with
+ * ncm_ipc_open, which returns the buffer's address in that process (unmap
+ * with ncm_ipc_close). ncm_copy_async and ncm_copy2d_async are
+ * cudaMemcpyAsync / cudaMemcpy2DAsync device-to-device on `stream`: with a
+ * peer's mapping as source or destination they run on the copy engines over
+ * NVLink, so the exchange takes no SM from kernels running meanwhile.
+ * Ordering between ranks is the caller's: a copy into a peer's buffer must
+ * start after the peer is done with it, and the peer may read it only after
+ * the copy completed (a collective barrier on both sides serves). */
+typedef struct ncm_ipc_handle {
+  uint8_t handle[64]; /* cudaIpcMemHandle_t of the allocation */
+  uint64_t offset;    /* the buffer's offset inside that allocation */
+  uint64_t bytes;     /* the buffer's size */
+} ncm_ipc_handle_t;
+NCM_API int ncm_ipc_export(const void* dev_ptr, uint64_t bytes, ncm_ipc_handle_t* out);
+NCM_API int ncm_ipc_open(const ncm_ipc_handle_t* handle, void** dev_ptr_out);
+NCM_API int ncm_ipc_close(void* dev_ptr);
+NCM_API int ncm_copy_async(void* dst, const void* src, uint64_t bytes, ncm_stream_t stream);
+NCM_API int ncm_copy2d_async(void* dst, uint64_t dst_pitch, const void* src, uint64_t src_pitch,
+                             uint64_t width_bytes, uint64_t rows, ncm_stream_t stream);
+
 /* Area pooling by an integer factor (F.interpolate mode="area" with T % factor == 0,
  * vq_forward_semantics.md:67,80): y[b,j,:] = (sum_{i<factor} x[b,j*factor+i,:]) / factor,
  * summed in increasing i in f32. x [B,T,D] f32, y [B,T/factor,D] f32. */
@@ -352,6 +377,15 @@ NCM_API int ncm_embedding_gather(ncm_ctx_t* ctx, const uint16_t* table, int64_t 
 NCM_API int ncm_rope_tables_host(int32_t head_dim, float theta, const int32_t* positions, int64_t T, float* cos_out,
                                  float* sin_out);
 
+/* Host function: the same tables from Llama 3 scaled frequencies, as
+ * rope_llama3 (packages/kernels/root.zig:636-666) adjusts rope_default's
+ * (factor, low/high frequency factors, original context length: the
+ * rope_scaling of a Llama 3 config.json). Its assertions (:645-648) are
+ * reported as NCM_EINVAL. */
+NCM_API int ncm_rope_tables_llama3_host(int32_t head_dim, float theta, float factor, float low_freq_factor,
+                                        float high_freq_factor, int64_t original_max_position_embeddings,
+                                        const int32_t* positions, int64_t T, float* cos_out, float* sin_out);
+
 /* Attention mask description. mode: 0 causal (causal_mask, root.zig:380-399,
  * no sliding window), 1 block-diagonal (src/ncm_mask.zig:10-42), 2 block-causal
  * (each level also sees every earlier level). In block modes positions are
@@ -400,9 +434,16 @@ typedef struct ncm_decoder_config {
   int64_t head_dim; /* must be 64 */
   int64_t intermediate_size;
   float rms_norm_epsilon;
-  float rope_theta; /* default RoPE (rope_default) */
+  float rope_theta; /* RoPE base (rope_default's theta) */
   int32_t use_level_encoding;
   ncm_mask_t mask;
+  /* RoPE frequencies: 0 rope_default, 1 rope_llama3 (root.zig:636-666) with
+   * the four parameters below (ignored for 0) */
+  int32_t rope_type;
+  float rope_factor;
+  float rope_low_freq_factor;
+  float rope_high_freq_factor;
+  int64_t rope_original_max_position_embeddings;
 } ncm_decoder_config_t;
 
 typedef struct ncm_decoder_layer_weights {
@@ -442,17 +483,27 @@ NCM_API int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, con
  * allocation (its arena or caching allocator must account for all memory),
  * and latency-bound paths that may not stall on cudaMalloc, which can
  * synchronise the device. It takes no context and allocates
- * nothing: its scratch (the bf16 copy of the residual, the per-split argmin
- * partials, the code norms when sqnorm is NULL, an error word) is a 16 MiB
- * device array that every GPU loading the library holds until exit, so
- * 2*N*D + 4*K bytes (plus split partials) must fit in it; larger problems
- * are rejected with NCM_EINVAL. It runs on the current device; the first call
- * on each device looks up the array's device address (make that call before
- * any stream capture). All calls share the array: calls that overlap on the
- * GPU race. Results equal ncm_rvq_level's; device-side failures are not
- * reported (there is no context to carry them). */
+ * nothing: its scratch (an error word, the bf16 copy of the residual, the
+ * per-split argmin partials, the code norms when sqnorm is NULL) is a 16 MiB
+ * device array that every GPU loading the library holds
+ * until exit, so 2*N*D + 4*K bytes (plus split partials) must fit in it;
+ * larger problems are rejected with NCM_EINVAL. It runs on the current
+ * device, in the current CUDA context; the first call in each context looks
+ * up the array's device address (make that call before any stream capture).
+ * All calls share the array: calls that overlap on the GPU race. It runs
+ * ncm_rvq_level's plan and kernels, so codes and residual equal that entry
+ * point's bit for bit. Device-side failures (a bounded wait that gave up, an
+ * out-of-range code) accumulate in the array's error word until
+ * ncm_rvq_level_noalloc_status reads it. */
 NCM_API int ncm_rvq_level_noalloc(float* residual, const uint16_t* codebook, const float* sqnorm, int32_t* codes,
                                   int64_t N, int64_t D, int64_t K, ncm_stream_t stream);
+
+/* No counterpart in the reference (companion of ncm_rvq_level_noalloc, which
+ * has no context to carry errors). Waits for `stream`, reads the error word of
+ * the current context's no-allocation scratch into *flags (nullable; bit 1 a
+ * wait timed out, bit 2 an out-of-range index), clears it, and returns NCM_OK,
+ * NCM_ETIMEOUT or NCM_ERANGE accordingly. Allocates nothing. */
+NCM_API int ncm_rvq_level_noalloc_status(ncm_stream_t stream, int32_t* flags);
 
 /* ------------------------------------------------------- measurement */
 

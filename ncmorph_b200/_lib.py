@@ -54,6 +54,12 @@ class Mask(ctypes.Structure):
     ]
 
 
+class IpcHandle(ctypes.Structure):
+    """Mirror of ncm_ipc_handle_t."""
+
+    _fields_ = [("handle", ctypes.c_uint8 * 64), ("offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
+
+
 class DecoderConfig(ctypes.Structure):
     """Mirror of ncm_decoder_config_t."""
 
@@ -68,6 +74,11 @@ class DecoderConfig(ctypes.Structure):
         ("rope_theta", ctypes.c_float),
         ("use_level_encoding", c_i32),
         ("mask", Mask),
+        ("rope_type", c_i32),
+        ("rope_factor", ctypes.c_float),
+        ("rope_low_freq_factor", ctypes.c_float),
+        ("rope_high_freq_factor", ctypes.c_float),
+        ("rope_original_max_position_embeddings", c_i64),
     ]
 
 
@@ -115,9 +126,12 @@ SIGNATURES: dict[str, list] = {
     "ncm_rms_norm_bf16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp],
     "ncm_embedding_gather": [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     "ncm_rope_tables_host": [c_i32, ctypes.c_float, c_vp, c_i64, c_vp, c_vp],
+    "ncm_rope_tables_llama3_host": [c_i32, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_i64,
+                                    c_vp, c_i64, c_vp, c_vp],
     "ncm_attention_bf16": [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, ctypes.POINTER(Mask), c_vp],
     "ncm_ncm_forward": [c_vp, ctypes.POINTER(DecoderConfig), ctypes.POINTER(DecoderWeights), c_vp, c_vp, c_vp],
     "ncm_rvq_level_noalloc": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
+    "ncm_rvq_level_noalloc_status": [c_vp, ctypes.POINTER(c_i32)],
     "ncm_profile_enable": [c_vp, ctypes.c_int],
     "ncm_profile_read": [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i64)],
     "ncm_tokenizer_forward": [c_vp, ctypes.POINTER(TokenizerConfig), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
@@ -130,6 +144,11 @@ SIGNATURES: dict[str, list] = {
     "ncm_tied_head_argmax": [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_comm_unique_id": [c_vp],
     "ncm_ctx_comm_init": [c_vp, c_vp, c_i32, c_i32],
+    "ncm_ipc_export": [c_vp, ctypes.c_uint64, ctypes.POINTER(IpcHandle)],
+    "ncm_ipc_open": [ctypes.POINTER(IpcHandle), ctypes.POINTER(c_vp)],
+    "ncm_ipc_close": [c_vp],
+    "ncm_copy_async": [c_vp, c_vp, ctypes.c_uint64, c_vp],
+    "ncm_copy2d_async": [c_vp, ctypes.c_uint64, c_vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, c_vp],
     "ncm_rvq_encode_sharded": [c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_load_tensor_bf16": [c_vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64, c_i32, c_vp, c_vp],
     "ncm_qkv_projection_rope": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i32, c_i32, c_vp],

@@ -156,9 +156,10 @@ static int rvq_level_core(ncm_ctx* ctx, const uint16_t* a_bf16, const uint16_t* 
     return ncm_fail(NCM_EINVAL, "rvq: tensor map encoding failed (N=%lld D=%lld K=%lld)", (long long)N,
                     (long long)D, (long long)K);
   // Code splits merge inside the distance kernel (split fixup) only when no
-  // update follows: with an update, the CTA finishing a row block would run
-  // the whole 128-row update at the end of the kernel on one SM, while
-  // rvq_apply_kernel spreads it over every SM (measured 6x faster).
+  // update follows: the CTA finishing a row block's last split writes its
+  // codes. With an update, rvq_apply_kernel merges and updates over every SM
+  // (the update at the end of the distance kernel measured slower at every
+  // split size, whether one CTA or all of a row block's CTAs ran it).
   const bool fixup = plan.splits > 1 && top2 == nullptr && !update;
   int* counters = fixup ? rvq_counters(ctx, plan.row_blocks) : nullptr;
   const bool merged = plan.splits == 1 || counters != nullptr;

@@ -270,14 +270,40 @@ cudaError_t launch_embedding_gather(const uint16_t* table, int vocab, int width,
   return cudaGetLastError();
 }
 
-// RoPE cos/sin tables at explicit positions, on the host with libm exactly as
-// rope_default + rope_tables + tables_at_positions compute them
-// (packages/kernels/root.zig:305-348, src/ncm_position.zig:71-118).
-void rope_tables_host(int head_dim, float theta, const int* positions, int T, float* cos_out, float* sin_out) {
+// RoPE inverse frequencies with libm, in the reference's f32 operation order:
+// rope_default (packages/kernels/root.zig:305-316, :668-674), and with
+// `llama3` the Llama 3 adjustment of rope_llama3 (root.zig:636-666).
+void rope_inv_freq(int head_dim, float theta, const RopeLlama3* llama3, float* inv) {
   const int half = head_dim / 2;
-  std::vector<float> inv(half);
   const float hdf = static_cast<float>(head_dim);
   for (int i = 0; i < half; ++i) inv[i] = 1.0f / powf(theta, static_cast<float>(2 * i) / hdf);
+  if (llama3 == nullptr) return;
+  const float factor = llama3->factor, low = llama3->low_freq_factor, high = llama3->high_freq_factor;
+  const float old_ctx = static_cast<float>(llama3->original_max_position_embeddings);
+  const float low_wl =
+      static_cast<float>(static_cast<double>(llama3->original_max_position_embeddings) / static_cast<double>(low));
+  const float high_wl =
+      static_cast<float>(static_cast<double>(llama3->original_max_position_embeddings) / static_cast<double>(high));
+  const float two_pi = static_cast<float>(2.0 * 3.14159265358979323846);
+  for (int i = 0; i < half; ++i) {
+    const float f = inv[i];
+    const float wl = two_pi / f;
+    const float lf = wl > low_wl ? f / factor : f;
+    const float sm = (old_ctx / wl - low) / (high - low);
+    const float smoothed = (1.0f - sm) * lf / factor + sm * lf;
+    const bool medium = !(wl < high_wl) && !(wl > low_wl);
+    inv[i] = medium ? smoothed : lf;
+  }
+}
+
+// RoPE cos/sin tables at explicit positions, on the host with libm exactly as
+// rope_tables + tables_at_positions compute them (packages/kernels/root.zig:318-348,
+// src/ncm_position.zig:71-118), from rope_default's or rope_llama3's frequencies.
+void rope_tables_host(int head_dim, float theta, const int* positions, int T, float* cos_out, float* sin_out,
+                      const RopeLlama3* llama3) {
+  const int half = head_dim / 2;
+  std::vector<float> inv(half);
+  rope_inv_freq(head_dim, theta, llama3, inv.data());
   for (int t = 0; t < T; ++t) {
     const float pf = static_cast<float>(positions[t]);
     for (int i = 0; i < half; ++i) {

@@ -174,7 +174,14 @@ cudaError_t launch_add_level_embedding(uint16_t* h, const uint16_t* emb, const i
                                        cudaStream_t st);
 cudaError_t launch_embedding_gather(const uint16_t* table, int vocab, int width, const int32_t* ids, int T,
                                     uint16_t* out, int* err, cudaStream_t st);
-void rope_tables_host(int head_dim, float theta, const int* positions, int T, float* cos_out, float* sin_out);
+// Llama 3 frequency scaling (rope_llama3's parameters).
+struct RopeLlama3 {
+  float factor, low_freq_factor, high_freq_factor;
+  int64_t original_max_position_embeddings;
+};
+void rope_inv_freq(int head_dim, float theta, const RopeLlama3* llama3, float* inv);
+void rope_tables_host(int head_dim, float theta, const int* positions, int T, float* cos_out, float* sin_out,
+                      const RopeLlama3* llama3 = nullptr);
 // Fused masked attention over the Q and K columns of fused QKV rows (row
 // stride qkv_stride elements) and V transposed to [Hkv*64, T]; head_dim 64.
 // mode 0 causal, 1 block-diagonal, 2 block-causal.

@@ -80,6 +80,19 @@ int ncm_rope_tables_host(int32_t head_dim, float theta, const int32_t* positions
   return NCM_OK;
 }
 
+int ncm_rope_tables_llama3_host(int32_t head_dim, float theta, float factor, float low_freq_factor,
+                                float high_freq_factor, int64_t original_max_position_embeddings,
+                                const int32_t* positions, int64_t T, float* cos_out, float* sin_out) {
+  // the preconditions rope_llama3 asserts (packages/kernels/root.zig:645-648), reported instead
+  if (head_dim <= 0 || head_dim % 2 != 0 || !(theta > 0.f) || !(factor > 0.f) || !(low_freq_factor > 0.f) ||
+      !(high_freq_factor > low_freq_factor) || original_max_position_embeddings <= 0 || T < 0 ||
+      (T > 0 && (!positions || !cos_out || !sin_out)))
+    return ncm_fail(NCM_EINVAL, "rope_tables_llama3: bad arguments");
+  const RopeLlama3 l3{factor, low_freq_factor, high_freq_factor, original_max_position_embeddings};
+  rope_tables_host(head_dim, theta, positions, static_cast<int>(T), cos_out, sin_out, &l3);
+  return NCM_OK;
+}
+
 int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t, const float* sin_t,
                        uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
                        ncm_stream_t stream) {
@@ -153,6 +166,10 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   const int64_t Hd = cfg->hidden_size, V = cfg->vq_width, F = cfg->intermediate_size;
   const int H = static_cast<int>(cfg->num_attention_heads), Hkv = static_cast<int>(cfg->num_key_value_heads);
   if (cfg->head_dim != 64) return ncm_fail(NCM_EINVAL, "ncm_forward: head_dim must be 64");
+  if (cfg->rope_type != 0 &&
+      (cfg->rope_type != 1 || !(cfg->rope_factor > 0.f) || !(cfg->rope_low_freq_factor > 0.f) ||
+       !(cfg->rope_high_freq_factor > cfg->rope_low_freq_factor) || cfg->rope_original_max_position_embeddings <= 0))
+    return ncm_fail(NCM_EINVAL, "ncm_forward: rope_type %d or its llama3 parameters are invalid", cfg->rope_type);
   if (Hd <= 0 || V <= 0 || F <= 0 || Hd % 8 || V % 8 || F % 8 || H <= 0 || Hkv <= 0 || H % Hkv)
     return ncm_fail(NCM_EINVAL, "ncm_forward: bad dimensions");
   if ((rc = check_mask(&m, T))) return rc;
@@ -206,6 +223,15 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   mix(theta_bits);
   mix(static_cast<uint64_t>(m.prefix_length));
   mix(static_cast<uint64_t>(cfg->use_level_encoding));
+  mix(static_cast<uint64_t>(cfg->rope_type));
+  if (cfg->rope_type == 1) {
+    uint32_t b[3];
+    std::memcpy(&b[0], &cfg->rope_factor, 4);
+    std::memcpy(&b[1], &cfg->rope_low_freq_factor, 4);
+    std::memcpy(&b[2], &cfg->rope_high_freq_factor, 4);
+    for (uint32_t v : b) mix(v);
+    mix(static_cast<uint64_t>(cfg->rope_original_max_position_embeddings));
+  }
   for (int i = 0; i < m.num_levels; ++i) mix(static_cast<uint64_t>(m.level_lengths[i]));
   if (key != ctx->rope_key || ctx->rope_cos == nullptr) {
     std::vector<int> pos(T), lev(T);
@@ -214,7 +240,10 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
     for (int i = 0; i < m.num_levels; ++i)
       for (int p = 0; p < m.level_lengths[i]; ++p, ++t) pos[t] = p, lev[t] = cfg->use_level_encoding ? i : -1;
     std::vector<float> ch(T * 64), sh(T * 64);
-    rope_tables_host(64, cfg->rope_theta, pos.data(), static_cast<int>(T), ch.data(), sh.data());
+    const RopeLlama3 l3{cfg->rope_factor, cfg->rope_low_freq_factor, cfg->rope_high_freq_factor,
+                        cfg->rope_original_max_position_embeddings};
+    rope_tables_host(64, cfg->rope_theta, pos.data(), static_cast<int>(T), ch.data(), sh.data(),
+                     cfg->rope_type == 1 ? &l3 : nullptr);
     NCM_CUDA_TRY(cudaStreamSynchronize(st));  // no forward in flight still reads the old tables
     if (T > ctx->rope_rows) {
       cudaFree(ctx->rope_cos);

@@ -18,8 +18,15 @@
 //              while the tensor cores already work on the next row block
 //
 // A work unit is (row block of 128 residuals, range of code tiles). When the
-// rows alone cannot fill the GPU the code range is split, each split writes a
-// (distance, index) partial per row, and rvq_apply_kernel reduces them.
+// rows alone cannot fill the GPU the code range is split and each split
+// writes a (distance, index) partial per row. The splits are then merged by
+// rvq_apply_kernel, which also applies the residual update over every SM, or,
+// when no update follows, by the CTA that finishes a row block's last split.
+// (A cooperative variant, in which every split's CTA waited for the row
+// block's other splits and updated its own column slice, measured slower at
+// every size from 1,024 to 8,192 rows: the update then ran at the end of the
+// kernel on 8 warps per SM, with far less memory parallelism than the
+// separate full-GPU apply launch.)
 #include <algorithm>
 #include <cfloat>
 #include <climits>
@@ -93,9 +100,9 @@ struct ArgminArgs {
   const uint16_t* codebook;
   // dist = fmaf(mul, acc, csq[k]); mul = -2 (RVQ) or *mul_dev when given (tied head)
   const float* mul_dev;
-  // split fixup (splits > 1): per row block arrival counters (zero before the
-  // launch, zero again after it); the CTA that completes a row block's last
-  // split merges the partials, writes the codes and runs the fused update
+  // split fixup (splits > 1, no update): per row block arrival counters
+  // (zero before the launch, zero again after it); the CTA that completes a
+  // row block's last split merges the partials and writes the codes
   int* counters;
   // top-2 gap (the GAP instantiation only)
   float* gap;        // [N] relative gap, splits == 1
@@ -1071,9 +1078,10 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
   a.tiles_per_split = plan.tiles_per_split;
   a.code_tiles = plan.code_tiles;
   a.n_units = plan.n_units;
-  // the split fixup needs counters and does not carry the top-2 gap
-  a.counters = (plan.splits > 1 && top2 == nullptr) ? counters : nullptr;
-  a.fuse = (fu != nullptr && (plan.splits == 1 || a.counters != nullptr)) ? 1 : 0;
+  // the split fixup needs counters, does not carry the top-2 gap, and writes
+  // codes only (an update after a split plan is rvq_apply_kernel's)
+  a.counters = (plan.splits > 1 && top2 == nullptr && fu == nullptr) ? counters : nullptr;
+  a.fuse = (fu != nullptr && plan.splits == 1) ? 1 : 0;
   a.resid = fu ? fu->resid : nullptr;
   a.src_bf16 = fu ? fu->src_bf16 : nullptr;
   a.shadow = fu ? fu->shadow : nullptr;

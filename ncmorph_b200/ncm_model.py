@@ -44,14 +44,23 @@ def level_positions(prefix_length: int, level_lengths) -> np.ndarray:
     return np.asarray(pos, dtype=np.int32)
 
 
-def rope_tables(head_dim: int, theta: float, positions) -> tuple[np.ndarray, np.ndarray]:
-    """Host RoPE tables [T, head_dim] with libm, as the reference builds them."""
+def rope_tables(head_dim: int, theta: float, positions, llama3: tuple | None = None
+                ) -> tuple[np.ndarray, np.ndarray]:
+    """Host RoPE tables [T, head_dim] with libm, as the reference builds them:
+    rope_default's frequencies, or rope_llama3's when `llama3` = (factor,
+    low_freq_factor, high_freq_factor, original_max_position_embeddings)."""
     pos = np.ascontiguousarray(positions, dtype=np.int32)
     T = pos.size
     c = np.empty((T, head_dim), np.float32)
     s = np.empty((T, head_dim), np.float32)
-    _lib.call("ncm_rope_tables_host", head_dim, float(theta), ctypes.c_void_p(pos.ctypes.data), T,
-              ctypes.c_void_p(c.ctypes.data), ctypes.c_void_p(s.ctypes.data))
+    vp = ctypes.c_void_p
+    if llama3 is None:
+        _lib.call("ncm_rope_tables_host", head_dim, float(theta), vp(pos.ctypes.data), T, vp(c.ctypes.data),
+                  vp(s.ctypes.data))
+    else:
+        factor, low, high, orig = llama3
+        _lib.call("ncm_rope_tables_llama3_host", head_dim, float(theta), float(factor), float(low), float(high),
+                  int(orig), vp(pos.ctypes.data), T, vp(c.ctypes.data), vp(s.ctypes.data))
     return c, s
 
 
@@ -126,6 +135,10 @@ class Config:
     rope_theta: float = 500000.0
     use_level_encoding: bool = True
     head_dim: int = 64
+    # Llama 3 frequency scaling (rope_llama3, packages/kernels/root.zig:636-666):
+    # (factor, low_freq_factor, high_freq_factor, original_max_position_embeddings),
+    # or None for rope_default
+    rope_llama3: tuple | None = None
 
     @property
     def seq_len(self) -> int:
@@ -147,6 +160,10 @@ def forward(cfg: Config, w: Weights, inputs: torch.Tensor, out: torch.Tensor | N
     c.rms_norm_epsilon, c.rope_theta = cfg.rms_norm_epsilon, cfg.rope_theta
     c.use_level_encoding = int(cfg.use_level_encoding)
     c.mask = make_mask(cfg.mask, cfg.prefix_length, cfg.level_lengths)
+    if cfg.rope_llama3 is not None:
+        c.rope_type = 1
+        (c.rope_factor, c.rope_low_freq_factor, c.rope_high_freq_factor,
+         c.rope_original_max_position_embeddings) = cfg.rope_llama3
     layers = (_lib.DecoderLayerWeights * len(w.layers))()
     for i, L in enumerate(w.layers):
         for name in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down"):

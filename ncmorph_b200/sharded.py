@@ -44,11 +44,22 @@ class ShardedEncoder:
     stream while the next call already encodes (two buffer sets, so results
     stay valid until the call after next). Call `wait()` before the current
     stream reads a call's results; a device-wide synchronize also covers them.
+    A call must be made after the caller's reads of the results of the call
+    before last (on any stream) are ordered before the current stream.
+
+    transport: "nccl" gathers with all_gather_into_tensor (NCCL kernels);
+    "peer" pushes this rank's codes and reconstructions straight into every
+    other rank's output buffers with copy-engine copies over CUDA IPC
+    mappings (ncm_ipc_* / ncm_copy*_async), so the exchange takes no SMs
+    from the encode it overlaps. Each peer exchange is bracketed by two
+    one-element all-reduces on the group (every rank has finished encoding
+    this call, so its buffers are free; every rank's copies have landed).
+    The peer transport needs every rank on one node and overlap=True.
     """
 
     def __init__(self, codebooks: torch.Tensor, total_rows: int, x_dtype: torch.dtype = torch.bfloat16,
                  sqnorms: torch.Tensor | None = None, group=None, encode: Callable | None = None,
-                 overlap: bool = False):
+                 overlap: bool = False, transport: str = "nccl"):
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.group = group
@@ -74,6 +85,92 @@ class ShardedEncoder:
             self.encoded = [torch.cuda.Event() for _ in range(sets)]
             self.gathered = [torch.cuda.Event() for _ in range(sets)]
             self.used = [False] * sets
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.peers = None
+        if transport == "peer" and self.world > 1:
+            if not overlap:
+                raise ValueError("the peer transport streams batches: use overlap=True")
+            self._setup_peers()
+
+    # ------------------------------------------------------------ peer transport
+    def _setup_peers(self) -> None:
+        """Exchanges the IPC handles of every rank's output buffers and maps
+        the peers' ones: peers[b][r] = (codes_out base, recon_all base) of rank
+        r's buffer set b, as addresses in this process."""
+        import ctypes
+
+        from . import _lib
+        lib = _lib.load()
+        mine = []
+        for b in range(len(self.codes_out)):
+            for t in (self.codes_out[b], self.recon_all[b]):
+                h = _lib.IpcHandle()
+                _lib.check(lib.ncm_ipc_export(ctypes.c_void_p(t.data_ptr()), t.numel() * t.element_size(),
+                                              ctypes.byref(h)))
+                mine.append(bytes(h))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.group)
+        self.peers = []
+        self._opened = []
+        for b in range(len(self.codes_out)):
+            row = []
+            for r in range(self.world):
+                if r == self.rank:
+                    row.append((self.codes_out[b].data_ptr(), self.recon_all[b].data_ptr()))
+                    continue
+                ptrs = []
+                for k in range(2):
+                    h = _lib.IpcHandle.from_buffer_copy(everyone[r][2 * b + k])
+                    p = ctypes.c_void_p()
+                    _lib.check(lib.ncm_ipc_open(ctypes.byref(h), ctypes.byref(p)))
+                    self._opened.append(p.value)
+                    ptrs.append(p.value)
+                row.append(tuple(ptrs))
+            self.peers.append(row)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.codebooks.device)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (peer transport); collective."""
+        if self.peers is None:
+            return
+        from . import _lib
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            _lib.check(_lib.load().ncm_ipc_close(p))
+        self._opened = []
+        self.peers = None
+
+    def _barrier(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _push(self, b: int) -> None:
+        """On the comm stream: rank r's codes [L, n] go to columns
+        [r*n, (r+1)*n) of every rank's codes_out[b] (a pitched copy) and its
+        reconstruction rows (encoded in place in recon_all[b]) to the same
+        rows of every peer's recon_all[b]."""
+        import ctypes
+
+        from . import _lib
+        lib = _lib.load()
+        st = ctypes.c_void_p(self.comm.cuda_stream)
+        L, n, D = self.L, self.n, self.recon_all[b].shape[1]
+        es = self.recon_all[b].element_size()
+        rec_off = self.rank * n * D * es
+        src_rec = self.recon_all[b].data_ptr() + rec_off
+        src_codes = self.codes_pad[b].data_ptr()
+        self._barrier()                      # every rank's buffers of set b are free
+        for k in range(1, self.world + 1):
+            r = (self.rank + k) % self.world  # staggered: rank r's first copy goes to r+1
+            codes_dst, recon_dst = self.peers[b][r]
+            _lib.check(lib.ncm_copy2d_async(ctypes.c_void_p(codes_dst + self.rank * n * 4), self.world * n * 4,
+                                            ctypes.c_void_p(src_codes), n * 4, n * 4, L, st))
+            if r != self.rank:
+                _lib.check(lib.ncm_copy_async(ctypes.c_void_p(recon_dst + rec_off), ctypes.c_void_p(src_rec),
+                                              n * D * es, st))
+        self._barrier()                      # every rank's copies into this rank's buffers have landed
 
     @property
     def rows(self) -> int:
@@ -98,17 +195,24 @@ class ShardedEncoder:
         cur = torch.cuda.current_stream() if self.overlap else None
         if self.overlap and self.used[b]:
             cur.wait_event(self.gathered[b])  # this buffer set's previous gathers have finished
+        # the peer transport encodes the reconstruction straight into this
+        # rank's rows of the gathered output
+        recon_dst = (self.recon_all[b][self.rank * self.n:(self.rank + 1) * self.n] if self.peers is not None
+                     else self.recon_pad[b])
         if valid == self.n:
-            self.encode(x_local, self.codebooks, self.sqnorms, self.codes_pad[b], self.recon_pad[b])
+            self.encode(x_local, self.codebooks, self.sqnorms, self.codes_pad[b], recon_dst)
         elif valid > 0:  # short last shard: encode into dense buffers, then pad
             codes = torch.empty((self.L, valid), dtype=torch.int32, device=x_local.device)
-            self.encode(x_local, self.codebooks, self.sqnorms, codes, self.recon_pad[b][:valid])
+            self.encode(x_local, self.codebooks, self.sqnorms, codes, recon_dst[:valid])
             self.codes_pad[b][:, :valid] = codes
         if self.overlap:
             self.encoded[b].record(cur)
             with torch.cuda.stream(self.comm):
                 self.comm.wait_event(self.encoded[b])
-                self._gather(b)
+                if self.peers is not None:
+                    self._push(b)
+                else:
+                    self._gather(b)
                 self.gathered[b].record(self.comm)
             self.used[b] = True
         else:

@@ -148,6 +148,39 @@ void rotate_head(float* v, const float* c, const float* s, size_t n, bool bm) {
   }
 }
 
+// packages/kernels/root.zig:537-575: one query row and head against every
+// key row: bf16-mode scores bf16(bf16(q.k) * 1/sqrt(hd)) over the allowed
+// keys, softmax, bf16 probabilities, context sums in increasing key order.
+void attend_row(const float* q, const float* Kt, const float* V, size_t T, size_t kvw, size_t kvh, size_t hd,
+                const uint8_t* mask_row, bool bm, float* sc, float* pr, float* c) {
+  const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  bool any = false;
+  for (size_t ki = 0; ki < T; ++ki) {
+    if (!mask_row[ki]) {
+      sc[ki] = -kInf;
+      continue;
+    }
+    any = true;
+    const float* k = &Kt[ki * kvw + kvh * hd];
+    float s = 0.0f;
+    for (size_t d = 0; d < hd; ++d) s += q[d] * k[d];
+    const float sv = mrb(s, bm);
+    sc[ki] = mrb(sv * scale, bm);
+  }
+  if (any) {
+    orc_softmax(sc, pr, T);
+    if (bm)
+      for (size_t ki = 0; ki < T; ++ki) pr[ki] = rb(pr[ki]);
+  } else {
+    std::fill(pr, pr + T, 0.0f);
+  }
+  for (size_t d = 0; d < hd; ++d) {
+    float s = 0.0f;
+    for (size_t ki = 0; ki < T; ++ki) s += pr[ki] * V[ki * kvw + kvh * hd + d];
+    c[d] = mrb(s, bm);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -507,41 +540,46 @@ int orc_attention(const float* in, const orc_attention_weights_t* W, size_t T, s
       rotate_head(k, cos_t + t * hd, sin_t + t * hd, hd, bm);
     }
   std::vector<float> sc(T), pr(T);
-  const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
   for (size_t qi = 0; qi < T; ++qi)
-    for (size_t h = 0; h < H; ++h) {
-      const float* q = &Q[qi * qw + h * hd];
-      const size_t kvh = h / group;
-      bool any = false;
-      for (size_t ki = 0; ki < T; ++ki) {
-        if (!mask[qi * T + ki]) {
-          sc[ki] = -kInf;
-          continue;
-        }
-        any = true;
-        const float* k = &Kt[ki * kvw + kvh * hd];
-        float s = 0.0f;
-        for (size_t d = 0; d < hd; ++d) s += q[d] * k[d];
-        const float sv = mrb(s, bm);
-        sc[ki] = mrb(sv * scale, bm);
-      }
-      if (any) {
-        orc_softmax(sc.data(), pr.data(), T);
-        if (bm)
-          for (size_t ki = 0; ki < T; ++ki) pr[ki] = rb(pr[ki]);
-      } else {
-        std::fill(pr.begin(), pr.end(), 0.0f);
-      }
-      float* c = &C[qi * qw + h * hd];
-      for (size_t d = 0; d < hd; ++d) {
-        float s = 0.0f;
-        for (size_t ki = 0; ki < T; ++ki) s += pr[ki] * V[ki * kvw + kvh * hd + d];
-        c[d] = mrb(s, bm);
-      }
-    }
+    for (size_t h = 0; h < H; ++h)
+      attend_row(&Q[qi * qw + h * hd], Kt.data(), V.data(), T, kvw, h / group, hd, mask + qi * T, bm, sc.data(),
+                 pr.data(), &C[qi * qw + h * hd]);
   if (ctx_trace) std::memcpy(ctx_trace, C.data(), sizeof(float) * T * qw);
   project(C.data(), W->o_w, W->o_b, out, T, qw, hidden, bm);
   return 0;
+}
+
+// attention_impl's per-row core for a subset of query rows: Q [nrows, H*hd]
+// (projected and rotated), K and V [T, Hkv*hd] (K rotated) of every row,
+// mask rows [nrows, T]. Each output row is computed exactly as
+// orc_attention computes that row; (row, head) pairs run in parallel.
+int orc_attention_core_rows(const float* Q, const float* Kt, const float* V, const uint8_t* mask, size_t nrows,
+                            size_t T, size_t H, size_t Hkv, size_t hd, float* ctx, int bf16_mode, int threads) {
+  if (T == 0 || hd == 0 || H == 0 || Hkv == 0 || H % Hkv != 0) return -1;
+  if (threads < 1) threads = 1;
+  const bool bm = bf16_mode != 0;
+  const size_t qw = H * hd, kvw = Hkv * hd, group = H / Hkv;
+  const long long pairs = static_cast<long long>(nrows * H);
+#pragma omp parallel num_threads(threads)
+  {
+    std::vector<float> sc(T), pr(T);
+#pragma omp for schedule(dynamic, 4)
+    for (long long e = 0; e < pairs; ++e) {
+      const size_t r = static_cast<size_t>(e) / H, h = static_cast<size_t>(e) % H;
+      attend_row(Q + r * qw + h * hd, Kt, V, T, kvw, h / group, hd, mask + r * T, bm, sc.data(), pr.data(),
+                 ctx + r * qw + h * hd);
+    }
+  }
+  return 0;
+}
+
+// rotate_head (packages/kernels/root.zig:615-633) over every head of n rows
+// [n, heads*hd], row r with its own table row cos_t[r], sin_t[r] ([n, hd]).
+void orc_rotate_rows(float* x, size_t n, size_t heads, size_t hd, const float* cos_t, const float* sin_t,
+                     int bf16_mode) {
+  for (size_t r = 0; r < n; ++r)
+    for (size_t h = 0; h < heads; ++h) rotate_head(x + (r * heads + h) * hd, cos_t + r * hd, sin_t + r * hd, hd,
+                                                   bf16_mode != 0);
 }
 
 // ------------------------------------------------------------------- RVQ

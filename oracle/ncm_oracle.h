@@ -89,6 +89,15 @@ int orc_attention(const float* in, const orc_attention_weights_t* w, size_t T, s
                   size_t kv_heads, size_t head_dim, float eps, const float* cos_t, const float* sin_t,
                   const uint8_t* mask, float* out, int bf16_mode, float* context_trace);
 
+/* attention_impl's core for a subset of query rows (Q projected and rotated
+ * [nrows, H*hd]; K rotated and V [T, Hkv*hd]; mask rows [nrows, T]); context
+ * rows [nrows, H*hd], the same bits as orc_attention's rows. */
+int orc_attention_core_rows(const float* Q, const float* Kt, const float* V, const uint8_t* mask, size_t nrows,
+                            size_t T, size_t H, size_t Hkv, size_t hd, float* ctx, int bf16_mode, int threads);
+/* rotate_head over every head of n rows, each row with its own table row. */
+void orc_rotate_rows(float* x, size_t n, size_t heads, size_t hd, const float* cos_t, const float* sin_t,
+                     int bf16_mode);
+
 /* ---- RVQ (spec restatement) */
 void orc_code_sqnorm(const uint16_t* cb, float* out, size_t K, size_t D);
 /* One level. If codes_in is non-NULL the residual is advanced with those codes

@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
         "orc_apply_post_upsample_conv": ([f32p, f32p, f32p, sz, sz], ctypes.c_int),
         "orc_attention": ([f32p, ctypes.POINTER(AttnWeights), sz, sz, sz, sz, sz, ctypes.c_float, f32p, f32p, u8p,
                            f32p, ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
+        "orc_attention_core_rows": ([f32p, f32p, f32p, u8p, sz, sz, sz, sz, sz, f32p, ctypes.c_int, ctypes.c_int],
+                                    ctypes.c_int),
+        "orc_rotate_rows": ([f32p, sz, sz, sz, f32p, f32p, ctypes.c_int], None),
         "orc_code_sqnorm": ([u16p, f32p, sz, sz], None),
         "orc_rvq_level": ([f32p, u16p, f32p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, sz, sz, sz,
                            ctypes.c_int], None),
@@ -288,6 +291,33 @@ def attention(x, weights: dict, heads, kv_heads, head_dim, eps, cos_t, sin_t, ma
     if rc != 0:
         raise ValueError("attention: bad arguments")
     return out
+
+
+def attention_rows(x, weights: dict, heads, kv_heads, head_dim, cos_t, sin_t, mask, rows, bf16_mode=True,
+                   threads=1):
+    """attention_impl (packages/kernels/root.zig:450-581) for the query rows
+    `rows` only: K and V are projected for every row of x, Q for the chosen
+    rows; each returned row [len(rows), hidden] has the bits orc_attention
+    gives that row (no biases, no QK-norm). cos_t/sin_t [T, head_dim], mask
+    [T, T]."""
+    x = _c(x, np.float32)
+    rows = np.asarray(rows, np.int64)
+    T, hidden = x.shape
+    # project (root.zig:583-609): matmul_bf16 in bf16 mode, else the f32 32-tile matmul
+    proj = (lambda a, w: matmul_bf16(a, w, threads=threads)) if bf16_mode else matmul  # noqa: E731
+    q = proj(x[rows], weights["q_w"])
+    k = proj(x, weights["k_w"])
+    v = proj(x, weights["v_w"])
+    cos_t, sin_t = _c(cos_t, np.float32), _c(sin_t, np.float32)
+    lib().orc_rotate_rows(q, rows.size, heads, head_dim, _c(cos_t[rows], np.float32), _c(sin_t[rows], np.float32),
+                          int(bf16_mode))
+    lib().orc_rotate_rows(k, T, kv_heads, head_dim, cos_t, sin_t, int(bf16_mode))
+    ctx = np.empty((rows.size, heads * head_dim), np.float32)
+    rc = lib().orc_attention_core_rows(q, k, v, _c(np.asarray(mask)[rows], np.uint8), rows.size, T, heads, kv_heads,
+                                       head_dim, ctx, int(bf16_mode), threads)
+    if rc != 0:
+        raise ValueError("attention_rows: bad arguments")
+    return proj(ctx, weights["o_w"])
 
 
 # ------------------------------------------------------------------- RVQ

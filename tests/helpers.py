@@ -44,6 +44,26 @@ def check_codes(gpu: np.ndarray, oracle_best: np.ndarray, gap: np.ndarray, what:
     return {"rows": int(gpu.size), "near_ties": int((~far).sum()), "flips": int(mism.sum())}
 
 
+def check_free_running(gpu: np.ndarray, free_best: np.ndarray, tf_gap: np.ndarray, what: str) -> dict:
+    """Free-running comparison over L levels ([L, n] codes): the oracle encodes
+    the rows on its own (free_best), so a near-tie flip at one level changes
+    the residual and may change every later level. Each row that diverges
+    must do so first at a level whose gap is below NEAR_TIE; until that level
+    both histories are identical, so the teacher-forced oracle's gap there
+    (tf_gap) is the free-running oracle's too."""
+    L, n = gpu.shape
+    differ = gpu != free_best
+    diverged = differ.any(axis=0)
+    first = np.where(diverged, differ.argmax(axis=0), -1)
+    rows = np.nonzero(diverged)[0]
+    gaps_at_first = tf_gap[first[rows], rows]
+    bad = rows[gaps_at_first >= NEAR_TIE]
+    assert bad.size == 0, (f"{what}: row {bad[0]} first diverges at level {first[bad[0]]} where the gap is "
+                           f"{tf_gap[first[bad[0]], bad[0]]} (not a near-tie)")
+    return {"rows": int(n), "diverged_rows": int(rows.size), "codes_differing": int(differ.sum()),
+            "first_divergence_levels": np.bincount(first[rows], minlength=L).tolist()}
+
+
 def check_gemm(y: np.ndarray, ref: np.ndarray, absprod: np.ndarray, what: str) -> float:
     tol = BF16_REL * np.abs(ref) + ACC_ABS * absprod
     err = np.abs(y.astype(np.float64) - ref.astype(np.float64))

@@ -47,7 +47,7 @@ def test_sharded_encode_capi_two_gpus(tmp_path):
         assert (tmp_path / f"rank{r}").read_text() == "ok"
 
 
-def _worker_overlap(rank, nranks, port, n_local, out_dir):
+def _worker_overlap(rank, nranks, port, total, out_dir, transport):
     import datetime
 
     import torch.distributed as dist
@@ -58,14 +58,14 @@ def _worker_overlap(rank, nranks, port, n_local, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=nranks, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        N, D, K, L = n_local * nranks, 256, 1024, 3
+        N, D, K, L = total, 256, 1024, 3
         g = torch.Generator(device=dev).manual_seed(6)
         xs = [torch.randn((N, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
         cbs = torch.randn((L, K, D), generator=g, device=dev).to(torch.bfloat16)
-        enc = sharded.ShardedEncoder(cbs, N, overlap=True)
+        enc = sharded.ShardedEncoder(cbs, N, overlap=True, transport=transport)
         ok = True
         # three calls: both buffer sets, the first one reused by the third call
-        outs = [enc(x[rank * n_local:(rank + 1) * n_local].contiguous()) for x in xs]
+        outs = [enc(x[enc.start:enc.stop].contiguous()) for x in xs]
         enc.wait()
         torch.cuda.synchronize(dev)
         for x, (codes, recon) in zip(xs[1:], outs[1:]):  # the first call's buffers were reused by the third
@@ -74,13 +74,17 @@ def _worker_overlap(rank, nranks, port, n_local, out_dir):
                                                                      ref_recon.view(torch.int16))
         with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
+        enc.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_sharded_encoder_overlapped_gathers_two_gpus(tmp_path):
-    """ShardedEncoder(overlap=True): the all-gathers run on a second stream
-    while the next call encodes; results equal a single-GPU encode."""
+@pytest.mark.parametrize("transport,total", [("nccl", 8192), ("peer", 8192), ("peer", 8092)])
+def test_sharded_encoder_overlapped_gathers_two_gpus(tmp_path, transport, total):
+    """ShardedEncoder(overlap=True): the all-gathers (NCCL kernels, or
+    copy-engine pushes into the peers' IPC-mapped buffers) run on a second
+    stream while the next call encodes; results equal a single-GPU encode,
+    with even shards and with a short last shard."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import socket
@@ -91,7 +95,7 @@ def test_sharded_encoder_overlapped_gathers_two_gpus(tmp_path):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    ctx = mp.start_processes(_worker_overlap, args=(2, port, 4096, str(tmp_path)), nprocs=2, join=False,
+    ctx = mp.start_processes(_worker_overlap, args=(2, port, total, str(tmp_path), transport), nprocs=2, join=False,
                              start_method="spawn")
     deadline = time.time() + 240
     while not ctx.join(timeout=5):

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import check_codes, check_gemm, from_dev_bf16, to_dev_bf16
+from helpers import check_codes, check_free_running, check_gemm, from_dev_bf16, to_dev_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -22,7 +22,12 @@ def _seeded(shape, scale, dev, seed):
     return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
 
 
-def run_tokenizer_case(orc, dev, B, T, Din, D, K, factors, L, sample, seed=7):
+def _threads():
+    import os
+    return max(1, min(64, os.cpu_count() or 1))
+
+
+def run_tokenizer_case(orc, dev, B, T, Din, D, K, factors, L, sample, seed=7, free_running=False):
     from ncmorph_b200 import kernels, vq
     S = len(factors)
     x = _seeded((B, T, Din), 1.0, dev, seed)
@@ -53,6 +58,7 @@ def run_tokenizer_case(orc, dev, B, T, Din, D, K, factors, L, sample, seed=7):
     r = orc.bf16_widen(h_bits).astype(np.float32).copy()
     acc = np.zeros_like(r)
     stats = []
+    free = []
     for s, f in enumerate(factors):
         P = N // f
         u = orc.pool_avg(r.reshape(B, T, D), f).reshape(P, D)
@@ -61,9 +67,17 @@ def run_tokenizer_case(orc, dev, B, T, Din, D, K, factors, L, sample, seed=7):
         assert cs.min() >= 0 and cs.max() < K
         pr = np.sort(rng.choice(P, size=min(sample, P), replace=False))
         us = np.ascontiguousarray(u[pr])
+        gaps = np.empty((L, pr.size), np.float32)
         for l in range(L):
-            best, gap = orc.rvq_level(us, cbs_np[s, l], sq[s, l], codes_in=cs[l, pr])
-            stats.append(check_codes(cs[l, pr], best, gap, f"scale {s} level {l}"))
+            best, gaps[l] = orc.rvq_level(us, cbs_np[s, l], sq[s, l], codes_in=cs[l, pr], threads=_threads())
+            stats.append(check_codes(cs[l, pr], best, gaps[l], f"scale {s} level {l}"))
+        if free_running:
+            # the scale's L levels encoded by the oracle on its own from the same pooled rows
+            uf = np.ascontiguousarray(u[pr])
+            fb = np.empty((L, pr.size), np.int32)
+            for l in range(L):
+                fb[l], _ = orc.rvq_level(uf, cbs_np[s, l], sq[s, l], threads=_threads())
+            free.append(check_free_running(cs[:, pr], fb, gaps, f"scale {s}"))
         orc.scale_update(cs, cbs_np[s], r, acc, B, T, f)
     recon_bits = from_dev_bf16(recon).reshape(N, D)
     assert np.array_equal(recon_bits, orc.bf16_bits(acc))
@@ -74,7 +88,7 @@ def run_tokenizer_case(orc, dev, B, T, Din, D, K, factors, L, sample, seed=7):
     ref_y = orc.matmul_bf16(rf, w_out_np, threads=8)
     y_np = orc.bf16_widen(from_dev_bf16(y).reshape(N, Din)[rows])
     check_gemm(y_np, ref_y, np.abs(rf) @ np.abs(w_out_np).T, "output projection")
-    return stats
+    return (stats, free) if free_running else stats
 
 
 def test_tokenizer_small_all_rows(orc, cuda_dev):
@@ -84,10 +98,15 @@ def test_tokenizer_small_all_rows(orc, cuda_dev):
 
 
 def test_tokenizer_config2_full_size_sampled(orc, cuda_dev):
-    """BASELINE config 2 shapes: B=8, T=2048, 2048->1024, 5 scales x 8 levels, K=4096."""
-    stats = run_tokenizer_case(orc, cuda_dev, B=8, T=2048, Din=2048, D=1024, K=4096, factors=[16, 8, 4, 2, 1],
-                               L=8, sample=48)
-    print("config2 flips", sum(s["flips"] for s in stats), "near", sum(s["near_ties"] for s in stats))
+    """BASELINE config 2 shapes: B=8, T=2048, 2048->1024, 5 scales x 8 levels,
+    K=4096; 256 pooled rows per (scale, level) teacher-forced, and the same
+    rows encoded free-running by the oracle through each scale's 8 levels."""
+    stats, free = run_tokenizer_case(orc, cuda_dev, B=8, T=2048, Din=2048, D=1024, K=4096, factors=[16, 8, 4, 2, 1],
+                                     L=8, sample=256, free_running=True)
+    print("config2 teacher-forced: flips", sum(s["flips"] for s in stats), "near-ties",
+          sum(s["near_ties"] for s in stats), "of", sum(s["rows"] for s in stats), "codes")
+    print("config2 free-running: rows diverged per scale", [f["diverged_rows"] for f in free], "of",
+          [f["rows"] for f in free], "codes differing", [f["codes_differing"] for f in free])
 
 
 def test_config5_encode_sampled(orc, cuda_dev):
@@ -125,16 +144,21 @@ def test_config5_encode_sampled(orc, cuda_dev):
         r = r - e[codes[l].long()]
         del a, e, d_best
     del r, rec_f32
-    # oracle, teacher-forced, on a row sample
+    # oracle on a 2048-row sample: teacher-forced (every level's codes and the
+    # final residual), then free-running (the oracle's own cascade of codes)
     rng = np.random.default_rng(5)
-    rows = np.sort(rng.choice(N, size=24, replace=False))
+    rows = np.sort(rng.choice(N, size=2048, replace=False))
     xs = from_dev_bf16(x[torch.from_numpy(rows).to(cuda_dev)])
     cbs_np = from_dev_bf16(cbs)
     cs = codes.cpu().numpy()[:, rows]
-    best, gaps, res_o, _ = orc.rvq_encode(xs, cbs_np, codes_in=cs, threads=8)
-    for l in range(L):
-        check_codes(cs[l], best[l], gaps[l], f"config5 level {l}")
+    best, gaps, res_o, _ = orc.rvq_encode(xs, cbs_np, codes_in=cs, threads=_threads())
+    st = [check_codes(cs[l], best[l], gaps[l], f"config5 level {l}") for l in range(L)]
     assert np.array_equal(resid[torch.from_numpy(rows).to(cuda_dev)].cpu().numpy(), res_o)
+    free_best, _, _, _ = orc.rvq_encode(xs, cbs_np, threads=_threads())
+    fr = check_free_running(cs, free_best, gaps, "config5")
+    print(f"config5 teacher-forced: flips {sum(s['flips'] for s in st)}, near-ties "
+          f"{sum(s['near_ties'] for s in st)} of {L * rows.size} codes; free-running: {fr['diverged_rows']} of "
+          f"{rows.size} rows diverge ({fr['codes_differing']} codes), first at levels {fr['first_divergence_levels']}")
 
 
 def _phi_weights(S, D, dev, seed):

@@ -211,6 +211,27 @@ def test_tiny_decoder_attention_context(orc):
     assert np.allclose(out[1], (x[0] + x[1]) / 2, atol=1e-6)
 
 
+@pytest.mark.parametrize("bf16_mode", [True, False])
+def test_attention_rows_equal_full_attention_rows(orc, bf16_mode):
+    """The row-subset attention (K/V of every row, Q of the chosen rows) gives
+    each chosen row the same bits as orc_attention, which restates
+    attention_impl for all rows; block-causal mask, GQA 4:2."""
+    rng = np.random.default_rng(21)
+    T, hidden, H, Hkv, hd = 96, 128, 4, 2, 64
+    x = orc.round_bf16(rng.standard_normal((T, hidden)).astype(np.float32))
+    w = {n: orc.round_bf16((rng.standard_normal((o, i)) * 0.05).astype(np.float32))
+         for n, o, i in (("q_w", H * hd, hidden), ("k_w", Hkv * hd, hidden), ("v_w", Hkv * hd, hidden),
+                         ("o_w", hidden, H * hd))}
+    levels = [16, 16, 32, 32]
+    pos = np.asarray(orc.fill_level_positions(0, levels), np.int64)
+    _, c, s = orc.rope_default(hd, 500000.0, int(pos.max()) + 1)
+    mask = orc.block_causal_mask(0, levels).astype(np.uint8)
+    full = orc.attention(x, w, H, Hkv, hd, 1e-5, c[pos], s[pos], mask, bf16_mode=bf16_mode)
+    rows = [0, 5, 17, 33, 50, 64, 95]
+    got = orc.attention_rows(x, w, H, Hkv, hd, c[pos], s[pos], mask, rows, bf16_mode=bf16_mode, threads=3)
+    assert np.array_equal(got.view(np.uint32), full[rows].view(np.uint32))
+
+
 def _golden_npz(name):
     return np.load(GOLDEN / name)
 

@@ -130,3 +130,30 @@ def test_scale_update_matches_numpy(orc):
     up = np.repeat(q, f, axis=0)
     assert np.array_equal(r, (r0 - up).astype(np.float32))
     assert np.array_equal(acc, up)
+
+
+def test_free_running_check_accepts_near_tie_divergence_and_rejects_others(orc):
+    """The free-running parity rule on planted data: a row may diverge from
+    the oracle's own cascade only first at a near-tie level; a divergence
+    first seen at a clear gap is a failure."""
+    import pytest
+    from helpers import NEAR_TIE, check_free_running
+    rng = np.random.default_rng(9)
+    N, D, K, L = 64, 16, 32, 4
+    x = orc.bf16_bits(rng.standard_normal((N, D)).astype(np.float32))
+    cbs = np.stack([bf16_codebook(orc, rng, K, D, 0.5 ** l) for l in range(L)])
+    free, gaps, _, _ = orc.rvq_encode(x, cbs)
+    st = check_free_running(free.copy(), free, gaps, "identical")
+    assert st["diverged_rows"] == 0
+    # plant a flip at level 1 of one row and pretend that level was a near-tie
+    planted = free.copy()
+    planted[1, 3] = (planted[1, 3] + 1) % K
+    planted[2:, 3] = 0
+    g = gaps.copy()
+    g[1, 3] = NEAR_TIE / 2
+    st = check_free_running(planted, free, g, "near-tie flip")
+    assert st["diverged_rows"] == 1 and st["first_divergence_levels"] == [0, 1, 0, 0]
+    # the same flip where the oracle's gap was clear must fail
+    g[1, 3] = 10 * NEAR_TIE
+    with pytest.raises(AssertionError):
+        check_free_running(planted, free, g, "clear-gap flip")
