@@ -79,7 +79,7 @@ def test_noalloc_first_call_holds_at_most_its_array(cuda_dev):
 
 def test_noalloc_matches_rvq_level_on_two_calls(cuda_dev):
     # First call: config-1 level shape with caller-supplied norms (code-split
-    # partials and merge counters in the scratch). Second call: smaller and
+    # partials in the scratch). Second call: smaller and
     # ragged, norms computed in the scratch; the first call's leftovers must
     # not leak into it.
     _compare(cuda_dev, 4096, 256, 1024, 1, True)
