@@ -107,3 +107,28 @@ def test_bias_and_ragged_tiles(orc, cuda_dev, M, K, N):
     xf, wf, bf = orc.bf16_widen(x), orc.bf16_widen(w), orc.bf16_widen(b)
     ref = orc.matmul_bf16(xf, wf, bf)
     check_gemm(orc.bf16_widen(from_dev_bf16(y)), ref, np.abs(xf) @ np.abs(wf).T + np.abs(bf), "bias")
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 8192, 2048),   # CTA pairs, 128 tiles: a second wave 73 % full
+                                   (8192, 2048, 512),    # one-CTA 128-wide tiles
+                                   (512, 2048, 512),     # 64-wide tiles, fewer tiles than SMs
+                                   (4096, 2048, 3072)])  # the decoder's QKV width
+def test_every_element_of_decoder_and_sweep_shapes(cuda_dev, M, K, N):
+    """Every output element, bias included, against an f32 product of the
+    same bf16 operands within the GEMM bar (the sweep test above checks six
+    rows per shape against the oracle's bits)."""
+    from ncmorph_b200 import kernels
+    g = torch.Generator(device=cuda_dev).manual_seed(M + K + N)
+    x = torch.randn((M, K), generator=g, device=cuda_dev).to(torch.bfloat16)
+    w = (torch.randn((N, K), generator=g, device=cuda_dev) * 0.02).to(torch.bfloat16)
+    b = (torch.randn((N,), generator=g, device=cuda_dev) * 0.1).to(torch.bfloat16)
+    y = kernels.linear_bf16(x, w, b).float()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = x.float() @ w.float().t() + b.float()
+        scale = x.float().abs() @ w.float().abs().t() + b.float().abs()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    bad = (y - ref).abs() > 2e-2 * ref.abs() + 1e-5 * scale + 1e-6
+    assert int(bad.sum()) == 0, f"{int(bad.sum())} elements outside the bar, first at {bad.nonzero()[0].tolist()}"
