@@ -185,6 +185,20 @@ static int rvq_encode_core(ncm_ctx* ctx, const uint16_t* x, const uint16_t* code
                            int32_t* codes, uint16_t* recon, float* resid, bool keep_resid, uint16_t* shadow,
                            RvqPartial* part, const RvqPlan& plan, int64_t N, int64_t D, int64_t K,
                            cudaStream_t st) {
+  RvqLevelsPlan lp;
+  if (rvq_levels_plan(ctx->num_sms, N, D, K, L, &lp)) {
+    // few row blocks: every level in one launch (clusters share the code range)
+    {
+      Launch _launch(ctx, KID_RVQ_ARGMIN, st);
+      NCM_CUDA_TRY(launch_rvq_levels(lp, x, codebooks, sqnorms, L, codes, resid, keep_resid, shadow, recon,
+                                     ctx->d_err, N, D, K, st));
+    }
+    if (recon != nullptr && !lp.reg) {
+      Launch _launch(ctx, KID_DECODE, st);
+      NCM_CUDA_TRY(launch_rvq_decode(codes, codebooks, L, recon, nullptr, N, D, K, ctx->d_err, st));
+    }
+    return NCM_OK;
+  }
   for (int l = 0; l < L; ++l) {
     const bool last = (l == L - 1);
     const bool update = !last || keep_resid;

@@ -249,6 +249,24 @@ cudaError_t launch_rvq_apply(const RvqPlan& plan, const RvqPartial* part, int32_
                              int64_t D, int64_t K, bool update, cudaStream_t stream, const RvqTop2* top2 = nullptr);
 
 cudaError_t launch_code_sqnorm(const uint16_t* codebook, float* sqnorm, int64_t K, int64_t D, cudaStream_t stream);
+
+// Every level of a small encode in one launch (rvq_levels.cu): one cluster of
+// `cluster` CTAs per 128-row block, CTA r holding code tiles [r * tpc, ...)
+// and residual columns [r * slice, ...). Applies when the row blocks cannot
+// fill half the SMs (one level per launch would split the code range).
+struct RvqLevelsPlan {
+  int row_blocks, cluster, tpc, code_tiles, slice;
+  int reg;  // the residual slice stays in registers and the kernel writes the reconstruction
+};
+bool rvq_levels_plan(int num_sms, int64_t N, int64_t D, int64_t K, int L, RvqLevelsPlan* out);
+// codes [L, N], resid (f32; holds the final residual with keep_resid),
+// shadow (bf16 scratch [N, D]); x [N, D] bf16 rows. With plan.reg the
+// kernel also writes recon (bf16 [N, D], nullable); otherwise the caller
+// decodes.
+cudaError_t launch_rvq_levels(const RvqLevelsPlan& plan, const uint16_t* x, const uint16_t* codebooks,
+                              const float* sqnorms, int L, int32_t* codes, float* resid, bool keep_resid,
+                              uint16_t* shadow, uint16_t* recon, int* err, int64_t N, int64_t D, int64_t K,
+                              cudaStream_t stream);
 cudaError_t launch_rvq_decode(const int32_t* codes, const uint16_t* codebooks, int L, uint16_t* recon_bf16,
                               float* recon_f32, int64_t N, int64_t D, int64_t K, int* err, cudaStream_t stream);
 cudaError_t launch_pool_avg(const float* x, float* y, uint16_t* y_bf16, int64_t B, int64_t T, int64_t D, int f,

@@ -305,6 +305,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
 // All threads of both CTAs: release this CTA's prior writes, wait for the peer.
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -313,6 +319,46 @@ __device__ __forceinline__ void cluster_sync_all() {
 // Arrive on an mbarrier given by its shared::cluster address (possibly the peer's).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Waits (bounded, as mbar_wait) for a phase of a local mbarrier whose
+// arrivals come from other CTAs of the cluster, with cluster-scope acquire:
+// their writes released before arriving are visible afterwards.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if ((it & 31u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) accesses that synchronise with it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// 8-byte load from the shared memory of a CTA of the cluster (cluster address).
+__device__ __forceinline__ int2 ld_shared_cluster_v2(uint32_t cluster_addr) {
+  int2 v;
+  asm volatile("ld.shared::cluster.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {

@@ -235,3 +235,39 @@ def test_rvq_level_top2_duplicate_codeword_gap_is_zero(cuda_dev):
     codes, gap = vq.rvq_level_top2(torch.from_numpy(r).to(cuda_dev), to_dev_bf16(cb, cuda_dev))
     assert codes.tolist()[:2] == [7, 7]
     assert gap.tolist()[:2] == [0.0, 0.0] and gap.tolist()[2] > 0
+
+
+@pytest.mark.parametrize("N,D,K,L,keep", [
+    (4096, 256, 1024, 4, True),      # 32 row blocks x clusters of 4 CTAs
+    (4096, 256, 1024, 4, False),
+    (1000, 136, 700, 3, True),       # ragged rows, columns (slices of 48 and 40) and codes
+    (2048, 1024, 2048, 8, False),    # D = 1024 (slices of 128 columns: residual in global memory)
+    (640, 64, 300, 6, True),         # 5 row blocks, slice 32 over two CTAs
+    (4096, 256, 256, 5, True),       # one code tile: clusters of one CTA
+])
+def test_small_encode_in_one_launch_matches_levels(orc, cuda_dev, N, D, K, L, keep):
+    """Few row blocks: every level runs in one launch, one cluster of CTAs per
+    128-row block sharing the code range through distributed shared memory.
+    Codes and residual must equal ncm_rvq_level applied level by level (the
+    split plan with rvq_apply_kernel) bit for bit, and the oracle outside
+    near-ties; the reconstruction equals the oracle's."""
+    from ncmorph_b200 import vq
+    rng = np.random.default_rng(N * 3 + D + K + L)
+    x = gen_bf16(rng, (N, D))
+    cbs = _cbs(rng, L, K, D, 0.6)
+    xd, cbs_d = to_dev_bf16(x, cuda_dev), to_dev_bf16(cbs, cuda_dev)
+    codes_d, recon_d, resid_d = vq.rvq_encode(xd, cbs_d, want_residual=keep)
+    # level by level through the single-level entry point
+    r = xd.float().clone()
+    ref_codes = torch.stack([vq.rvq_level(r, cbs_d[l]) for l in range(L)])
+    torch.cuda.synchronize()
+    assert torch.equal(codes_d, ref_codes)
+    if keep:
+        assert torch.equal(resid_d, r)
+    codes = codes_d.cpu().numpy()
+    best, gaps, resid, recon = orc.rvq_encode(x, cbs, codes_in=codes)
+    for l in range(L):
+        check_codes(codes[l], best[l], gaps[l], f"one-launch level {l}")
+    if keep:
+        assert np.array_equal(resid_d.cpu().numpy(), resid)
+    assert np.array_equal(from_dev_bf16(recon_d), orc.bf16_bits(recon))
