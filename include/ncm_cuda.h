@@ -409,6 +409,18 @@ NCM_API int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride
                                const float* sin_t, uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads,
                                const ncm_mask_t* mask, ncm_stream_t stream);
 
+/* ncm_attention_bf16 for layers with QK-norm (attention_impl with
+ * query_norm_weight and key_norm_weight, packages/kernels/root.zig:471,
+ * :500-530, bf16 mode): every Q head of qkv gets rms_norm_bf16 (root.zig:
+ * 243-252) with q_norm [64] and every K head with k_norm [64] (bf16 device,
+ * both required), eps = the config's rms_norm_epsilon, then RoPE if cos/sin
+ * are given, IN PLACE, before the attention. Bit-identical to the reference's
+ * norm and rotation (its sum-of-squares order included). */
+NCM_API int ncm_attention_qk_norm_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t,
+                                       const float* sin_t, const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                                       uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads,
+                                       const ncm_mask_t* mask, ncm_stream_t stream);
+
 /* Fused QKV projection of one decoder layer (src/decoder.zig:171-190 and
  * rotate_head, packages/kernels/root.zig:615-633): qkv [T, (heads + 2 kv_heads) * 64]
  * = bf16(x . w^T + bias) with RoPE (bf16 mode, tables cos_t/sin_t [T, 64] f32
@@ -455,6 +467,11 @@ typedef struct ncm_decoder_layer_weights {
   const uint16_t* ln_2;      /* [hidden] */
   const uint16_t* gate_up;   /* [2*F, hidden]: gate_weight rows, then up_weight rows */
   const uint16_t* down;      /* [hidden, F] */
+  /* QK-norm (ncm_model.zig:42-43, root.zig:500-530): per-head RMSNorm scales
+   * [64] for the Q and K heads, applied before RoPE with rms_norm_epsilon;
+   * both or NULL (Qwen3-style checkpoints carry them) */
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
 } ncm_decoder_layer_weights_t;
 
 typedef struct ncm_decoder_weights {

@@ -85,7 +85,8 @@ class DecoderConfig(ctypes.Structure):
 class DecoderLayerWeights(ctypes.Structure):
     """Mirror of ncm_decoder_layer_weights_t (device pointers)."""
 
-    _fields_ = [(n, c_vp) for n in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down")]
+    _fields_ = [(n, c_vp) for n in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down", "q_norm",
+                                    "k_norm")]
 
 
 class DecoderWeights(ctypes.Structure):
@@ -129,6 +130,8 @@ SIGNATURES: dict[str, list] = {
     "ncm_rope_tables_llama3_host": [c_i32, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_i64,
                                     c_vp, c_i64, c_vp, c_vp],
     "ncm_attention_bf16": [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, ctypes.POINTER(Mask), c_vp],
+    "ncm_attention_qk_norm_bf16": [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_vp, c_i64, c_i32, c_i32,
+                                   ctypes.POINTER(Mask), c_vp],
     "ncm_ncm_forward": [c_vp, ctypes.POINTER(DecoderConfig), ctypes.POINTER(DecoderWeights), c_vp, c_vp, c_vp],
     "ncm_rvq_level_noalloc": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp],
     "ncm_rvq_level_noalloc_status": [c_vp, ctypes.POINTER(c_i32)],

@@ -124,6 +124,101 @@ __global__ void __launch_bounds__(256) rope_bf16_kernel(uint16_t* __restrict__ q
   v[i + HALF] = f32_to_bf16(left2 + right2);
 }
 
+// ------------------------------------------------------ QK-norm + RoPE
+// attention_impl with query/key norm weights (packages/kernels/root.zig:
+// 500-530, bf16 mode): each Q head gets rms_norm_bf16 with q_norm, each K head
+// with k_norm (root.zig:243-252), then rotate_head (:615-633), in place on the
+// fused QKV rows. Eight threads per (token, head); thread j holds elements
+// 8j..8j+7 of the 64-wide head.
+//
+// The sum of squares keeps the reference's order for 64 elements
+// (pinned_torch_sum_squares_f32, root.zig:152-224: two 4x8 accumulator rows,
+// no full level step): acc[r][l] = x[8r+l]^2 + x[8(r+4)+l]^2 for r < 4,
+// vs[l] = ((acc[0][l] + acc[1][l]) + acc[2][l]) + acc[3][l], then
+// sum = vs[0] + vs[1] + ... + vs[7]; every product and sum rounded on its own.
+// The shuffles below reproduce exactly that, so the norm is bit-identical.
+__global__ void __launch_bounds__(256) qk_norm_rope_bf16_kernel(uint16_t* __restrict__ qkv, long long stride, int T,
+                                                                int heads, int kv_heads,
+                                                                const uint16_t* __restrict__ q_norm,
+                                                                const uint16_t* __restrict__ k_norm, float eps,
+                                                                const float* __restrict__ cos_t,
+                                                                const float* __restrict__ sin_t) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int heads_qk = heads + kv_heads;
+  const long long group = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+  const int j = threadIdx.x & 7;
+  // whole 8-lane groups drop out together, so the group's shuffles stay convergent
+  if (group >= static_cast<long long>(T) * heads_qk) return;
+  const unsigned gmask = 0xffu << (threadIdx.x & 24);
+  const int head = static_cast<int>(group % heads_qk);
+  const int t = static_cast<int>(group / heads_qk);
+  uint16_t* hp = qkv + t * stride + head * 64 + j * 8;
+  const uint4 raw = *reinterpret_cast<const uint4*>(hp);
+  const uint32_t p[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[2 * e] = bf16lo(p[e]), v[2 * e + 1] = bf16hi(p[e]);
+  const uint16_t* scale = head < heads ? q_norm : k_norm;
+  if (scale != nullptr) {
+    float acc[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      const float sq = __fmul_rn(v[l], v[l]);
+      acc[l] = __fadd_rn(sq, __shfl_down_sync(gmask, sq, 4, 8));    // rows r and r+4 (valid in j < 4)
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      float vs = __shfl_sync(gmask, acc[l], 0, 8);
+      vs = __fadd_rn(vs, __shfl_sync(gmask, acc[l], 1, 8));
+      vs = __fadd_rn(vs, __shfl_sync(gmask, acc[l], 2, 8));
+      vs = __fadd_rn(vs, __shfl_sync(gmask, acc[l], 3, 8));
+      sum = __fadd_rn(sum, vs);
+    }
+    const float inv = 1.0f / sqrtf(__fdiv_rn(sum, 64.f) + eps);
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(scale + j * 8));
+    const uint32_t q[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t n = cvt_bf16x2(__fmul_rn(v[2 * e], inv), __fmul_rn(v[2 * e + 1], inv));
+      const uint32_t m = cvt_bf16x2(__fmul_rn(bf16lo(n), bf16lo(q[e])), __fmul_rn(bf16hi(n), bf16hi(q[e])));
+      v[2 * e] = bf16lo(m), v[2 * e + 1] = bf16hi(m);
+    }
+  }
+  uint32_t o4[4];
+  if (cos_t != nullptr) {
+    // pair (i, i+32): threads j and j^4 exchange their eight values
+    const bool first_half = j < 4;
+    const int col = j * 8;
+    const float* c = cos_t + static_cast<size_t>(t) * 64;
+    const float* s = sin_t + static_cast<size_t>(t) * 64;
+    auto rb = [](float f) { return bf16_to_f32(f32_to_bf16(f)); };
+    float r[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      const float other = __shfl_xor_sync(gmask, v[l], 4, 8);
+      if (first_half) {
+        // element i = col + l: left + right with first = own, second = partner
+        const float left = rb(__fmul_rn(v[l], rb(c[col + l])));
+        const float right = rb(__fmul_rn(-other, rb(s[col + l])));
+        r[l] = __fadd_rn(left, right);
+      } else {
+        // element i + 32 = col + l: first = partner, second = own
+        const float left2 = rb(__fmul_rn(v[l], rb(c[col + l])));
+        const float right2 = rb(__fmul_rn(other, rb(s[col + l])));
+        r[l] = __fadd_rn(left2, right2);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o4[e] = cvt_bf16x2(r[2 * e], r[2 * e + 1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o4[e] = cvt_bf16x2(v[2 * e], v[2 * e + 1]);
+  }
+  *reinterpret_cast<uint4*>(hp) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+}
+
 // --------------------------------------------------------- V transpose
 // vt[(kvh*64 + d) * T + t] = qkv[t * stride + voff + kvh*64 + d], 64x64 tiles.
 __global__ void __launch_bounds__(256) v_transpose_kernel(const uint16_t* __restrict__ qkv, long long stride,
@@ -238,6 +333,14 @@ cudaError_t launch_rope_bf16(uint16_t* qkv, long long stride, int T, int heads_q
   rope_bf16_kernel<<<blocks_for(static_cast<long long>(T) * heads_qk * 32, 256), 256, 0, st>>>(qkv, stride, T,
                                                                                              heads_qk, c, s);
   return cudaGetLastError();
+}
+
+cudaError_t launch_qk_norm_rope_bf16(uint16_t* qkv, long long stride, int T, int heads, int kv_heads,
+                                     const uint16_t* q_norm, const uint16_t* k_norm, float eps, const float* c,
+                                     const float* s, cudaStream_t st) {
+  const long long threads = static_cast<long long>(T) * (heads + kv_heads) * 8;
+  return launch_pdl(qk_norm_rope_bf16_kernel, dim3(blocks_for(threads, 256)), dim3(256), 0, st, 1, qkv, stride, T,
+                    heads, kv_heads, q_norm, k_norm, eps, c, s);
 }
 
 cudaError_t launch_v_transpose(const uint16_t* qkv, long long stride, long long voff, int T, int vwidth, uint16_t* vt,

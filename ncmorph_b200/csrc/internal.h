@@ -166,6 +166,11 @@ cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* w, const uin
                                  int width, float eps, cudaStream_t st);
 cudaError_t launch_rope_bf16(uint16_t* qkv, long long stride, int T, int heads_qk, const float* c, const float* s,
                              cudaStream_t st);
+// per-head RMSNorm (q_norm on the Q heads, k_norm on the K heads; either
+// null skips it) then RoPE (skipped when c is null), in place, bf16 mode
+cudaError_t launch_qk_norm_rope_bf16(uint16_t* qkv, long long stride, int T, int heads, int kv_heads,
+                                     const uint16_t* q_norm, const uint16_t* k_norm, float eps, const float* c,
+                                     const float* s, cudaStream_t st);
 cudaError_t launch_v_transpose(const uint16_t* qkv, long long stride, long long voff, int T, int vwidth, uint16_t* vt,
                                cudaStream_t st);
 cudaError_t launch_silu_mul_bf16(const uint16_t* gu, uint16_t* out, int T, int F, cudaStream_t st);

@@ -93,9 +93,12 @@ int ncm_rope_tables_llama3_host(int32_t head_dim, float theta, float factor, flo
   return NCM_OK;
 }
 
-int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t, const float* sin_t,
-                       uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
-                       ncm_stream_t stream) {
+// ncm_attention_bf16 and its QK-norm variant: RoPE (or QK-norm then RoPE) and
+// the V transpose, then the fused attention kernel
+static int attention_entry(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t,
+                           const float* sin_t, const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                           uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
+                           ncm_stream_t stream) {
   int rc = ctx_ok(ctx);
   if (rc) return rc;
   if (T <= 0 || T > INT32_MAX || T % 8 != 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || !qkv || !out)
@@ -115,7 +118,10 @@ int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const 
   uint16_t* vt = reinterpret_cast<uint16_t*>(ws + o_vt);
   {
     Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
-    if (cos_t != nullptr)
+    if (q_norm != nullptr)
+      NCM_CUDA_TRY(launch_qk_norm_rope_bf16(qkv, qkv_stride, static_cast<int>(T), heads, kv_heads, q_norm, k_norm, eps,
+                                            cos_t, sin_t, st));
+    else if (cos_t != nullptr)
       NCM_CUDA_TRY(launch_rope_bf16(qkv, qkv_stride, static_cast<int>(T), heads + kv_heads, cos_t, sin_t, st));
     NCM_CUDA_TRY(launch_v_transpose(qkv, qkv_stride, static_cast<int64_t>(heads + kv_heads) * 64,
                                     static_cast<int>(T), static_cast<int>(vw), vt, st));
@@ -123,6 +129,26 @@ int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const 
   Launch _l(ctx, KID_ATTENTION, st);
   return attention_bf16(ctx, qkv, qkv_stride, vt, out, static_cast<int>(T), heads, kv_heads, mask->mode,
                         mask->prefix_length, mask->prefix_pad_mask, mask->level_lengths, mask->num_levels, st);
+}
+
+int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t, const float* sin_t,
+                       uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
+                       ncm_stream_t stream) {
+  return attention_entry(ctx, qkv, qkv_stride, cos_t, sin_t, nullptr, nullptr, 0.f, out, T, heads, kv_heads, mask,
+                         stream);
+}
+
+int ncm_attention_qk_norm_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t,
+                               const float* sin_t, const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                               uint16_t* out, int64_t T, int32_t heads, int32_t kv_heads, const ncm_mask_t* mask,
+                               ncm_stream_t stream) {
+  if (int rc = ctx_ok(ctx)) return rc;
+  if (q_norm == nullptr || k_norm == nullptr)
+    return ncm_fail(NCM_EINVAL, "attention: give both q_norm and k_norm (attention_impl takes both or neither)");
+  if (!a16(q_norm) || !a16(k_norm)) return ncm_fail(NCM_EINVAL, "attention: norm weights must be 16-byte aligned");
+  if (!(eps >= 0.f)) return ncm_fail(NCM_EINVAL, "attention: eps must be a non-negative number");
+  return attention_entry(ctx, qkv, qkv_stride, cos_t, sin_t, q_norm, k_norm, eps, out, T, heads, kv_heads, mask,
+                         stream);
 }
 
 int ncm_qkv_projection_rope(ncm_ctx_t* ctx, const uint16_t* x, const uint16_t* w, const uint16_t* bias,
@@ -181,6 +207,10 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
     const auto& L = W->layers[l];
     if (!L.ln_1 || !L.qkv || !L.o || !L.ln_2 || !L.gate_up || !L.down)
       return ncm_fail(NCM_EINVAL, "ncm_forward: layer %d is missing a weight", l);
+    if ((L.q_norm == nullptr) != (L.k_norm == nullptr))
+      return ncm_fail(NCM_EINVAL, "ncm_forward: layer %d needs both q_norm and k_norm or neither", l);
+    if ((L.q_norm && !a16(L.q_norm)) || (L.k_norm && !a16(L.k_norm)))
+      return ncm_fail(NCM_EINVAL, "ncm_forward: layer %d norm weights must be 16-byte aligned", l);
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t QKV = static_cast<int64_t>(H + 2 * Hkv) * 64;
@@ -321,7 +351,14 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
       Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
       NCM_CUDA_TRY(launch_rms_norm_bf16(h, L.ln_1, nullptr, nrm, Ti, static_cast<int>(Hd), eps, st));
     }
-    if (T > 64) {
+    if (L.q_norm != nullptr) {
+      // QK-norm sits between the projection and RoPE (ncm_model.zig:271-272,
+      // root.zig:500-530), so the RoPE epilogue does not apply
+      if ((rc = linear_bf16(ctx, nrm, L.qkv, L.qkv_bias, qkv, nullptr, T, Hd, QKV, st))) return rc;
+      Launch _l(ctx, KID_DECODER_ELEMENTWISE, st);
+      NCM_CUDA_TRY(launch_qk_norm_rope_bf16(qkv, QKV, Ti, H, Hkv, L.q_norm, L.k_norm, eps, cosd, sind, st));
+      NCM_CUDA_TRY(launch_v_transpose(qkv, QKV, static_cast<int64_t>(H + Hkv) * 64, Ti, Hkv * 64, vt, st));
+    } else if (T > 64) {
       // RoPE and the V transpose in the projection's epilogue
       if ((rc = linear_qkv_rope(ctx, nrm, L.qkv, L.qkv_bias, qkv, vt, ctx->rope_cos_bf, ctx->rope_sin_bf, T, Hd, QKV,
                                 static_cast<int64_t>(H + Hkv) * 64, st)))

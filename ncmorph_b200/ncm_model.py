@@ -85,14 +85,21 @@ def embedding_gather(table: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
 
 
 def attention_bf16(qkv: torch.Tensor, heads: int, kv_heads: int, mask: _lib.Mask,
-                   cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
+                   cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                   q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None,
+                   eps: float = 1e-6) -> torch.Tensor:
     """Context [T, heads*64] from fused QKV rows [T, (heads + 2*kv_heads)*64];
-    RoPE (if cos/sin given) is applied to qkv in place."""
+    QK-norm (if q_norm/k_norm [64] bf16 are given, with eps) and then RoPE (if
+    cos/sin given) are applied to qkv in place."""
     T, stride = qkv.shape
     need(qkv, bf16, "qkv")
     out = torch.empty((T, heads * 64), dtype=bf16, device=qkv.device)
-    _lib.call("ncm_attention_bf16", context(qkv.device), ptr(qkv), stride, ptr(cos), ptr(sin), ptr(out), T, heads,
-              kv_heads, ctypes.byref(mask), stream_of(qkv))
+    if q_norm is None and k_norm is None:
+        _lib.call("ncm_attention_bf16", context(qkv.device), ptr(qkv), stride, ptr(cos), ptr(sin), ptr(out), T, heads,
+                  kv_heads, ctypes.byref(mask), stream_of(qkv))
+    else:
+        _lib.call("ncm_attention_qk_norm_bf16", context(qkv.device), ptr(qkv), stride, ptr(cos), ptr(sin),
+                  ptr(q_norm), ptr(k_norm), eps, ptr(out), T, heads, kv_heads, ctypes.byref(mask), stream_of(qkv))
     return out
 
 
@@ -106,6 +113,9 @@ class LayerWeights:
     down: torch.Tensor
     qkv_bias: torch.Tensor | None = None
     o_bias: torch.Tensor | None = None
+    # QK-norm scales [64] bf16 (ncm_model.zig:42-43): both or None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
 
 
 @dataclass
@@ -166,7 +176,7 @@ def forward(cfg: Config, w: Weights, inputs: torch.Tensor, out: torch.Tensor | N
          c.rope_original_max_position_embeddings) = cfg.rope_llama3
     layers = (_lib.DecoderLayerWeights * len(w.layers))()
     for i, L in enumerate(w.layers):
-        for name in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down"):
+        for name in ("ln_1", "qkv", "qkv_bias", "o", "o_bias", "ln_2", "gate_up", "down", "q_norm", "k_norm"):
             setattr(layers[i], name, _vp(getattr(L, name)))
     W = _lib.DecoderWeights()
     W.input_projection = _vp(w.input_projection)

@@ -23,8 +23,9 @@ def _selection(rows_from: int, width: int, count: int) -> np.ndarray:
     return w
 
 
-def oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mask_bool):
-    """Context [T, H*64] from qkv rows via orc_attention with selection projections."""
+def oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mask_bool, q_norm=None, k_norm=None, eps=1e-5):
+    """Context [T, H*64] from qkv rows via orc_attention with selection
+    projections (and QK-norm scales, when given)."""
     T, width = qkv_bits.shape
     x = orc.bf16_widen(qkv_bits)
     w = {
@@ -35,7 +36,9 @@ def oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mask_bool):
         "o_w": _selection(0, H * 64, H * 64) if width == H * 64 else np.vstack(
             [np.eye(H * 64, dtype=np.float32), np.zeros((width - H * 64, H * 64), np.float32)]),
     }
-    out = orc.attention(x, w, H, Hkv, 64, 1e-5, cos, sin, mask_bool.astype(np.uint8), bf16_mode=True)
+    if q_norm is not None:
+        w["q_norm"], w["k_norm"] = q_norm, k_norm
+    out = orc.attention(x, w, H, Hkv, 64, eps, cos, sin, mask_bool.astype(np.uint8), bf16_mode=True)
     return out[:, : H * 64]
 
 
@@ -138,6 +141,88 @@ def test_rope_in_place_matches_rotate_head(orc, cuda_dev):
     assert np.array_equal(got[:, (H + Hkv) * 64:], qkv_bits[:, (H + Hkv) * 64:])  # V untouched
 
 
+def _oracle_qk_norm_rope(orc, qkv_bits, H, Hkv, qn, kn, eps, cos, sin):
+    """Q and K columns after attention_impl's per-head rms_norm_bf16 and
+    rotate_head (root.zig:500-530), from the oracle's own functions."""
+    x = orc.bf16_widen(qkv_bits)[:, : (H + Hkv) * 64].copy()
+    T = x.shape[0]
+    for t in range(T):
+        for hh in range(H + Hkv):
+            x[t, hh * 64:(hh + 1) * 64] = orc.rms_norm(x[t, hh * 64:(hh + 1) * 64], qn if hh < H else kn, eps,
+                                                       bf16_mode=True)
+    x = np.ascontiguousarray(x)
+    if cos is not None:
+        orc.lib().orc_rotate_rows(x, T, H + Hkv, 64, np.ascontiguousarray(cos, np.float32),
+                                  np.ascontiguousarray(sin, np.float32), 1)
+    return orc.bf16_bits(x)
+
+
+@pytest.mark.parametrize("T,H,Hkv,rope,scale", [(256, 4, 2, True, 1.0), (200, 2, 1, False, 1.0),
+                                                (64, 8, 2, True, 1e-3), (64, 2, 2, True, 40.0)])
+def test_qk_norm_then_rope_bit_exact(orc, cuda_dev, T, H, Hkv, rope, scale):
+    """Per-head RMSNorm with q_norm / k_norm, then RoPE, in place: every Q and
+    K element equals the oracle's rms_norm_bf16 + rotate_head bit for bit (the
+    GPU keeps the reference's sum-of-squares order), V stays untouched. The
+    scale moves the heads' magnitude (tiny and large rows)."""
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(T * 7 + H)
+    width = (H + 2 * Hkv) * 64
+    qkv_bits = orc.bf16_bits(orc.bf16_widen(gen_bf16(rng, (T, width))) * np.float32(scale))
+    qn = gen_bf16(rng, (64,))
+    kn = gen_bf16(rng, (64,))
+    eps = 1e-6
+    pos = ncm_model.level_positions(0, (T // 2, T - T // 2))
+    cos, sin = ncm_model.rope_tables(64, 1000000.0, pos) if rope else (None, None)
+    qkv = to_dev_bf16(qkv_bits, cuda_dev)
+    mask = ncm_model.make_mask("block_causal", 0, (T // 2, T - T // 2))
+    dev = (lambda a: None if a is None else torch.from_numpy(a).to(cuda_dev))  # noqa: E731
+    ncm_model.attention_bf16(qkv, H, Hkv, mask, dev(cos), dev(sin), q_norm=to_dev_bf16(qn, cuda_dev),
+                             k_norm=to_dev_bf16(kn, cuda_dev), eps=eps)
+    got = from_dev_bf16(qkv)
+    ref = _oracle_qk_norm_rope(orc, qkv_bits, H, Hkv, orc.bf16_widen(qn), orc.bf16_widen(kn), eps, cos, sin)
+    diff = np.argwhere(got[:, : (H + Hkv) * 64] != ref)
+    assert diff.size == 0, f"{len(diff)} Q/K elements differ; first {diff[0]}"
+    assert np.array_equal(got[:, (H + Hkv) * 64:], qkv_bits[:, (H + Hkv) * 64:])
+
+
+@pytest.mark.parametrize("mode,T,prefix,levels,pad,H,Hkv", [
+    ("block_causal", 256, 0, (16, 16, 32, 64, 128), (), 4, 2),
+    ("block_diagonal", 200, 1, (7, 32, 160), (True,), 2, 1),
+])
+def test_attention_qk_norm_matches_oracle(orc, cuda_dev, mode, T, prefix, levels, pad, H, Hkv):
+    """ncm_attention_qk_norm_bf16 against attention_impl with
+    query_norm_weight / key_norm_weight (root.zig:450-581, bf16 mode)."""
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(T + 11 * H)
+    width = (H + 2 * Hkv) * 64
+    qkv_bits = gen_bf16(rng, (T, width))
+    qn = orc.bf16_bits(1.0 + 0.2 * rng.standard_normal(64).astype(np.float32))
+    kn = orc.bf16_bits(1.0 + 0.2 * rng.standard_normal(64).astype(np.float32))
+    eps = 1e-6
+    mask, mb, pos = _mask_case(orc, mode, T, prefix, levels, pad)
+    cos, sin = ncm_model.rope_tables(64, 1000000.0, pos)
+    qkv = to_dev_bf16(qkv_bits, cuda_dev)
+    ctx = ncm_model.attention_bf16(qkv, H, Hkv, mask, torch.from_numpy(cos).to(cuda_dev),
+                                   torch.from_numpy(sin).to(cuda_dev), q_norm=to_dev_bf16(qn, cuda_dev),
+                                   k_norm=to_dev_bf16(kn, cuda_dev), eps=eps)
+    got = orc.bf16_widen(from_dev_bf16(ctx))
+    ref = oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mb, orc.bf16_widen(qn), orc.bf16_widen(kn), eps)
+    vmax = np.abs(orc.bf16_widen(qkv_bits[:, (H + Hkv) * 64:])).max()
+    err = np.abs(got - ref)
+    bad = np.argwhere(err > 2e-2 * np.abs(ref) + 1e-2 * vmax)
+    assert bad.size == 0, f"{len(bad)} context elements outside the bar; first {bad[0]}"
+
+
+def test_attention_qk_norm_needs_both_scales(cuda_dev):
+    from ncmorph_b200 import _lib, ncm_model
+    qkv = torch.zeros((64, 256), dtype=torch.bfloat16, device=cuda_dev)
+    qn = torch.ones((64,), dtype=torch.bfloat16, device=cuda_dev)
+    mask = ncm_model.make_mask("causal", 0, (), ())
+    with pytest.raises(_lib.NcmError) as e:
+        ncm_model.attention_bf16(qkv, 2, 1, mask, q_norm=qn)
+    assert e.value.status == _lib.NCM_EINVAL
+
+
 def test_rope_tables_bit_exact(orc):
     from ncmorph_b200 import ncm_model
     pos = ncm_model.level_positions(1, (3, 5))
@@ -235,6 +320,8 @@ def oracle_ncm_forward(orc, cfg, w, inputs_bits):
         n = norm_rows(h, f(L.ln_1))
         qkv = f(L.qkv)
         aw = {"q_w": qkv[: H * 64], "k_w": qkv[H * 64:(H + Hkv) * 64], "v_w": qkv[(H + Hkv) * 64:], "o_w": f(L.o)}
+        if L.q_norm is not None:
+            aw["q_norm"], aw["k_norm"] = f(L.q_norm), f(L.k_norm)
         att = orc.attention(n, aw, H, Hkv, 64, eps, cos, sin, mask.astype(np.uint8), bf16_mode=True)
         h = rb(h + att)
         n = norm_rows(h, f(L.ln_2))
@@ -259,6 +346,28 @@ def test_ncm_forward_small_matches_oracle(orc, cuda_dev, mask, prefix, levels):
     got = orc.bf16_widen(from_dev_bf16(out))
     ref = oracle_ncm_forward(orc, cfg, w, inputs)
     _assert_rows_within(got, ref, f"ncm forward {mask}")
+
+
+@pytest.mark.parametrize("levels", [(16, 16, 32, 64, 128), (8, 8, 16)])
+def test_ncm_forward_qk_norm_matches_oracle(orc, cuda_dev, levels):
+    """Layers with q_norm / k_norm (ncm_model.zig:42-43, as Qwen3-style
+    checkpoints carry): the projection runs without the RoPE epilogue and the
+    per-head norm + RoPE kernel follows it; 256 rows and 32 rows (the swapped
+    GEMM form)."""
+    from ncmorph_b200 import ncm_model
+    cfg = ncm_model.Config(hidden_size=256, vq_width=64, num_attention_heads=4, num_key_value_heads=2,
+                           intermediate_size=512, level_lengths=levels, prefix_length=0, mask="block_causal")
+    w = _rand_weights(cfg, cuda_dev, 8, layers=2)
+    g = torch.Generator(device=cuda_dev).manual_seed(9)
+    for L in w.layers:
+        L.q_norm = (1.0 + 0.2 * torch.randn((64,), generator=g, device=cuda_dev)).to(torch.bfloat16)
+        L.k_norm = (1.0 + 0.2 * torch.randn((64,), generator=g, device=cuda_dev)).to(torch.bfloat16)
+    rng = np.random.default_rng(10)
+    inputs = gen_bf16(rng, (cfg.seq_len, cfg.vq_width))
+    out = ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(out))
+    ref = oracle_ncm_forward(orc, cfg, w, inputs)
+    _assert_rows_within(got, ref, "ncm forward with QK-norm")
 
 
 def test_ncm_forward_decode_size_split_k_matches_oracle(orc, cuda_dev):

@@ -113,6 +113,25 @@ def test_rms_norm_cascade_sum_bits(orc):
     assert np.float32(orc.sum_squares_pinned(t)).view(np.uint32) == 0x40FD0000
 
 
+def test_head_sum_of_squares_order(orc):
+    """The order the QK-norm kernel sums one 64-wide head in: the cascade of
+    root.zig:152-224 with two 4x8 accumulator rows and no full level step,
+    acc[r][l] = x[8r+l]^2 + x[8(r+4)+l]^2, vs[l] = ((acc0 + acc1) + acc2) + acc3,
+    sum = vs[0] + ... + vs[7], each step rounded to f32."""
+    rng = np.random.default_rng(12)
+    f = np.float32
+    for scale in (1.0, 1e-3, 300.0):
+        for _ in range(200):
+            x = (rng.standard_normal(64) * scale).astype(f)
+            sq = (x * x).astype(f).reshape(8, 8)
+            acc = [f(sq[r] + sq[r + 4]) for r in range(4)]
+            vs = f(f(f(acc[0] + acc[1]) + acc[2]) + acc[3])
+            total = f(0)
+            for v in vs:
+                total = f(total + v)
+            assert total.view(np.uint32) == np.float32(orc.sum_squares_pinned(x)).view(np.uint32)
+
+
 def test_small_exact_cases(orc):
     # packages/kernels/root.zig:772-797
     assert np.array_equal(orc.softmax(np.array([2, 2], np.float32)), np.array([0.5, 0.5], np.float32))
