@@ -386,17 +386,22 @@ NCM_API int ncm_rope_tables_llama3_host(int32_t head_dim, float theta, float fac
                                         float high_freq_factor, int64_t original_max_position_embeddings,
                                         const int32_t* positions, int64_t T, float* cos_out, float* sin_out);
 
-/* Attention mask description. mode: 0 causal (causal_mask, root.zig:380-399,
- * no sliding window), 1 block-diagonal (src/ncm_mask.zig:10-42), 2 block-causal
- * (each level also sees every earlier level). In block modes positions are
- * [prefix | level 0 | level 1 | ...]; prefix_pad_mask bit i marks prefix key i
- * as padding (prefix_length <= 64). */
+/* Attention mask description. mode: 0 causal (causal_mask, root.zig:380-399;
+ * ncm_model's source_causal, src/ncm_model.zig:199-203), 1 block-diagonal
+ * (src/ncm_mask.zig:10-42), 2 block-causal (each level also sees every earlier
+ * level). In block modes positions are [prefix | level 0 | level 1 | ...];
+ * prefix_pad_mask bit i marks prefix key i as padding (prefix_length <= 64).
+ * sliding_window (causal mode only; 0 = none): query q sees keys
+ * q - sliding_window < k <= q. ncm_attention_bf16 ignores the levels in causal
+ * mode; ncm_ncm_forward still takes its RoPE positions and level embeddings
+ * from prefix_length and level_lengths there, as ncm_model does. */
 typedef struct ncm_mask {
   int32_t mode;
   int32_t prefix_length;
   uint64_t prefix_pad_mask;
   int32_t num_levels;
   int32_t level_lengths[32];
+  int32_t sliding_window;
 } ncm_mask_t;
 
 /* Multi-head GQA attention core of attention_impl in bf16 mode

@@ -51,6 +51,7 @@ class Mask(ctypes.Structure):
         ("prefix_pad_mask", ctypes.c_uint64),
         ("num_levels", c_i32),
         ("level_lengths", c_i32 * 32),
+        ("sliding_window", c_i32),
     ]
 
 

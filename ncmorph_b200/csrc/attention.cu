@@ -48,6 +48,7 @@ struct AttnArgs {
   int* err;
   int T, H, Hkv;
   int mode;        // 0 causal, 1 block-diagonal, 2 block-causal
+  int window;      // causal mode: keys q - window < k <= q (0: no window)
   int prefix;      // P (block modes)
   unsigned long long pad_mask;  // bit i set: prefix key i is padding
   int nlev;
@@ -61,12 +62,13 @@ __device__ __forceinline__ int level_of(const AttnArgs& a, int pos) {
   return l;
 }
 
-// Key intervals the CTA's queries may see: [0, P) and [A, B).
+// Key intervals the CTA's queries may see: [0, P) and [A, B). A sliding
+// window moves A up to the first query's earliest key.
 __device__ __forceinline__ void cta_key_span(const AttnArgs& a, int q0, int& P, int& A, int& B) {
   const int qmax = min(q0 + AT_Q - 1, a.T - 1);
   if (a.mode == 0) {
     P = 0;
-    A = 0;
+    A = a.window > 0 ? max(q0 - a.window + 1, 0) : 0;
     B = qmax + 1;
     return;
   }
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const TileSpan sp = span[gi];
     int lo = 0, hi = 0;
     if (args.mode == 0) {
-      lo = 0;
+      lo = args.window > 0 ? max(q - args.window + 1, 0) : 0;
       hi = q + 1;
     } else if (q >= args.prefix && q < args.T) {
       const int lq = level_of(args, q);
@@ -504,8 +506,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
 int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const uint16_t* vt, uint16_t* out, int T,
                    int H, int Hkv, int mode, int prefix, unsigned long long pad_mask, const int* level_lens,
-                   int nlev, cudaStream_t stream) {
-  if (T <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || nlev < 0 || nlev > kMaxLevels || prefix < 0 || prefix > 64)
+                   int nlev, int window, cudaStream_t stream) {
+  if (T <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || nlev < 0 || nlev > kMaxLevels ||
+      (mode != 0 && (prefix < 0 || prefix > 64)) || window < 0 || (window > 0 && mode != 0))
     return ncm_fail(NCM_EINVAL, "attention: bad arguments");
   AttnArgs a{};
   a.out = out;
@@ -514,6 +517,7 @@ int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const 
   a.H = H;
   a.Hkv = Hkv;
   a.mode = mode;
+  a.window = window;
   a.prefix = mode == 0 ? 0 : prefix;
   a.pad_mask = pad_mask;
   a.scale = 1.0f / std::sqrt(static_cast<float>(AT_D));

@@ -189,10 +189,11 @@ void rope_tables_host(int head_dim, float theta, const int* positions, int T, fl
                       const RopeLlama3* llama3 = nullptr);
 // Fused masked attention over the Q and K columns of fused QKV rows (row
 // stride qkv_stride elements) and V transposed to [Hkv*64, T]; head_dim 64.
-// mode 0 causal, 1 block-diagonal, 2 block-causal.
+// mode 0 causal (window > 0: keys q - window < k <= q), 1 block-diagonal,
+// 2 block-causal.
 int attention_bf16(ncm_ctx* ctx, const uint16_t* qkv, int64_t qkv_stride, const uint16_t* vt, uint16_t* out, int T,
                    int H, int Hkv, int mode, int prefix, unsigned long long pad_mask, const int* level_lens,
-                   int nlev, cudaStream_t stream);
+                   int nlev, int window, cudaStream_t stream);
 
 // ---- RVQ launchers (rvq.cu)
 struct RvqPartial {

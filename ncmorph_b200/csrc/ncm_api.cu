@@ -23,6 +23,8 @@ int ctx_ok(ncm_ctx* ctx) {
 int check_mask(const ncm_mask_t* m, int64_t T) {
   if (m == nullptr) return ncm_fail(NCM_EINVAL, "attention: null mask");
   if (m->mode < 0 || m->mode > 2) return ncm_fail(NCM_EINVAL, "attention: mask mode %d unknown", m->mode);
+  if (m->sliding_window < 0 || (m->sliding_window > 0 && m->mode != 0))
+    return ncm_fail(NCM_EINVAL, "attention: sliding_window %d (non-negative, causal mode only)", m->sliding_window);
   if (m->mode == 0) return NCM_OK;
   if (m->prefix_length < 0 || m->prefix_length > 64)
     return ncm_fail(NCM_EINVAL, "attention: prefix_length %d outside [0, 64]", m->prefix_length);
@@ -128,7 +130,8 @@ static int attention_entry(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, co
   }
   Launch _l(ctx, KID_ATTENTION, st);
   return attention_bf16(ctx, qkv, qkv_stride, vt, out, static_cast<int>(T), heads, kv_heads, mask->mode,
-                        mask->prefix_length, mask->prefix_pad_mask, mask->level_lengths, mask->num_levels, st);
+                        mask->prefix_length, mask->prefix_pad_mask, mask->level_lengths, mask->num_levels,
+                        mask->sliding_window, st);
 }
 
 int ncm_attention_bf16(ncm_ctx_t* ctx, uint16_t* qkv, int64_t qkv_stride, const float* cos_t, const float* sin_t,
@@ -186,9 +189,16 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
   if (rc) return rc;
   if (!cfg || !W || !inputs || !out) return ncm_fail(NCM_EINVAL, "ncm_forward: null argument");
   const ncm_mask_t& m = cfg->mask;
-  if (m.mode != 1 && m.mode != 2) return ncm_fail(NCM_EINVAL, "ncm_forward: mask mode must be block-diagonal or block-causal");
+  // causal mode is ncm_model's source_causal: the levels still give the RoPE
+  // positions and the level embeddings
+  if (m.num_levels <= 0 || m.num_levels > 32 || m.prefix_length < 0)
+    return ncm_fail(NCM_EINVAL, "ncm_forward: num_levels %d or prefix_length %d out of range", m.num_levels,
+                    m.prefix_length);
   int64_t T = m.prefix_length;
-  for (int i = 0; i < m.num_levels && i < 32; ++i) T += m.level_lengths[i];
+  for (int i = 0; i < m.num_levels; ++i) {
+    if (m.level_lengths[i] <= 0) return ncm_fail(NCM_EINVAL, "ncm_forward: level %d is empty", i);
+    T += m.level_lengths[i];
+  }
   const int64_t Hd = cfg->hidden_size, V = cfg->vq_width, F = cfg->intermediate_size;
   const int H = static_cast<int>(cfg->num_attention_heads), Hkv = static_cast<int>(cfg->num_key_value_heads);
   if (cfg->head_dim != 64) return ncm_fail(NCM_EINVAL, "ncm_forward: head_dim must be 64");
@@ -372,7 +382,7 @@ int ncm_ncm_forward(ncm_ctx_t* ctx, const ncm_decoder_config_t* cfg, const ncm_d
     {
       Launch _l(ctx, KID_ATTENTION, st);
       if ((rc = attention_bf16(ctx, qkv, QKV, vt, ctxb, Ti, H, Hkv, m.mode, m.prefix_length, m.prefix_pad_mask,
-                               m.level_lengths, m.num_levels, st)))
+                               m.level_lengths, m.num_levels, m.sliding_window, st)))
         return rc;
     }
     // h = bf16(h + bf16(ctx . O^T + b)) in the projection's epilogue

@@ -21,9 +21,11 @@ MASK_MODES = {"causal": 0, "block_diagonal": 1, "block_causal": 2}
 bf16 = torch.bfloat16
 
 
-def make_mask(mode: str, prefix_length: int = 0, level_lengths=(), prefix_pad=()) -> _lib.Mask:
+def make_mask(mode: str, prefix_length: int = 0, level_lengths=(), prefix_pad=(),
+              sliding_window: int | None = None) -> _lib.Mask:
     m = _lib.Mask()
     m.mode = MASK_MODES[mode]
+    m.sliding_window = int(sliding_window or 0)
     m.prefix_length = int(prefix_length)
     bits = 0
     for i, padded in enumerate(prefix_pad):
@@ -140,7 +142,10 @@ class Config:
     intermediate_size: int
     level_lengths: tuple
     prefix_length: int = 0
+    # "causal" is ncm_model's source_causal (src/ncm_model.zig:199-203), which
+    # may carry a sliding window; the block masks take none
     mask: str = "block_causal"
+    sliding_window: int | None = None
     rms_norm_epsilon: float = 1e-5
     rope_theta: float = 500000.0
     use_level_encoding: bool = True
@@ -169,7 +174,7 @@ def forward(cfg: Config, w: Weights, inputs: torch.Tensor, out: torch.Tensor | N
     c.head_dim, c.intermediate_size = cfg.head_dim, cfg.intermediate_size
     c.rms_norm_epsilon, c.rope_theta = cfg.rms_norm_epsilon, cfg.rope_theta
     c.use_level_encoding = int(cfg.use_level_encoding)
-    c.mask = make_mask(cfg.mask, cfg.prefix_length, cfg.level_lengths)
+    c.mask = make_mask(cfg.mask, cfg.prefix_length, cfg.level_lengths, sliding_window=cfg.sliding_window)
     if cfg.rope_llama3 is not None:
         c.rope_type = 1
         (c.rope_factor, c.rope_low_freq_factor, c.rope_high_freq_factor,

@@ -42,11 +42,12 @@ def oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mask_bool, q_norm=Non
     return out[:, : H * 64]
 
 
-def _mask_case(orc, mode, T, prefix=0, levels=(), pad=()):
+def _mask_case(orc, mode, T, prefix=0, levels=(), pad=(), window=None):
     from ncmorph_b200.ncm_model import level_positions, make_mask
     if mode == "causal":
-        mb = orc.causal_mask(np.arange(T), np.arange(T))
+        mb = orc.causal_mask(np.arange(T), np.arange(T), window or 0)
         pos = np.arange(T, dtype=np.int32)
+        return make_mask(mode, prefix, levels, pad, sliding_window=window), mb, pos
     elif mode == "block_diagonal":
         mb = orc.block_diagonal_mask(prefix, list(levels), list(pad))
         pos = level_positions(prefix, levels)
@@ -82,6 +83,45 @@ def test_attention_matches_oracle(orc, cuda_dev, mode, T, prefix, levels, pad, H
     bad = np.argwhere(err > tol)
     assert bad.size == 0, f"{len(bad)} context elements outside the bar; first {bad[0]} got {got[tuple(bad[0])]} ref {ref[tuple(bad[0])]}"
     print(f"{mode} T={T}: max |err| {err.max():.3g}, mean {err.mean():.3g}")
+
+
+@pytest.mark.parametrize("T,window,H,Hkv", [(384, 100, 4, 2), (512, 128, 2, 1), (1024, 300, 4, 1),
+                                             (264, 1, 2, 2), (256, 4096, 2, 1)])
+def test_attention_sliding_window_matches_oracle(orc, cuda_dev, T, window, H, Hkv):
+    """Causal attention with a sliding window (causal_mask, root.zig:380-399:
+    q - W < k <= q): windows inside a tile, on a tile boundary, across
+    several tiles, of one key, and wider than the sequence; key tiles left of
+    every query's window are skipped."""
+    from ncmorph_b200 import ncm_model
+    rng = np.random.default_rng(T + window)
+    width = (H + 2 * Hkv) * 64
+    qkv_bits = gen_bf16(rng, (T, width))
+    mask, mb, pos = _mask_case(orc, "causal", T, window=window)
+    cos, sin = ncm_model.rope_tables(64, 10000.0, pos)
+    ctx = ncm_model.attention_bf16(to_dev_bf16(qkv_bits, cuda_dev), H, Hkv, mask, torch.from_numpy(cos).to(cuda_dev),
+                                   torch.from_numpy(sin).to(cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(ctx))
+    ref = oracle_attention_core(orc, qkv_bits, H, Hkv, cos, sin, mb)
+    vmax = np.abs(orc.bf16_widen(qkv_bits[:, (H + Hkv) * 64:])).max()
+    err = np.abs(got - ref)
+    bad = np.argwhere(err > 2e-2 * np.abs(ref) + 1e-2 * vmax)
+    assert bad.size == 0, f"{len(bad)} context elements outside the bar; first {bad[0]}"
+    if window == 1:
+        # one key: the context is that row's own V head, rounded
+        v = orc.bf16_widen(qkv_bits[:, (H + Hkv) * 64:])
+        for hh in range(H):
+            kv = hh // (H // Hkv)
+            assert np.array_equal(got[:, hh * 64:(hh + 1) * 64], v[:, kv * 64:(kv + 1) * 64])
+
+
+def test_sliding_window_only_in_causal_mode(cuda_dev):
+    from ncmorph_b200 import _lib, ncm_model
+    qkv = torch.zeros((64, 256), dtype=torch.bfloat16, device=cuda_dev)
+    for mask in (ncm_model.make_mask("block_causal", 0, (32, 32), sliding_window=8),
+                 ncm_model.make_mask("causal", sliding_window=-1)):
+        with pytest.raises(_lib.NcmError) as e:
+            ncm_model.attention_bf16(qkv, 2, 1, mask)
+        assert e.value.status == _lib.NCM_EINVAL
 
 
 @pytest.mark.parametrize("step", [128, 512])
@@ -308,8 +348,12 @@ def oracle_ncm_forward(orc, cfg, w, inputs_bits):
             h[off:off + n] = rb(h[off:off + n] + emb[i])
         off += n
     cos, sin = _oracle_rope(orc, cfg)
-    mask = (orc.block_causal_mask if cfg.mask == "block_causal" else orc.block_diagonal_mask)(
-        cfg.prefix_length, list(cfg.level_lengths))
+    if cfg.mask == "causal":
+        # source_causal (ncm_model.zig:199-203): sequence order, optional window
+        mask = orc.causal_mask(np.arange(T), np.arange(T), cfg.sliding_window or 0)
+    else:
+        mask = (orc.block_causal_mask if cfg.mask == "block_causal" else orc.block_diagonal_mask)(
+            cfg.prefix_length, list(cfg.level_lengths))
     H, Hkv, F = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size
     eps = cfg.rms_norm_epsilon
 
@@ -346,6 +390,25 @@ def test_ncm_forward_small_matches_oracle(orc, cuda_dev, mask, prefix, levels):
     got = orc.bf16_widen(from_dev_bf16(out))
     ref = oracle_ncm_forward(orc, cfg, w, inputs)
     _assert_rows_within(got, ref, f"ncm forward {mask}")
+
+
+@pytest.mark.parametrize("prefix,levels,window", [(2, (16, 16, 32, 64, 126), None), (0, (16, 16, 32, 64, 128), 96),
+                                                  (1, (7, 32), 8)])
+def test_ncm_forward_source_causal_matches_oracle(orc, cuda_dev, prefix, levels, window):
+    """ncm_model with source_causal (src/ncm_model.zig:199-203): causal in
+    sequence order with an optional sliding window, while RoPE positions and
+    level embeddings still follow the levels."""
+    from ncmorph_b200 import ncm_model
+    cfg = ncm_model.Config(hidden_size=256, vq_width=64, num_attention_heads=4, num_key_value_heads=2,
+                           intermediate_size=512, level_lengths=levels, prefix_length=prefix, mask="causal",
+                           sliding_window=window)
+    w = _rand_weights(cfg, cuda_dev, 11, layers=2)
+    rng = np.random.default_rng(12)
+    inputs = gen_bf16(rng, (cfg.seq_len, cfg.vq_width))
+    out = ncm_model.forward(cfg, w, to_dev_bf16(inputs, cuda_dev))
+    got = orc.bf16_widen(from_dev_bf16(out))
+    ref = oracle_ncm_forward(orc, cfg, w, inputs)
+    _assert_rows_within(got, ref, f"ncm forward source_causal window {window}")
 
 
 @pytest.mark.parametrize("levels", [(16, 16, 32, 64, 128), (8, 8, 16)])
