@@ -90,6 +90,7 @@ def test_config1_encode_decode(orc, cuda_dev):
     (300 * 128, 64, 300, 2, True),
     (300 * 128, 64, 300, 1, False),         # one level: its input is the bf16 rows themselves
     (160 * 128, 72, 32, 37, False),         # two 32-level code groups in the decode
+    (60 * 256 + 77, 256, 1024, 2, True),    # 61 ragged 256-row units: CTA pairs with some pairs idle-free
 ])
 def test_fused_update_path_matches_oracle(orc, cuda_dev, N, D, K, L, keep):
     """Row blocks >= SM count: one code split, so the residual update (f32 and
