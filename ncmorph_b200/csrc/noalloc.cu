@@ -143,7 +143,8 @@ extern "C" NCM_API int ncm_rvq_level_noalloc(float* residual, const uint16_t* co
   const size_t sq_bytes = sqnorm ? 0 : round256(static_cast<size_t>(K) * sizeof(float));
   size_t need = kErrBytes + shadow_bytes + round256(plan.partial_bytes) + sq_bytes;
   if (need > kNoAllocScratchBytes && plan.splits > 1) {
-    // the partials do not fit: one split per row block needs none
+    // the partials do not fit: one split per 128-row block needs none
+    plan.pair = 0;
     plan.splits = 1;
     plan.tiles_per_split = plan.code_tiles;
     plan.n_units = plan.row_blocks;

@@ -989,56 +989,68 @@ int max_active_pairs(int num_sms) {
 }
 }  // namespace
 
-RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K, bool allow_pair) {
-  RvqPlan p{};
-  p.row_blocks = ceil_div(N, BM);
-  p.code_tiles = ceil_div(K, BN);
-  if (allow_pair) {
-    // CTA pairs (one MMA over 256 rows, each CTA loading half of every code
-    // tile) when the 256-row units alone fill every pair: no code split
-    const int pairs = max_active_pairs(num_sms);
-    const int units = ceil_div(N, 2 * BM);
-    if (pairs > 0 && units >= pairs) {
-      p.pair = 1;
-      p.splits = 1;
-      p.tiles_per_split = p.code_tiles;
-      p.n_units = units;
-      p.grid = 2 * pairs;
-      p.partial_bytes = 0;
-      return p;
-    }
-  }
-  if (p.row_blocks >= num_sms) {
-    // enough row blocks for every SM: no code split, so the residual update
-    // can run inside the distance kernel
-    p.splits = 1;
-    p.tiles_per_split = p.code_tiles;
-    p.n_units = p.row_blocks;
-    p.grid = num_sms;
-    p.partial_bytes = 0;
-    return p;
-  }
-  // Pick the split count that minimises (waves x tiles per unit); prefer fewer
-  // splits on ties since every split adds a partial write and a reduction.
-  long long best_cost = -1;
-  int best_s = 1;
-  for (int s = 1; s <= p.code_tiles; ++s) {
-    const int tps = ceil_div(p.code_tiles, s);
-    const int s_eff = ceil_div(p.code_tiles, tps);
+// Split count s minimising (waves x tiles per unit) for `blocks` row units
+// on `slots` concurrent workers; fewer splits on ties, since every split adds
+// a partial write and a reduction.
+static void best_split(int blocks, int code_tiles, int slots, int& best_s, long long& best_cost) {
+  best_cost = -1;
+  best_s = 1;
+  for (int s = 1; s <= code_tiles; ++s) {
+    const int tps = ceil_div(code_tiles, s);
+    const int s_eff = ceil_div(code_tiles, tps);
     if (s_eff != s) continue;
-    const long long units = static_cast<long long>(p.row_blocks) * s;
-    const long long waves = (units + num_sms - 1) / num_sms;
+    const long long units = static_cast<long long>(blocks) * s;
+    const long long waves = (units + slots - 1) / slots;
     const long long cost = waves * tps;
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best_s = s;
     }
   }
-  p.splits = best_s;
-  p.tiles_per_split = ceil_div(p.code_tiles, best_s);
-  p.n_units = p.row_blocks * p.splits;
+}
+
+RvqPlan rvq_plan(int num_sms, int64_t N, int64_t K, bool allow_pair) {
+  RvqPlan p{};
+  p.row_blocks = ceil_div(N, BM);
+  p.code_tiles = ceil_div(K, BN);
+  // one-CTA units: (128-row block, code range) on every SM; with enough row
+  // blocks for every SM there is no code split, so the residual update can
+  // run inside the distance kernel
+  int s1 = 1;
+  long long cost1 = 0;
+  if (p.row_blocks >= num_sms)
+    cost1 = static_cast<long long>(ceil_div(p.row_blocks, num_sms)) * p.code_tiles;
+  else
+    best_split(p.row_blocks, p.code_tiles, num_sms, s1, cost1);
+  p.splits = s1;
+  p.tiles_per_split = ceil_div(p.code_tiles, s1);
+  p.n_units = p.row_blocks * s1;
   p.grid = p.n_units < num_sms ? p.n_units : num_sms;
-  p.partial_bytes = p.splits > 1 ? static_cast<size_t>(p.splits) * N * sizeof(RvqPartial) : 0;
+  p.partial_bytes = s1 > 1 ? static_cast<size_t>(s1) * N * sizeof(RvqPartial) : 0;
+  if (allow_pair) {
+    // CTA pairs: one MMA over 256 rows, each CTA loading half of every code
+    // tile, so a pair's tile step costs a one-CTA step in time with a third
+    // less operand traffic per SM and deeper staging. Used whenever its step
+    // count (waves x tiles per unit over the pairs) is no larger.
+    const int pairs = max_active_pairs(num_sms);
+    const int units = ceil_div(N, 2 * BM);
+    if (pairs > 0) {
+      int s2 = 1;
+      long long cost2 = 0;
+      if (units >= pairs)
+        cost2 = static_cast<long long>(ceil_div(units, pairs)) * p.code_tiles;
+      else
+        best_split(units, p.code_tiles, pairs, s2, cost2);
+      if (cost2 <= cost1) {
+        p.pair = 1;
+        p.splits = s2;
+        p.tiles_per_split = ceil_div(p.code_tiles, s2);
+        p.n_units = units * s2;
+        p.grid = 2 * (p.n_units < pairs ? p.n_units : pairs);  // every pair gets at least one unit
+        p.partial_bytes = s2 > 1 ? static_cast<size_t>(s2) * N * sizeof(RvqPartial) : 0;
+      }
+    }
+  }
   return p;
 }
 
@@ -1046,7 +1058,7 @@ cudaError_t launch_rvq_argmin(const RvqPlan& plan, const CUtensorMap& tmA, const
                               const float* sqnorm, int32_t* codes, RvqPartial* part, int* err, int64_t N,
                               int64_t D, int64_t K, cudaStream_t stream, const RvqFusedUpdate* fu,
                               const RvqTop2* top2, const float* mul_dev, int* counters) {
-  if (plan.pair && (top2 != nullptr || plan.splits != 1)) return cudaErrorInvalidValue;
+  if (plan.pair && top2 != nullptr) return cudaErrorInvalidValue;
   // the shared-memory opt-in is per device and per instantiation: remember which devices have it
   static DeviceFlags attr_set[3];
   const int gi = plan.pair ? 2 : (top2 != nullptr ? 1 : 0);
