@@ -245,6 +245,11 @@ def test_rvq_level_top2_duplicate_codeword_gap_is_zero(cuda_dev):
     (2048, 1024, 2048, 8, False),    # D = 1024 (slices of 128 columns: residual in global memory)
     (640, 64, 300, 6, True),         # 5 row blocks, slice 32 over two CTAs
     (4096, 256, 256, 5, True),       # one code tile: clusters of one CTA
+    # the operand kept in shared memory (64-column slices, D <= 256): clusters of 2 and 3 CTAs,
+    # a ragged last slice (56 columns) and ragged rows
+    (2000, 128, 512, 5, True),
+    (1536, 192, 768, 4, False),
+    (3000, 248, 1024, 4, True),
 ])
 def test_small_encode_in_one_launch_matches_levels(orc, cuda_dev, N, D, K, L, keep):
     """Few row blocks: every level runs in one launch, one cluster of CTAs per
