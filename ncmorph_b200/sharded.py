@@ -231,6 +231,83 @@ def sharded_encode(x_local: torch.Tensor, codebooks: torch.Tensor, total_rows: i
     return codes, recon
 
 
+# ----------------------------------------------------- batch-sharded tokenizer
+
+def _device_tokenizer(x, w_in, codebooks, w_out, pool_factors, **kw):
+    from . import vq
+    return vq.tokenizer_forward(x, w_in, codebooks, w_out, pool_factors, **kw)
+
+
+class ShardedTokenizer:
+    """Multiscale tokenizer forward (R6) sharded by whole batch items.
+
+    Every pooling window of the tokenizer lies inside one batch item, so rank
+    r runs the whole forward on its items [b0, b1) of the global batch with
+    no exchange, and the results are all-gathered once at the end: codes per
+    scale [L, B*T/f_s], reconstructions [B, T, D] and outputs [B, T, Din],
+    each in the batch order of a single-GPU forward. Ranks hold equally many
+    (padded) items so one all_gather_into_tensor per tensor suffices; the
+    last ranks may hold fewer real items, or none.
+
+    `forward(x, w_in, codebooks, w_out, pool_factors, **kw)` returns
+    (codes list, recon, y) as ncmorph_b200.vq.tokenizer_forward does, which is
+    the default.
+    """
+
+    def __init__(self, batch: int, seq_len: int, pool_factors: list[int], group=None,
+                 forward: Callable | None = None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.batch, self.T = batch, seq_len
+        self.pool_factors = list(pool_factors)
+        if any(seq_len % f for f in self.pool_factors):
+            raise ValueError("every pool factor must divide the sequence length")
+        self.forward = forward or _device_tokenizer
+        self.b0, self.b1, self.nb = shard_bounds(batch, self.world, self.rank)
+
+    @property
+    def items(self) -> int:
+        return self.b1 - self.b0
+
+    def _gather(self, local: torch.Tensor, per_item: int) -> torch.Tensor:
+        """[nb * per_item, ...] on every rank -> [batch * per_item, ...] in batch order."""
+        out = torch.empty((self.world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+        parts = []
+        for r in range(self.world):
+            b0, b1, _ = shard_bounds(self.batch, self.world, r)
+            base = r * self.nb * per_item
+            parts.append(out[base:base + (b1 - b0) * per_item])
+        return torch.cat(parts, 0)
+
+    def __call__(self, x_local: torch.Tensor, w_in: torch.Tensor, codebooks: torch.Tensor, w_out: torch.Tensor,
+                 **kw) -> tuple[list[torch.Tensor], torch.Tensor, torch.Tensor]:
+        if x_local.shape[0] != self.items or x_local.shape[1] != self.T:
+            raise ValueError(f"rank {self.rank} owns batch items [{self.b0}, {self.b1}) of length {self.T} "
+                             f"but got {tuple(x_local.shape[:2])}")
+        S, L, D = codebooks.shape[0], codebooks.shape[1], codebooks.shape[-1]
+        if len(self.pool_factors) != S:
+            raise ValueError("one pool factor per scale is required")
+        Din, dev = x_local.shape[2], x_local.device
+        rows = [self.T // f for f in self.pool_factors]  # pooled rows per batch item, per scale
+        codes_pad = [torch.zeros((L, self.nb * n), dtype=torch.int32, device=dev) for n in rows]
+        recon_pad = torch.zeros((self.nb, self.T, D), dtype=torch.bfloat16, device=dev)
+        y_pad = torch.zeros((self.nb, self.T, Din), dtype=torch.bfloat16, device=dev)
+        if self.items > 0:
+            codes, recon, y = self.forward(x_local, w_in, codebooks, w_out, self.pool_factors, **kw)
+            for s, n in enumerate(rows):
+                codes_pad[s][:, : self.items * n] = codes[s]
+            recon_pad[: self.items] = recon
+            y_pad[: self.items] = y
+        # codes: gather each scale as [nb * n, L] rows so the batch order is the row order
+        codes_all = [self._gather(c.t(), n).t().contiguous() for c, n in zip(codes_pad, rows)]
+        recon_all = self._gather(recon_pad.view(self.nb * self.T, D), self.T).view(self.batch, self.T, D)
+        y_all = self._gather(y_pad.view(self.nb * self.T, Din), self.T).view(self.batch, self.T, Din)
+        return codes_all, recon_all, y_all
+
+
 # ---------------------------------------------------------------- C ABI form
 # The same sharding through the library's own NCCL communicator
 # (ncm_ctx_comm_init / ncm_rvq_encode_sharded), for hosts without a

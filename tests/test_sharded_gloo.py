@@ -108,3 +108,73 @@ def test_shard_bounds_cover_rows_once():
             if covered is not None:
                 assert covered == list(range(total))
             assert spans[0][0] == 0 and spans[-1][1] == total
+
+
+# ----------------------------------------------------- batch-sharded tokenizer
+def _fake_tokenizer(x, w_in, codebooks, w_out, pool_factors, **kw):
+    """Stands in for tokenizer_forward with the same shapes; every output of a
+    batch item depends only on that item (as the real forward's do)."""
+    b, T, Din = x.shape
+    S, L, K, D = codebooks.shape
+    xf = x.float()
+    codes = []
+    for f in pool_factors:
+        pooled = xf.view(b, T // f, f, Din).mean(2).reshape(b * T // f, Din)
+        codes.append(torch.stack([(pooled[:, l % Din] * 1000).round().to(torch.int32) + l for l in range(L)]))
+    recon = xf[..., :D].to(torch.bfloat16)
+    y = (xf * 2).to(torch.bfloat16)
+    return codes, recon, y
+
+
+def _tok_data(batch, T=16, Din=8, D=4, S=3, L=2, K=5):
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((batch, T, Din), generator=g).to(torch.bfloat16)
+    cbs = torch.randn((S, L, K, D), generator=g).to(torch.bfloat16)
+    return x, cbs, [4, 2, 1]
+
+
+def _tok_worker(rank, world, port, batch, out_path):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from ncmorph_b200.sharded import ShardedTokenizer
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        x, cbs, pf = _tok_data(batch)
+        tok = ShardedTokenizer(batch, x.shape[1], pf, forward=_fake_tokenizer)
+        codes, recon, y = tok(x[tok.b0:tok.b1], None, cbs, None)
+        torch.save({"codes": codes, "recon": recon.view(torch.int16), "y": y.view(torch.int16),
+                    "items": tok.items}, out_path + f".{rank}")
+    except Exception as e:  # noqa: BLE001
+        with open(out_path + f".err{rank}", "w") as f:
+            f.write(repr(e))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("world,batch", [(2, 4), (2, 3), (3, 2)])
+def test_sharded_tokenizer_matches_single_process(world, batch):
+    """Whole batch items per rank (uneven, and a rank with none): every rank
+    gets the codes of every scale, the reconstructions and the outputs in the
+    batch order of one forward over the whole batch."""
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "tok")
+        mp.start_processes(_tok_worker, args=(world, port, batch, out), nprocs=world, join=True,
+                           start_method="spawn")
+        errs = {r: open(out + f".err{r}").read() for r in range(world) if os.path.exists(out + f".err{r}")}
+        assert not errs, errs
+        res = [torch.load(out + f".{r}") for r in range(world)]
+    x, cbs, pf = _tok_data(batch)
+    codes, recon, y = _fake_tokenizer(x, None, cbs, None, pf)
+    assert sum(r["items"] for r in res) == batch
+    for r in res:
+        assert len(r["codes"]) == len(pf)
+        for s in range(len(pf)):
+            assert torch.equal(r["codes"][s], codes[s]), (s, r["codes"][s], codes[s])
+        assert torch.equal(r["recon"], recon.view(torch.int16))
+        assert torch.equal(r["y"], y.view(torch.int16))
