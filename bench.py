@@ -1094,6 +1094,74 @@ def run_extras(a, dev):
     return out
 
 
+def run_tokenizer_sharded(a):
+    """Config 2 on N GPUs (torchrun): ShardedTokenizer with 8 batch items per
+    GPU (weak scaling; weights and codebooks identical on every rank, each
+    rank's items from its own seed). A step is the whole sharded forward,
+    the all-gather of the codes included; timed with CUDA events between
+    barriers, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ncmorph_b200 import sharded
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    try:
+        g = torch.Generator(device=dev).manual_seed(a.seed)
+
+        def rnd(shape, scale=1.0):
+            return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+        c = _tokenizer_setup(a, dev, rnd, g)
+        B, T = c["B"], c["T"]
+        gx = torch.Generator(device=dev).manual_seed(a.seed + 1000 + rank)
+        x = torch.randn((B, T, c["Din"]), generator=gx, device=dev).to(torch.bfloat16)
+        tok = sharded.ShardedTokenizer(B * world, T, c["factors"])
+        kw = dict(sqnorms=c["sq"], upsample=a.upsample, phi_weight=c["pw"], phi_bias=c["pb"], phi_ratio=0.5)
+
+        def step():
+            return tok(x, c["w_in"], c["cbs"], c["w_out"], **kw)
+
+        for _ in range(a.warmup):
+            step()
+        sampler = ClockSampler(local) if rank == 0 else None
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+        if sampler:
+            sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[local])
+        clocks = sampler.stop() if sampler else None
+        ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        if rank == 0:
+            emit({"metric": "tokenizer_vectors_per_s", "value": B * world * T / (ms * 1e-3), "unit": "vectors/s",
+                  "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+                  "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                  "dtype": "bf16 operands, f32 accumulation", "data": "synthetic",
+                  "config": {"workload": "multiscale tokenizer forward (BASELINE config 2), batch-sharded",
+                             "batch_per_gpu": B, "global_batch": B * world, "seq_len": T,
+                             "pool_factors": c["factors"], "parallelism": f"batch items x{world}",
+                             "collective": "NCCL all_gather of the codes of every scale (reconstructions and "
+                                           "outputs stay with the rank that owns the batch items)"},
+                  "e2e": None, "clocks": clocks})
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
 def run_secondary(a):
     import torch
 
@@ -1131,6 +1199,8 @@ def run_secondary(a):
 def main():
     _claim_stdout()
     a = parse_args()
+    if a.workload == "tokenizer" and int(os.environ.get("WORLD_SIZE", "1")) > 1 and a.impl != "reference":
+        return run_tokenizer_sharded(a)
     if a.workload != "rvq":
         return run_secondary(a)
     if a.impl == "reference":

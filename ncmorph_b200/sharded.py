@@ -243,9 +243,12 @@ class ShardedTokenizer:
 
     Every pooling window of the tokenizer lies inside one batch item, so rank
     r runs the whole forward on its items [b0, b1) of the global batch with
-    no exchange, and the results are all-gathered once at the end: codes per
-    scale [L, B*T/f_s], reconstructions [B, T, D] and outputs [B, T, Din],
-    each in the batch order of a single-GPU forward. Ranks hold equally many
+    no exchange, and the results are all-gathered once at the end in the
+    batch order of a single-GPU forward: the codes per scale [L, B*T/f_s]
+    always; with gather="all" also the reconstructions [B, T, D] and the
+    outputs [B, T, Din] (with the default gather="codes" those stay this
+    rank's items, as data-parallel training uses them: gathering them moves
+    3 * 2 * T * D bytes per item every call). Ranks hold equally many
     (padded) items so one all_gather_into_tensor per tensor suffices; the
     last ranks may hold fewer real items, or none.
 
@@ -255,7 +258,10 @@ class ShardedTokenizer:
     """
 
     def __init__(self, batch: int, seq_len: int, pool_factors: list[int], group=None,
-                 forward: Callable | None = None):
+                 forward: Callable | None = None, gather: str = "codes"):
+        if gather not in ("codes", "all"):
+            raise ValueError('gather is "codes" or "all"')
+        self.gather = gather
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.group = group
@@ -293,16 +299,21 @@ class ShardedTokenizer:
         Din, dev = x_local.shape[2], x_local.device
         rows = [self.T // f for f in self.pool_factors]  # pooled rows per batch item, per scale
         codes_pad = [torch.zeros((L, self.nb * n), dtype=torch.int32, device=dev) for n in rows]
-        recon_pad = torch.zeros((self.nb, self.T, D), dtype=torch.bfloat16, device=dev)
-        y_pad = torch.zeros((self.nb, self.T, Din), dtype=torch.bfloat16, device=dev)
         if self.items > 0:
             codes, recon, y = self.forward(x_local, w_in, codebooks, w_out, self.pool_factors, **kw)
             for s, n in enumerate(rows):
                 codes_pad[s][:, : self.items * n] = codes[s]
-            recon_pad[: self.items] = recon
-            y_pad[: self.items] = y
+        else:
+            recon = torch.empty((0, self.T, D), dtype=torch.bfloat16, device=dev)
+            y = torch.empty((0, self.T, Din), dtype=torch.bfloat16, device=dev)
         # codes: gather each scale as [nb * n, L] rows so the batch order is the row order
         codes_all = [self._gather(c.t(), n).t().contiguous() for c, n in zip(codes_pad, rows)]
+        if self.gather == "codes":
+            return codes_all, recon, y
+        recon_pad = torch.zeros((self.nb, self.T, D), dtype=torch.bfloat16, device=dev)
+        y_pad = torch.zeros((self.nb, self.T, Din), dtype=torch.bfloat16, device=dev)
+        recon_pad[: self.items] = recon
+        y_pad[: self.items] = y
         recon_all = self._gather(recon_pad.view(self.nb * self.T, D), self.T).view(self.batch, self.T, D)
         y_all = self._gather(y_pad.view(self.nb * self.T, Din), self.T).view(self.batch, self.T, Din)
         return codes_all, recon_all, y_all

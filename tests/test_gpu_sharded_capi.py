@@ -124,7 +124,7 @@ def _worker_tokenizer(rank, nranks, port, batch, out_dir):
         w_in = (torch.randn((D, Din), generator=g, device=dev) * 0.05).to(torch.bfloat16)
         w_out = (torch.randn((Din, D), generator=g, device=dev) * 0.05).to(torch.bfloat16)
         cbs = (torch.randn((S, L, K, D), generator=g, device=dev)).to(torch.bfloat16)
-        tok = sharded.ShardedTokenizer(batch, T, pf)
+        tok = sharded.ShardedTokenizer(batch, T, pf, gather="all")
         codes, recon, y = tok(x[tok.b0:tok.b1].contiguous(), w_in, cbs, w_out)
         # reference: each rank's items through one single-GPU forward, in batch order
         refs = []

@@ -133,7 +133,7 @@ def _tok_data(batch, T=16, Din=8, D=4, S=3, L=2, K=5):
     return x, cbs, [4, 2, 1]
 
 
-def _tok_worker(rank, world, port, batch, out_path):
+def _tok_worker(rank, world, port, batch, out_path, gather):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from ncmorph_b200.sharded import ShardedTokenizer
@@ -142,10 +142,10 @@ def _tok_worker(rank, world, port, batch, out_path):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     try:
         x, cbs, pf = _tok_data(batch)
-        tok = ShardedTokenizer(batch, x.shape[1], pf, forward=_fake_tokenizer)
+        tok = ShardedTokenizer(batch, x.shape[1], pf, forward=_fake_tokenizer, gather=gather)
         codes, recon, y = tok(x[tok.b0:tok.b1], None, cbs, None)
         torch.save({"codes": codes, "recon": recon.view(torch.int16), "y": y.view(torch.int16),
-                    "items": tok.items}, out_path + f".{rank}")
+                    "items": tok.items, "b0": tok.b0, "b1": tok.b1}, out_path + f".{rank}")
     except Exception as e:  # noqa: BLE001
         with open(out_path + f".err{rank}", "w") as f:
             f.write(repr(e))
@@ -156,15 +156,17 @@ def _tok_worker(rank, world, port, batch, out_path):
             pass
 
 
-@pytest.mark.parametrize("world,batch", [(2, 4), (2, 3), (3, 2)])
-def test_sharded_tokenizer_matches_single_process(world, batch):
+@pytest.mark.parametrize("world,batch,gather", [(2, 4, "all"), (2, 3, "all"), (3, 2, "all"), (2, 3, "codes"),
+                                                (3, 2, "codes")])
+def test_sharded_tokenizer_matches_single_process(world, batch, gather):
     """Whole batch items per rank (uneven, and a rank with none): every rank
-    gets the codes of every scale, the reconstructions and the outputs in the
-    batch order of one forward over the whole batch."""
+    gets the codes of every scale in the batch order of one forward over the
+    whole batch, and with gather="all" the reconstructions and outputs too
+    (else its own items' ones)."""
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "tok")
-        mp.start_processes(_tok_worker, args=(world, port, batch, out), nprocs=world, join=True,
+        mp.start_processes(_tok_worker, args=(world, port, batch, out, gather), nprocs=world, join=True,
                            start_method="spawn")
         errs = {r: open(out + f".err{r}").read() for r in range(world) if os.path.exists(out + f".err{r}")}
         assert not errs, errs
@@ -176,5 +178,6 @@ def test_sharded_tokenizer_matches_single_process(world, batch):
         assert len(r["codes"]) == len(pf)
         for s in range(len(pf)):
             assert torch.equal(r["codes"][s], codes[s]), (s, r["codes"][s], codes[s])
-        assert torch.equal(r["recon"], recon.view(torch.int16))
-        assert torch.equal(r["y"], y.view(torch.int16))
+        sl = slice(None) if gather == "all" else slice(r["b0"], r["b1"])
+        assert torch.equal(r["recon"], recon[sl].view(torch.int16))
+        assert torch.equal(r["y"], y[sl].view(torch.int16))
