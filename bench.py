@@ -1105,7 +1105,7 @@ def run_tokenizer_sharded(a):
     import torch
     import torch.distributed as dist
 
-    from ncmorph_b200 import sharded
+    from ncmorph_b200 import sharded, vq
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -1122,8 +1122,23 @@ def run_tokenizer_sharded(a):
         B, T = c["B"], c["T"]
         gx = torch.Generator(device=dev).manual_seed(a.seed + 1000 + rank)
         x = torch.randn((B, T, c["Din"]), generator=gx, device=dev).to(torch.bfloat16)
-        tok = sharded.ShardedTokenizer(B * world, T, c["factors"])
         kw = dict(sqnorms=c["sq"], upsample=a.upsample, phi_weight=c["pw"], phi_bias=c["pb"], phi_ratio=0.5)
+        # each rank's forward is one CUDA-graph replay on its fixed buffers, as
+        # on the default line: an eager forward is about 85 launches, and a
+        # rank whose host issued them slower than its GPU ran them set the
+        # pace (measured: 1.5 and 3.5 ms of host time per step on two ranks
+        # of one box); the code gathers stay eager
+        out = {}
+
+        def forward(xb, w_in, cbs, w_out, pf, **k):
+            if "run" not in out:
+                def once():
+                    out["res"] = vq.tokenizer_forward(xb, w_in, cbs, w_out, pf, **k)
+                out["run"] = _graphed(once, True)
+            out["run"]()
+            return out["res"]
+
+        tok = sharded.ShardedTokenizer(B * world, T, c["factors"], forward=forward)
 
         def step():
             return tok(x, c["w_in"], c["cbs"], c["w_out"], **kw)
@@ -1136,16 +1151,20 @@ def run_tokenizer_sharded(a):
         if sampler:
             sampler.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
         e0.record()
         for _ in range(a.steps):
             step()
         e1.record()
+        host_ms = (time.perf_counter() - t0) * 1e3 / a.steps  # host time to issue a step
         torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[local])
         clocks = sampler.stop() if sampler else None
-        ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        ms = float(ms.item())
+        mine = torch.tensor([e0.elapsed_time(e1) / a.steps, host_ms], device=dev)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        per_rank = [[round(float(v), 3) for v in t.tolist()] for t in every]
+        ms = max(r[0] for r in per_rank)
         if rank == 0:
             emit({"metric": "tokenizer_vectors_per_s", "value": B * world * T / (ms * 1e-3), "unit": "vectors/s",
                   "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
@@ -1154,9 +1173,11 @@ def run_tokenizer_sharded(a):
                   "config": {"workload": "multiscale tokenizer forward (BASELINE config 2), batch-sharded",
                              "batch_per_gpu": B, "global_batch": B * world, "seq_len": T,
                              "pool_factors": c["factors"], "parallelism": f"batch items x{world}",
+                             "cuda_graph": True,
                              "collective": "NCCL all_gather of the codes of every scale (reconstructions and "
                                            "outputs stay with the rank that owns the batch items)"},
-                  "e2e": None, "clocks": clocks})
+                  "e2e": None, "clocks": clocks,
+                  "per_rank_ms_device_host": per_rank})
     finally:
         dist.destroy_process_group()
     return 0
