@@ -1145,11 +1145,10 @@ def run_tokenizer_sharded(a):
 
         for _ in range(a.warmup):
             step()
-        sampler = ClockSampler(local) if rank == 0 else None
+        sampler = ClockSampler(local)
         dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
-        if sampler:
-            sampler.start()
+        sampler.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
@@ -1159,8 +1158,8 @@ def run_tokenizer_sharded(a):
         host_ms = (time.perf_counter() - t0) * 1e3 / a.steps  # host time to issue a step
         torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[local])
-        clocks = sampler.stop() if sampler else None
-        mine = torch.tensor([e0.elapsed_time(e1) / a.steps, host_ms], device=dev)
+        clocks = sampler.stop()
+        mine = torch.tensor([e0.elapsed_time(e1) / a.steps, host_ms, float(clocks.get("sm_mhz") or 0)], device=dev)
         every = [torch.empty_like(mine) for _ in range(world)]
         dist.all_gather(every, mine)
         per_rank = [[round(float(v), 3) for v in t.tolist()] for t in every]
@@ -1177,7 +1176,7 @@ def run_tokenizer_sharded(a):
                              "collective": "NCCL all_gather of the codes of every scale (reconstructions and "
                                            "outputs stay with the rank that owns the batch items)"},
                   "e2e": None, "clocks": clocks,
-                  "per_rank_ms_device_host": per_rank})
+                  "per_rank_ms_device_host_mhz": per_rank})
     finally:
         dist.destroy_process_group()
     return 0
