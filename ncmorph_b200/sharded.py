@@ -298,16 +298,25 @@ class ShardedTokenizer:
             raise ValueError("one pool factor per scale is required")
         Din, dev = x_local.shape[2], x_local.device
         rows = [self.T // f for f in self.pool_factors]  # pooled rows per batch item, per scale
-        codes_pad = [torch.zeros((L, self.nb * n), dtype=torch.int32, device=dev) for n in rows]
+        per_item = sum(rows)
+        # every scale's codes of an item side by side, items in order: one
+        # all-gather then puts the batch order in the row order
+        codes_pad = torch.zeros((self.nb, per_item, L), dtype=torch.int32, device=dev)
         if self.items > 0:
             codes, recon, y = self.forward(x_local, w_in, codebooks, w_out, self.pool_factors, **kw)
+            off = 0
             for s, n in enumerate(rows):
-                codes_pad[s][:, : self.items * n] = codes[s]
+                codes_pad[: self.items, off:off + n] = codes[s].t().reshape(self.items, n, L)
+                off += n
         else:
             recon = torch.empty((0, self.T, D), dtype=torch.bfloat16, device=dev)
             y = torch.empty((0, self.T, Din), dtype=torch.bfloat16, device=dev)
-        # codes: gather each scale as [nb * n, L] rows so the batch order is the row order
-        codes_all = [self._gather(c.t(), n).t().contiguous() for c, n in zip(codes_pad, rows)]
+        gathered = self._gather(codes_pad.view(self.nb * per_item, L), per_item).view(self.batch, per_item, L)
+        codes_all = []
+        off = 0
+        for n in rows:
+            codes_all.append(gathered[:, off:off + n].reshape(self.batch * n, L).t().contiguous())
+            off += n
         if self.gather == "codes":
             return codes_all, recon, y
         recon_pad = torch.zeros((self.nb, self.T, D), dtype=torch.bfloat16, device=dev)
